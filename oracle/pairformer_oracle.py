@@ -1,0 +1,331 @@
+"""CPU restatement of the reference's native Pairformer pair-path math.
+
+TEST INFRASTRUCTURE ONLY. This module is the parity checker for the CUDA
+backend in ``fireprot_b200``. It is imported by ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py``; the
+product path never imports or calls it.
+
+Parity pinning: the golden fixtures in ``tests/golden`` are produced by running
+the reference's own Python functions (``adapters/atlasfold/runtime.py``
+``triangle_attention`` / ``triangle_multiplication``,
+``backends/amd/triangle_multiplication.py`` ``_short_sequence_hip_fused``,
+``backends/amd/recycle.py`` ``_hip_transition`` and
+``backends/amd/triangle_attention.py`` ``_efficient_sdpa``) with torch
+stand-ins for their HIP elementwise helpers; ``tests/test_oracle_golden.py``
+checks this restatement against them.
+
+All arithmetic is torch on the CPU in the dtype of the inputs (float32 for
+parity, float64 for a second opinion). Layouts follow the reference: the pair
+tensor ``z`` is ``[N, N, c_z]`` channels-last, masks are ``[N, N]`` with 1 =
+valid.
+
+Reference citations (paths inside the reference project):
+- LayerNorm eps 1e-5: ``python/fireprot/backends/amd/recycle.py:101``.
+- Triangle multiplication order (mask/gate/LN_out/linear_z/residual):
+  ``python/fireprot/backends/amd/triangle_multiplication.py:162-193`` and the
+  contraction directions of ``python/fireprot/backends/amd/lt_bmm.py:85``.
+- Triangle attention (LN -> q/k/v -> bias -> mask -> softmax -> gate -> out):
+  ``python/fireprot/adapters/atlasfold/runtime.py:32-71``; Q pre-scaled by
+  1/sqrt(d) (``kernels/amd/fireprot_amd_ops.cu:915``); mask bias
+  ``1e9 * (mask - 1)`` (``patches/protenix/0005-...patch:35-38``).
+- Ending node = starting-node math on the transposed pair tensor, output
+  transposed back (``patches/protenix/0006-...patch:22,34``).
+- Pair transition ``W_out(silu(LN(z) W_a^T) * (LN(z) W_b^T))``:
+  ``python/fireprot/backends/amd/recycle.py:203-227``.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+from typing import Optional
+
+import torch
+
+LN_EPS = 1e-5
+MASK_INF = 1e9
+
+
+# --------------------------------------------------------------------------
+# parameters (names mirror the Protenix modules the reference hooks)
+# --------------------------------------------------------------------------
+@dataclasses.dataclass
+class TriMulParams:
+    """Weights of one ``TriangleMultiplicativeUpdate`` (all linears bias-free).
+
+    Mirrors ``linear_a_p/linear_a_g/linear_b_p/linear_b_g/linear_g/linear_z``
+    and ``layer_norm_in/layer_norm_out`` checked at
+    ``python/fireprot/backends/amd/triangle_multiplication.py:284-293``.
+    """
+    ln_in_w: torch.Tensor
+    ln_in_b: torch.Tensor
+    w_a_p: torch.Tensor  # [c_hidden, c_z]
+    w_a_g: torch.Tensor
+    w_b_p: torch.Tensor
+    w_b_g: torch.Tensor
+    w_g: torch.Tensor    # [c_z, c_z]
+    ln_out_w: torch.Tensor
+    ln_out_b: torch.Tensor
+    w_z: torch.Tensor    # [c_z, c_hidden]
+
+
+@dataclasses.dataclass
+class TriAttnParams:
+    """Weights of one ``TriangleAttention`` (``layer_norm``, ``linear`` for the
+    pair bias and the ``mha`` q/k/v/g/o linears).
+
+    ``b_g`` / ``b_o`` are the optional gating / output biases of the
+    upstream ``Attention`` module (``attention_gate.py:28-56`` accepts both).
+    """
+    ln_w: torch.Tensor
+    ln_b: torch.Tensor
+    w_q: torch.Tensor    # [H*d, c_z]
+    w_k: torch.Tensor
+    w_v: torch.Tensor
+    w_bias: torch.Tensor  # [H, c_z]
+    w_g: torch.Tensor    # [H*d, c_z]
+    w_o: torch.Tensor    # [c_z, H*d]
+    heads: int
+    head_dim: int
+    b_g: Optional[torch.Tensor] = None
+    b_o: Optional[torch.Tensor] = None
+
+
+@dataclasses.dataclass
+class TransitionParams:
+    """Weights of the pair ``Transition`` (``layernorm1``, ``linear_no_bias_a``,
+    ``linear_no_bias_b``, ``linear_no_bias``; ``transition_projection.py:27-38``)."""
+    ln_w: torch.Tensor
+    ln_b: torch.Tensor
+    w_a: torch.Tensor    # [n*c, c]
+    w_b: torch.Tensor    # [n*c, c]
+    w_out: torch.Tensor  # [c, n*c]
+
+
+@dataclasses.dataclass
+class PairBlockParams:
+    tri_mul_out: TriMulParams
+    tri_mul_in: TriMulParams
+    tri_att_start: TriAttnParams
+    tri_att_end: TriAttnParams
+    transition: TransitionParams
+
+
+def _normal(gen, shape, std, dtype):
+    return (torch.randn(*shape, generator=gen, dtype=torch.float32) * std).to(dtype)
+
+
+def make_trimul_params(c_z=128, c_hidden=128, seed=1, dtype=torch.float32,
+                       ln_affine_random=False) -> TriMulParams:
+    """Seeded random-init weights ~ N(0, 1/fan_in)."""
+    g = torch.Generator().manual_seed(seed)
+    s_in, s_h = 1.0 / math.sqrt(c_z), 1.0 / math.sqrt(c_hidden)
+    if ln_affine_random:
+        ln = [1.0 + 0.1 * torch.randn(c_z, generator=g), 0.1 * torch.randn(c_z, generator=g),
+              1.0 + 0.1 * torch.randn(c_hidden, generator=g), 0.1 * torch.randn(c_hidden, generator=g)]
+    else:
+        ln = [torch.ones(c_z), torch.zeros(c_z), torch.ones(c_hidden), torch.zeros(c_hidden)]
+    return TriMulParams(
+        ln_in_w=ln[0].to(dtype), ln_in_b=ln[1].to(dtype),
+        w_a_p=_normal(g, (c_hidden, c_z), s_in, dtype),
+        w_a_g=_normal(g, (c_hidden, c_z), s_in, dtype),
+        w_b_p=_normal(g, (c_hidden, c_z), s_in, dtype),
+        w_b_g=_normal(g, (c_hidden, c_z), s_in, dtype),
+        w_g=_normal(g, (c_z, c_z), s_in, dtype),
+        ln_out_w=ln[2].to(dtype), ln_out_b=ln[3].to(dtype),
+        w_z=_normal(g, (c_z, c_hidden), s_h, dtype),
+    )
+
+
+def make_triattn_params(c_z=128, heads=4, head_dim=32, seed=1, dtype=torch.float32,
+                        with_biases=False, ln_affine_random=False) -> TriAttnParams:
+    """Seeded random-init weights. BASELINE config 1 uses N(0, 1/128) for
+    W_q/k/v/g, LN gamma=1 / beta=0 and no gate/output bias."""
+    g = torch.Generator().manual_seed(seed)
+    hd = heads * head_dim
+    s_in, s_h = 1.0 / math.sqrt(c_z), 1.0 / math.sqrt(hd)
+    if ln_affine_random:
+        ln_w = 1.0 + 0.1 * torch.randn(c_z, generator=g)
+        ln_b = 0.1 * torch.randn(c_z, generator=g)
+    else:
+        ln_w, ln_b = torch.ones(c_z), torch.zeros(c_z)
+    p = TriAttnParams(
+        ln_w=ln_w.to(dtype), ln_b=ln_b.to(dtype),
+        w_q=_normal(g, (hd, c_z), s_in, dtype),
+        w_k=_normal(g, (hd, c_z), s_in, dtype),
+        w_v=_normal(g, (hd, c_z), s_in, dtype),
+        w_bias=_normal(g, (heads, c_z), s_in, dtype),
+        w_g=_normal(g, (hd, c_z), s_in, dtype),
+        w_o=_normal(g, (c_z, hd), s_h, dtype),
+        heads=heads, head_dim=head_dim,
+    )
+    if with_biases:
+        p.b_g = _normal(g, (hd,), 1.0, dtype)
+        p.b_o = _normal(g, (c_z,), 0.1, dtype)
+    return p
+
+
+def make_transition_params(c=128, n=4, seed=1, dtype=torch.float32,
+                           ln_affine_random=False) -> TransitionParams:
+    g = torch.Generator().manual_seed(seed)
+    if ln_affine_random:
+        ln_w = 1.0 + 0.1 * torch.randn(c, generator=g)
+        ln_b = 0.1 * torch.randn(c, generator=g)
+    else:
+        ln_w, ln_b = torch.ones(c), torch.zeros(c)
+    return TransitionParams(
+        ln_w=ln_w.to(dtype), ln_b=ln_b.to(dtype),
+        w_a=_normal(g, (n * c, c), 1.0 / math.sqrt(c), dtype),
+        w_b=_normal(g, (n * c, c), 1.0 / math.sqrt(c), dtype),
+        w_out=_normal(g, (c, n * c), 1.0 / math.sqrt(n * c), dtype),
+    )
+
+
+def make_block_params(c_z=128, seed=1, dtype=torch.float32) -> PairBlockParams:
+    return PairBlockParams(
+        tri_mul_out=make_trimul_params(c_z, c_z, seed=seed, dtype=dtype),
+        tri_mul_in=make_trimul_params(c_z, c_z, seed=seed + 1, dtype=dtype),
+        tri_att_start=make_triattn_params(c_z, seed=seed + 2, dtype=dtype),
+        tri_att_end=make_triattn_params(c_z, seed=seed + 3, dtype=dtype),
+        transition=make_transition_params(c_z, seed=seed + 4, dtype=dtype),
+    )
+
+
+def make_pair(n, c=128, seed=0, dtype=torch.float32) -> torch.Tensor:
+    """Seeded z ~ N(0, 1) of shape [n, n, c] (``torch.Generator().manual_seed``)."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(n, n, c, generator=g, dtype=torch.float32).to(dtype)
+
+
+def make_padding_mask(n, valid, dtype=torch.float32) -> torch.Tensor:
+    """Pair mask of a padded sequence: rows and columns >= valid are 0."""
+    v = torch.arange(n) < valid
+    return (v[:, None] & v[None, :]).to(dtype)
+
+
+# --------------------------------------------------------------------------
+# primitives
+# --------------------------------------------------------------------------
+def layer_norm(x, w, b, eps=LN_EPS):
+    """LayerNorm over the last dim (biased variance), as torch's native op."""
+    return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
+
+
+def attention_core(q, k, v, biases):
+    """The upstream ``_attention``: ``softmax(q @ k^T + sum(biases)) @ v``.
+
+    q, k, v: ``[*, H, Q, D]``; biases broadcast to ``[*, H, Q, K]`` and are
+    added in list order (mask bias first). Q is pre-scaled by the caller.
+    Returns ``[*, H, Q, D]`` (the reference's dispatch transposes it to
+    ``[*, Q, H, D]``; ``triangle_attention.py:129``).
+    """
+    a = torch.matmul(q, k.transpose(-1, -2))
+    for b in biases:
+        a = a + b
+    a = torch.softmax(a, dim=-1)
+    return torch.matmul(a, v)
+
+
+# --------------------------------------------------------------------------
+# pair operators
+# --------------------------------------------------------------------------
+def triangle_multiplication(z, mask, p: TriMulParams, *, outgoing: bool, add: bool = True):
+    """Protenix ``TriangleMultiplicativeUpdate`` inference semantics.
+
+    ``a = mask * sigmoid(LN(z) W_a_g^T) * (LN(z) W_a_p^T)`` (b likewise),
+    outgoing ``x_ij = sum_k a_ik b_jk``, incoming ``x_ij = sum_k a_ki b_kj``,
+    ``delta = sigmoid(LN(z) W_g^T) * (LN_out(x) W_z^T)``; the gate uses the
+    unmasked LN(z) (``triangle_multiplication.py:162-193``). Returns ``z +
+    delta`` when ``add`` else ``delta`` (``fireprot_amd_ops.cu:589-601``).
+    """
+    zn = layer_norm(z, p.ln_in_w, p.ln_in_b)
+    a = torch.sigmoid(zn @ p.w_a_g.T) * (zn @ p.w_a_p.T)
+    b = torch.sigmoid(zn @ p.w_b_g.T) * (zn @ p.w_b_p.T)
+    if mask is not None:
+        a = a * mask[..., None]
+        b = b * mask[..., None]
+    a_cf = a.permute(2, 0, 1)  # [c, N, N]
+    b_cf = b.permute(2, 0, 1)
+    if outgoing:
+        x = torch.matmul(a_cf, b_cf.transpose(-1, -2))  # sum_k a[c,i,k] b[c,j,k]
+    else:
+        x = torch.matmul(a_cf.transpose(-1, -2), b_cf)  # sum_k a[c,k,i] b[c,k,j]
+    x = x.permute(1, 2, 0)
+    x = layer_norm(x, p.ln_out_w, p.ln_out_b)
+    x = x @ p.w_z.T
+    g = torch.sigmoid(zn @ p.w_g.T)
+    delta = g * x
+    return z + delta if add else delta
+
+
+def triangle_attention(z, mask, p: TriAttnParams, *, starting: bool = True, chunk: int = 64):
+    """Triangle attention update ``delta`` (without the residual add).
+
+    Starting node: for row i, ``o_ij = sum_k softmax_k(q_ij.k_ik / sqrt(d) +
+    b^h_jk + 1e9 (mask_ik - 1)) v_ik``; ``delta_ij = W_o(g_ij * o_ij) + b_o``
+    with ``g = sigmoid(LN(z) W_g^T + b_g)`` and ``b^h = LN(z) W_bias^T``.
+    Ending node: the same on ``z^T`` (and ``mask^T``), result transposed back.
+    Follows ``adapters/atlasfold/runtime.py:32-71``; rows are processed in
+    chunks of ``chunk`` to bound the ``[chunk, H, N, N]`` score buffer.
+    """
+    x = z if starting else z.transpose(0, 1)
+    m = None if mask is None else (mask if starting else mask.transpose(0, 1))
+    n = x.shape[0]
+    H, d = p.heads, p.head_dim
+    xn = layer_norm(x, p.ln_w, p.ln_b)
+    scale = 1.0 / math.sqrt(d)
+    q = (xn @ p.w_q.T).reshape(n, n, H, d).permute(0, 2, 1, 3) * scale  # [i,h,j,d]
+    k = (xn @ p.w_k.T).reshape(n, n, H, d).permute(0, 2, 1, 3)
+    v = (xn @ p.w_v.T).reshape(n, n, H, d).permute(0, 2, 1, 3)
+    tri_bias = (xn @ p.w_bias.T).permute(2, 0, 1).unsqueeze(0)  # [1,h,j,k]
+    gate = xn @ p.w_g.T
+    if p.b_g is not None:
+        gate = gate + p.b_g
+    gate = torch.sigmoid(gate)
+    outs = []
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        biases = []
+        if m is not None:
+            biases.append((MASK_INF * (m[s:e] - 1.0))[:, None, None, :])
+        biases.append(tri_bias)
+        o = attention_core(q[s:e], k[s:e], v[s:e], biases)  # [c,h,j,d]
+        outs.append(o.permute(0, 2, 1, 3).reshape(e - s, n, H * d))
+    o = torch.cat(outs, 0)
+    out = (gate * o) @ p.w_o.T
+    if p.b_o is not None:
+        out = out + p.b_o
+    return out if starting else out.transpose(0, 1)
+
+
+def pair_transition(z, p: TransitionParams):
+    """Pair transition update ``W_out(silu(LN(z) W_a^T) * (LN(z) W_b^T))``."""
+    xn = layer_norm(z, p.ln_w, p.ln_b)
+    return (torch.nn.functional.silu(xn @ p.w_a.T) * (xn @ p.w_b.T)) @ p.w_out.T
+
+
+def pair_block(z, mask, p: PairBlockParams, *, attn_chunk: int = 64):
+    """Pair stack of one Pairformer block (AF3 Algorithm 17 order):
+    TriMul out, TriMul in, TriAttn start, TriAttn end, transition; each adds
+    its update to z (``patches/protenix/0006-...patch:14-37``)."""
+    z = triangle_multiplication(z, mask, p.tri_mul_out, outgoing=True, add=True)
+    z = triangle_multiplication(z, mask, p.tri_mul_in, outgoing=False, add=True)
+    z = z + triangle_attention(z, mask, p.tri_att_start, starting=True, chunk=attn_chunk)
+    z = z + triangle_attention(z, mask, p.tri_att_end, starting=False, chunk=attn_chunk)
+    z = z + pair_transition(z, p.transition)
+    return z
+
+
+# --------------------------------------------------------------------------
+# tolerance checks (north star: strict 1e-4, fast 1e-2, relative to the
+# fp32 output scale max|ref|)
+# --------------------------------------------------------------------------
+STRICT_TOL = 1e-4
+FAST_TOL = 1e-2
+
+
+def rel_max_err(actual, expected):
+    """max|actual - expected| / max|expected| (the output-scale relative error)."""
+    a = actual.detach().to("cpu", torch.float64)
+    e = expected.detach().to("cpu", torch.float64)
+    scale = e.abs().max().item()
+    return (a - e).abs().max().item() / (scale if scale > 0 else 1.0)

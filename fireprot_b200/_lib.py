@@ -1,0 +1,60 @@
+"""ctypes binding of ``libfireprot_b200.so`` (the only compute path).
+
+Loading never compiles and never falls back: a missing or stale library raises
+``ImportError``-style ``RuntimeError`` at first use, and every non-zero status
+returned by an entry point raises ``RuntimeError`` (the reference's launch
+policy, ``python/fireprot/backends/amd/lt_bmm.py:76-82``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_LOCK = threading.Lock()
+_LIB = None
+LIB_PATH = Path(os.environ.get("FIREPROT_B200_LIBRARY",
+                               Path(__file__).resolve().parent / "libfireprot_b200.so"))
+
+c_int, c_size_t, c_void_p, c_float = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
+
+# name -> (restype, argtypes); must match include/fireprot_b200.h
+SIGNATURES = {
+    "fpb_abi_version": (c_int, []),
+    "fpb_status_string": (ctypes.c_char_p, [c_int]),
+    "fpb_device_supported": (c_int, [c_int]),
+    "fpb_workspace_status": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_int)]),
+    "fpb_packed_bmm_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "fpb_packed_bmm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                               c_void_p, c_size_t, c_void_p]),
+}
+
+ABI_VERSION = 1
+
+
+def load():
+    """Return the loaded library, binding every declared entry point."""
+    global _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not LIB_PATH.is_file():
+            raise RuntimeError(
+                f"fireprot_b200 CUDA library is missing: {LIB_PATH}. "
+                "Build it with `python -m fireprot_b200.build`.")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.fpb_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"unsupported fireprot_b200 ABI {lib.fpb_abi_version()}")
+        _LIB = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = load().fpb_status_string(status).decode()
+        raise RuntimeError(f"{what} failed with status {status} ({msg})")

@@ -1,0 +1,59 @@
+/*
+ * fireprot_b200 — C ABI of the B200 (sm_100a) backend for the Pairformer
+ * pair-representation hot path.
+ *
+ * Conventions (mirroring the reference's C-ABI kernels):
+ *  - every entry point returns an int status: 0 ok, 2 unsupported shape,
+ *    3 misaligned pointer/stride, 4 invalid argument, 5 CUDA launch error,
+ *    6 device-side wait timed out, 7 workspace too small
+ *    (reference: kernels/amd/fireprot_ck_attention.cpp:35,68,106-108,
+ *    kernels/amd/fireprot_lt_bmm.cpp:47-48,62);
+ *  - pointers are raw device pointers, work is enqueued on `stream`, nothing
+ *    is allocated: the caller passes a workspace of at least the size the
+ *    matching *_workspace_size function returns (16-byte aligned); its first
+ *    256 bytes hold a device status word (see fpb_workspace_status);
+ *  - `precision`: 0 = strict FP32 (3xTF32 tensor-core products),
+ *    1 = fast (BF16 operands, FP32 accumulation);
+ *  - pair tensors are [N, N, C] FP32, C-contiguous (channels last), masks
+ *    [N, N] FP32 with 1 = valid (nullable: no mask).
+ */
+#ifndef FIREPROT_B200_H
+#define FIREPROT_B200_H
+
+#include <stddef.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FPB_STRICT 0
+#define FPB_FAST 1
+
+/* ABI version of this library (1). Reference: the Rust bridge's ABI gate,
+ * python/fireprot/ops/_bridge.py:32-33. */
+int fpb_abi_version(void);
+
+/* Human-readable text for a status code. */
+const char* fpb_status_string(int status);
+
+/* 0 when `device` is an sm_100 GPU. */
+int fpb_device_supported(int device);
+
+/* Synchronise `stream`, then read the device status word of `workspace`. */
+int fpb_workspace_status(const void* workspace, cudaStream_t stream, int* out_status);
+
+/* Batched triangle contraction over `batch` channel planes of n x n FP32:
+ * outgoing: out[c] = a[c] @ b[c]^T; incoming: out[c] = a[c]^T @ b[c].
+ * Replaces lt_packed_bmm (kernels/amd/fireprot_lt_bmm.cpp:46-63, Python
+ * caller python/fireprot/backends/amd/lt_bmm.py:65-85) for any n and batch;
+ * a, b, out contiguous [batch, n, n]. */
+size_t fpb_packed_bmm_workspace_size(int batch, int n, int precision);
+int fpb_packed_bmm(const float* a, const float* b, float* out, int batch, int n, int outgoing,
+                   int precision, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FIREPROT_B200_H */

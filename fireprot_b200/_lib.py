@@ -28,6 +28,9 @@ SIGNATURES = {
     "fpb_packed_bmm_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "fpb_packed_bmm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "fpb_trimul": (c_int, [c_void_p, c_void_p, c_int, c_int] + [c_void_p] * 10
+                   + [c_float, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
 }
 
 ABI_VERSION = 1

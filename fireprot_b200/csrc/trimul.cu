@@ -1,0 +1,581 @@
+// Triangle multiplicative update (outgoing / incoming), fused on sm_100a.
+//
+// Reference operator: Protenix TriangleMultiplicativeUpdate as dispatched by
+// python/fireprot/backends/amd/triangle_multiplication.py:389-430 (math at
+// :162-193, contraction directions at lt_bmm.py:85):
+//   zn = LN_in(z); a = mask * sigmoid(zn Wag^T) * (zn Wap^T); b likewise
+//   outgoing x_ij = sum_k a_ik b_jk ; incoming x_ij = sum_k a_ki b_kj
+//   z <- [z +] sigmoid(zn Wg^T) * (LN_out(x) Wz^T)
+//
+// Three launches per call:
+//  1. proj:     LN_in + [Wap;Wag;Wbp;Wbg] GEMM (128 x 512 per tile, TMEM
+//               512 columns) + gate/mask epilogue writing a, b channel-first
+//               [c][i][k] (3xTF32 hi/lo split in strict mode). The incoming
+//               direction reads z transposed (pair (i,k) <- z[k][i]) so that
+//               the contraction is always "A B^T".
+//  2. contract: batched tcgen05 N^3 contraction (contract.cu) -> x [c][i][j].
+//  3. out:      LN_in(z) Wg^T and LN_out(x) Wz^T (two 128x128 GEMMs sharing
+//               one A buffer) + sigmoid gate + residual, written in place.
+#include "kernels.h"
+#include "rowgemm.cuh"
+
+namespace fpb {
+
+struct TriMulProjArgs {
+  const float* z;
+  const float* mask;  // nullable
+  int n;
+  float eps;
+  const float* ln_w;
+  const float* ln_b;
+  void* a_hi;
+  void* a_lo;
+  void* b_hi;
+  void* b_lo;
+  int ld;
+  size_t cs;
+  int* status;
+};
+
+template <bool kStrict>
+constexpr int proj_smem_bytes() {
+  using C = RowCfg<kStrict>;
+  // fast mode requests extra shared memory so that only one CTA (and one
+  // 512-column TMEM allocation) is resident per SM.
+  const int need = C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256;
+  return need < 120 * 1024 ? 120 * 1024 : need;
+}
+
+template <bool kStrict, bool kTrans>
+__global__ void __launch_bounds__(192, 1)
+    trimul_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
+                       const __grid_constant__ CUtensorMap w_lo, TriMulProjArgs p) {
+  using C = RowCfg<kStrict>;
+  constexpr int WSTAGES = 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* A = smem;
+  uint8_t* W = smem + C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(W + WSTAGES * C::WSTAGE_BYTES);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = bars + WSTAGES;
+  uint64_t* a_full = bars + 2 * WSTAGES;
+  uint64_t* done = a_full + 1;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.n;
+  const long long npairs = (long long)n * n;
+  const long long p0 = (long long)blockIdx.x * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(a_full, 128);
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+  const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
+  constexpr int NLOADS = 4 * C::NKA;  // 4 chunks of 128 outputs x K atoms
+
+  if (warp < 4) {
+    // ---- producer: LayerNorm of 32 rows per warp into the A tile
+    const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
+    const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
+    const float4* z4 = reinterpret_cast<const float4*>(p.z);
+#pragma unroll 1
+    for (int rr = 0; rr < 32; rr += 4) {
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = warp * 32 + rr + u;
+        const long long pr = p0 + row;
+        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (pr < npairs) {
+          const long long r = pr / n, s = pr - r * n;
+          const long long src = kTrans ? (s * n + r) : pr;
+          x[u] = __ldg(z4 + src * 32 + lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = warp * 32 + rr + u;
+        const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
+        a_store4<kStrict>(A, row, lane * 4, y.x, y.y, y.z, y.w);
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(a_full);
+
+    // ---- epilogue: thread t owns tile row t (TMEM lane t)
+    const int t = warp * 32 + lane;
+    const long long pr = p0 + t;
+    const bool valid = pr < npairs;
+    long long r = 0, s = 0;
+    float m = 1.f;
+    if (valid) {
+      r = pr / n;
+      s = pr - r * n;
+      if (p.mask) m = __ldg(p.mask + (kTrans ? (s * n + r) : pr));
+    }
+    const size_t pos = (size_t)r * p.ld + (size_t)s;
+    if (mbar_wait(done, 0, g, 3)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {
+        void* dst_hi = part ? p.b_hi : p.a_hi;
+        void* dst_lo = part ? p.b_lo : p.a_lo;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float pv[32], gv[32];
+          tmem_row32(tmem, warp, part * 256 + cc * 32, pv);
+          tmem_row32(tmem, warp, part * 256 + 128 + cc * 32, gv);
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float v = sigmoidf_(gv[e]) * pv[e] * m;
+              const size_t idx = (size_t)(cc * 32 + e) * p.cs + pos;
+              if constexpr (kStrict) {
+                float h, l;
+                split_tf32(v, h, l);
+                static_cast<float*>(dst_hi)[idx] = h;
+                static_cast<float*>(dst_lo)[idx] = l;
+              } else {
+                static_cast<__nv_bfloat16*>(dst_hi)[idx] = __float2bfloat16_rn(v);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int q = 0; q < NLOADS; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
+        ++issued;
+      }
+      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+    }
+  } else {
+    if (lane == 0) {
+      const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
+      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
+      bool ok = mbar_wait(a_full, 0, g, 4);
+      if (ok) tc_fence_after();
+      for (int q = 0; q < NLOADS && ok; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        const uint32_t w = wring_wait(ring, q, g);
+        if (!w) {
+          ok = false;
+          break;
+        }
+        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
+                            w, w + C::ATOM_BYTES, idesc, ka == 0);
+        wring_release(ring, q);
+      }
+      if (ok) {
+        umma_commit(done);
+      } else {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------
+struct TriMulOutArgs {
+  float* z;
+  int n;
+  float eps_in, eps_out;
+  const float* ln_in_w;
+  const float* ln_in_b;
+  const float* ln_out_w;
+  const float* ln_out_b;
+  const void* x;  // [128][n][ldx] fp32 (strict) or bf16 (fast)
+  int ldx;
+  size_t xcs;
+  int add;
+  int* status;
+};
+
+template <bool kStrict>
+constexpr int out_smem_bytes() {
+  using C = RowCfg<kStrict>;
+  return C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024 /*ln_out params*/;
+}
+
+template <bool kStrict>
+__global__ void __launch_bounds__(192, 1)
+    trimul_out_kernel(const __grid_constant__ CUtensorMap w_hi,
+                      const __grid_constant__ CUtensorMap w_lo, TriMulOutArgs p) {
+  using C = RowCfg<kStrict>;
+  constexpr int WSTAGES = 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* A = smem;
+  uint8_t* W = smem + C::A_BYTES;
+  float* lnp = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // 256 floats
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lnp + 256);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = bars + WSTAGES;
+  uint64_t* a_full = bars + 2 * WSTAGES;
+  uint64_t* a_free = a_full + 1;
+  uint64_t* done = a_free + 1;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.n;
+  const long long npairs = (long long)n * n;
+  const long long p0 = (long long)blockIdx.x * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(a_full, 128);
+    mbar_init(a_free, 1);
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 128) {
+    lnp[threadIdx.x] = p.ln_out_w[threadIdx.x];
+    lnp[128 + threadIdx.x] = p.ln_out_b[threadIdx.x];
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+  const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
+  constexpr int NLOADS = 2 * C::NKA;
+
+  if (warp < 4) {
+    // ---- A1 = LN_in(z) (lane-cooperative rows)
+    {
+      const float4 lw = reinterpret_cast<const float4*>(p.ln_in_w)[lane];
+      const float4 lb = reinterpret_cast<const float4*>(p.ln_in_b)[lane];
+      const float4* z4 = reinterpret_cast<const float4*>(p.z);
+#pragma unroll 1
+      for (int rr = 0; rr < 32; rr += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long pr = p0 + warp * 32 + rr + u;
+          x[u] = pr < npairs ? z4[pr * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 y = ln_row_warp(x[u], lw, lb, p.eps_in);
+          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+    }
+    // ---- A2 = LN_out(x) (thread-per-row: x is channel-first)
+    const int t = warp * 32 + lane;
+    const long long pr = p0 + t;
+    const bool valid = pr < npairs;
+    const long long r = valid ? pr / n : 0, s = valid ? pr - (pr / n) * n : 0;
+    {
+      float v[128];
+      const size_t pos = (size_t)r * p.ldx + (size_t)s;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float val = 0.f;
+        if (valid) {
+          if constexpr (kStrict)
+            val = static_cast<const float*>(p.x)[(size_t)c * p.xcs + pos];
+          else
+            val = __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[(size_t)c * p.xcs + pos]);
+        }
+        v[c] = val;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) sum += v[c];
+      const float mean = sum * (1.0f / 128.0f);
+      float sq = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float d = v[c] - mean;
+        sq += d * d;
+      }
+      const float rs = rsqrtf(sq * (1.0f / 128.0f) + p.eps_out);
+      // the MMAs of GEMM 1 must have finished reading A before it is reused
+      const bool ok = mbar_wait(a_free, 0, g, 5);
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          a_store4<kStrict>(A, t, c, (v[c] - mean) * rs * lnp[c] + lnp[128 + c],
+                            (v[c + 1] - mean) * rs * lnp[c + 1] + lnp[129 + c],
+                            (v[c + 2] - mean) * rs * lnp[c + 2] + lnp[130 + c],
+                            (v[c + 3] - mean) * rs * lnp[c + 3] + lnp[131 + c]);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+    }
+    // ---- epilogue: delta = sigmoid(G) * Y, z <- [z +] delta
+    if (mbar_wait(done, 0, g, 3)) {
+      tc_fence_after();
+      float4* zrow = reinterpret_cast<float4*>(p.z) + (valid ? pr : 0) * 32;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float gv[32], yv[32];
+        tmem_row32(tmem, warp, cc * 32, gv);
+        tmem_row32(tmem, warp, 128 + cc * 32, yv);
+        if (valid) {
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.add) o = zrow[cc * 8 + v4];
+            o.x += sigmoidf_(gv[4 * v4]) * yv[4 * v4];
+            o.y += sigmoidf_(gv[4 * v4 + 1]) * yv[4 * v4 + 1];
+            o.z += sigmoidf_(gv[4 * v4 + 2]) * yv[4 * v4 + 2];
+            o.w += sigmoidf_(gv[4 * v4 + 3]) * yv[4 * v4 + 3];
+            zrow[cc * 8 + v4] = o;
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int q = 0; q < NLOADS; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
+        ++issued;
+      }
+      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+    }
+  } else {
+    if (lane == 0) {
+      const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
+      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
+      bool ok = true;
+      for (int q = 0; q < NLOADS && ok; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (ka == 0) {
+          if (nc == 1) umma_commit(a_free);  // GEMM 1 done reading A once it retires
+          if (!mbar_wait(a_full, nc & 1, g, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t w = wring_wait(ring, q, g);
+        if (!w) {
+          ok = false;
+          break;
+        }
+        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
+                            w, w + C::ATOM_BYTES, idesc, ka == 0);
+        wring_release(ring, q);
+      }
+      if (ok) {
+        umma_commit(done);
+      } else {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// weight packing: concatenate up to 4 [rows][128] FP32 matrices and split
+// them into tf32 hi/lo (strict) or convert to BF16 (fast).
+// ----------------------------------------------------------------------------
+struct PackSrc {
+  const float* m[4];
+  int count;
+  int rows_each;
+};
+
+__global__ void pack_weights_kernel(PackSrc src, void* hi, void* lo, int strict) {
+  const int total = src.count * src.rows_each * 128;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int mat = i / (src.rows_each * 128);
+    const int off = i - mat * src.rows_each * 128;
+    const float v = src.m[mat][off];
+    if (strict) {
+      float h, l;
+      split_tf32(v, h, l);
+      static_cast<float*>(hi)[i] = h;
+      static_cast<float*>(lo)[i] = l;
+    } else {
+      static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+int pack_weights(const PackSrc& src, void* hi, void* lo, bool strict, cudaStream_t stream) {
+  pack_weights_kernel<<<64, 256, 0, stream>>>(src, hi, lo, strict ? 1 : 0);
+  return launch_status();
+}
+
+bool make_weight_maps(const void* hi, const void* lo, int rows, bool strict, CUtensorMap* mh,
+                      CUtensorMap* ml) {
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t pitch = 128ull * esz;
+  bool ok = make_map_3d(mh, hi, dt, 128, rows, 1, pitch, pitch * rows, 128 / esz, 128, 1);
+  if (strict)
+    ok = ok && make_map_3d(ml, lo, dt, 128, rows, 1, pitch, pitch * rows, 128 / esz, 128, 1);
+  else
+    *ml = *mh;
+  return ok;
+}
+
+// workspace plan (shared by the size query and the call)
+template <class Alloc>
+struct TriMulPlan {
+  void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
+  void *a_hi = nullptr, *a_lo = nullptr, *b_hi = nullptr, *b_lo = nullptr, *x = nullptr;
+  int ld = 0, ldx = 0;
+  size_t cs = 0, xcs = 0;
+  void plan(Alloc& al, int n, bool strict) {
+    auto takef = [&](size_t c) -> void* { return al.template take<float>(c); };
+    auto takeh = [&](size_t c) -> void* { return al.template take<__nv_bfloat16>(c); };
+    auto take = [&](size_t c) -> void* { return strict ? takef(c) : takeh(c); };
+    wp_hi = take(512 * 128);
+    if (strict) wp_lo = take(512 * 128);
+    wo_hi = take(256 * 128);
+    if (strict) wo_lo = take(256 * 128);
+    ld = padded_ld(n, strict ? 4 : 2);
+    cs = (size_t)n * ld;
+    a_hi = take(128 * cs);
+    b_hi = take(128 * cs);
+    if (strict) {
+      a_lo = take(128 * cs);
+      b_lo = take(128 * cs);
+    }
+    ldx = padded_ld(n, strict ? 4 : 2);
+    xcs = (size_t)n * ldx;
+    x = take(128 * xcs);
+  }
+};
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" size_t fpb_trimul_workspace_size(int n, int c_z, int precision) {
+  if (n <= 0 || c_z != 128 || (precision != 0 && precision != 1)) return 0;
+  WsCounter cnt;
+  TriMulPlan<WsCounter> pl;
+  pl.plan(cnt, n, precision == 0);
+  return cnt.used;
+}
+
+extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const float* ln_in_w,
+                          const float* ln_in_b, const float* w_a_p, const float* w_a_g,
+                          const float* w_b_p, const float* w_b_g, const float* w_g,
+                          const float* ln_out_w, const float* ln_out_b, const float* w_z,
+                          float eps, int outgoing, int add, int precision, void* workspace,
+                          size_t workspace_bytes, cudaStream_t stream) {
+  if (!z || !ln_in_w || !ln_in_b || !w_a_p || !w_a_g || !w_b_p || !w_b_g || !w_g || !ln_out_w ||
+      !ln_out_b || !w_z || !workspace)
+    return kErrArg;
+  if (c_z != 128 || n <= 0) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_in_w) || !aligned16(ln_in_b))
+    return kErrAlign;
+  if (workspace_bytes < fpb_trimul_workspace_size(n, c_z, precision)) return kErrWorkspace;
+  const bool strict = precision == 0;
+  WsCursor cur(workspace, workspace_bytes);
+  TriMulPlan<WsCursor> pl;
+  pl.plan(cur, n, strict);
+  if (!cur.ok) return kErrWorkspace;
+  int* status = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+
+  int st = pack_weights(PackSrc{{w_a_p, w_a_g, w_b_p, w_b_g}, 4, 128}, pl.wp_hi, pl.wp_lo, strict,
+                        stream);
+  if (st) return st;
+  st = pack_weights(PackSrc{{w_g, w_z, nullptr, nullptr}, 2, 128}, pl.wo_hi, pl.wo_lo, strict,
+                    stream);
+  if (st) return st;
+  CUtensorMap mph, mpl, moh, mol;
+  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 512, strict, &mph, &mpl) ||
+      !make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol))
+    return kErrArg;
+
+  const long long npairs = (long long)n * n;
+  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  TriMulProjArgs pa{z, mask, n, eps, ln_in_w, ln_in_b, pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo,
+                    pl.ld, pl.cs, status};
+  {
+    const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
+    auto k = strict ? (outgoing ? trimul_proj_kernel<true, false> : trimul_proj_kernel<true, true>)
+                    : (outgoing ? trimul_proj_kernel<false, false>
+                                : trimul_proj_kernel<false, true>);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<tiles, 192, smem, stream>>>(mph, mpl, pa);
+    if ((st = launch_status())) return st;
+  }
+  ContractOperands op{pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo, pl.ld, pl.cs, 128, strict};
+  ContractArgs ca{};
+  ca.n = n;
+  ca.out = pl.x;
+  ca.ldo = pl.ldx;
+  ca.out_channel_stride = pl.xcs;
+  ca.out_bf16 = strict ? 0 : 1;
+  ca.status = status;
+  if ((st = launch_contract(op, ca, stream))) return st;
+  TriMulOutArgs oa{z, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, pl.x, pl.ldx, pl.xcs,
+                   add ? 1 : 0, status};
+  {
+    const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
+    auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<tiles, 192, smem, stream>>>(moh, mol, oa);
+    if ((st = launch_status())) return st;
+  }
+  return kOk;
+}

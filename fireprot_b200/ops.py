@@ -66,3 +66,40 @@ def packed_bmm(a: torch.Tensor, b: torch.Tensor, outgoing: bool, precision="stri
                                   int(bool(outgoing)), p, ws.data_ptr(), ws.numel(),
                                   _stream_ptr(a.device)), "fpb_packed_bmm")
     return (out, ws) if return_workspace else out
+
+
+def _f32(t, name, n=None):
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be float32")
+    return t.contiguous()
+
+
+def trimul(z: torch.Tensor, mask, w: dict, *, outgoing: bool, add: bool = True,
+           precision="strict", eps: float = 1e-5, return_workspace: bool = False):
+    """Triangle multiplicative update in place on ``z`` ``[n, n, 128]``.
+
+    ``w`` holds ``ln_in_w, ln_in_b, w_a_p, w_a_g, w_b_p, w_b_g, w_g, ln_out_w,
+    ln_out_b, w_z`` (torch Linear layouts). Returns ``z`` (same storage).
+    """
+    _require_cuda(z, mask)
+    if z.dtype != torch.float32 or z.ndim != 3 or z.shape[0] != z.shape[1] or z.shape[2] != 128:
+        raise RuntimeError("trimul takes a float32 [n, n, 128] pair tensor")
+    if not z.is_contiguous() or z.data_ptr() % 16:
+        raise RuntimeError("trimul needs a contiguous, 16-byte aligned z")
+    n = z.shape[0]
+    if mask is not None:
+        if tuple(mask.shape) != (n, n):
+            raise RuntimeError("mask must be [n, n]")
+        mask = mask.to(torch.float32).contiguous()
+    names = ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p", "w_b_g", "w_g", "ln_out_w",
+             "ln_out_b", "w_z")
+    ws_t = [_f32(w[k], k) for k in names]
+    _require_cuda(*ws_t)
+    lib = _lib.load()
+    p = precision_code(precision)
+    ws = workspace(lib.fpb_trimul_workspace_size(n, 128, p), z.device)
+    _lib.check(lib.fpb_trimul(z.data_ptr(), 0 if mask is None else mask.data_ptr(), n, 128,
+                              *[t.data_ptr() for t in ws_t], float(eps), int(bool(outgoing)),
+                              int(bool(add)), p, ws.data_ptr(), ws.numel(),
+                              _stream_ptr(z.device)), "fpb_trimul")
+    return (z, ws) if return_workspace else z

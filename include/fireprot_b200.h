@@ -52,6 +52,24 @@ size_t fpb_packed_bmm_workspace_size(int batch, int n, int precision);
 int fpb_packed_bmm(const float* a, const float* b, float* out, int batch, int n, int outgoing,
                    int precision, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Triangle multiplicative update, whole operator, in place on z [n, n, 128]:
+ *   zn = LN_in(z); a = mask*sigmoid(zn Wag^T)*(zn Wap^T); b likewise;
+ *   outgoing x_ij = sum_k a_ik b_jk, incoming x_ij = sum_k a_ki b_kj;
+ *   z <- [z +] sigmoid(zn Wg^T) * (LN_out(x) Wz^T)   (add = 1 / 0).
+ * Weights are torch Linear layouts [out, in] FP32 (bias-free), LN params
+ * [128]. Replaces the packed path of dispatch_triangle_multiplication
+ * (python/fireprot/backends/amd/triangle_multiplication.py:296-344, selected
+ * at :389-430) and its kernels dual_projection_tiled / lt_packed_bmm /
+ * packed_norm_vector / triangle_residual (kernels/amd/fireprot_amd_ops.cu:
+ * 594-646,663-708,787-863; kernels/amd/fireprot_lt_bmm.cpp:46-63).
+ * z and the LN_in parameters must be 16-byte aligned. */
+size_t fpb_trimul_workspace_size(int n, int c_z, int precision);
+int fpb_trimul(float* z, const float* mask, int n, int c_z, const float* ln_in_w,
+               const float* ln_in_b, const float* w_a_p, const float* w_a_g, const float* w_b_p,
+               const float* w_b_g, const float* w_g, const float* ln_out_w, const float* ln_out_b,
+               const float* w_z, float eps, int outgoing, int add, int precision, void* workspace,
+               size_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,9 @@ SIGNATURES = {
     "fpb_trimul_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "fpb_trimul": (c_int, [c_void_p, c_void_p, c_int, c_int] + [c_void_p] * 10
                    + [c_float, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_triattn_workspace_size": (c_size_t, [c_int] * 6),
+    "fpb_triattn": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int] + [c_void_p] * 10
+                    + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
 }
 
 ABI_VERSION = 1

@@ -29,4 +29,26 @@ struct ContractArgs {
 
 int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream);
 
+// Concatenate up to 4 [rows_each][128] FP32 weight matrices and split them
+// into tf32 hi/lo (strict) or convert them to BF16 (fast).
+struct PackSrc {
+  const float* m[4];
+  int count;
+  int rows_each;
+};
+int pack_weights(const PackSrc& src, void* hi, void* lo, bool strict, cudaStream_t stream);
+
+// TMA maps over packed weights [rows][128], one 128-byte K atom x 128 rows per box.
+bool make_weight_maps(const void* hi, const void* lo, int rows, bool strict, CUtensorMap* mh,
+                      CUtensorMap* ml);
+
+// Dynamic shared memory to request so that the number of co-resident CTAs
+// never exceeds what TMEM can hold (512 columns per SM): a CTA never waits
+// inside tcgen05.alloc.
+constexpr int tmem_safe_smem(int need, int tmem_cols) {
+  const int max_ctas = 512 / tmem_cols;
+  const int floor_bytes = (228 * 1024) / (max_ctas + 1) + 1024;
+  return need > floor_bytes ? need : floor_bytes;
+}
+
 }  // namespace fpb

@@ -189,6 +189,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Same for 64-byte rows (SWIZZLE_64B, layout type 4): 8-row x 64-byte atoms
+// at a stride of 512 bytes.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)4u << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::tf32 / kind::f16 (bf16 inputs), f32
 // accumulate, both operands K-major. Bits: [4,6) D format (1 = f32),
 // [7,10) A format, [10,13) B format (tf32 = 2, bf16 = 1), [17,23) N>>3,
@@ -238,6 +250,19 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   lo = x - hi;
 }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+// 2^x on the SFU (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset inside a K-major SW64 tile (64-byte rows, 512-byte atoms).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t byte_in_row) {
+  return (row >> 3) * 512u + (row & 7u) * 64u +
+         ((((byte_in_row >> 4) ^ ((row >> 1) & 3u)) & 3u) << 4) + (byte_in_row & 15u);
+}
 
 // Byte offset of element (row, k) inside a K-major SW128 tile whose rows are
 // 128 bytes (32 fp32 / 64 bf16) wide: 8-row atoms of 1024 bytes, 16-byte

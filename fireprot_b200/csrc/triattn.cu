@@ -1,0 +1,1016 @@
+// Triangle attention around the starting / ending node, fused on sm_100a.
+//
+// Reference operator: TriangleAttention.forward with the "fireprot" kernel
+// (patches/protenix/0002-...patch:35-58, 0005-...patch:19-42), math as in
+// python/fireprot/adapters/atlasfold/runtime.py:32-71:
+//   x = LN(z) (z^T for the ending node); q,k,v = x W{q,k,v}^T (q * d^-1/2)
+//   b^h_jk = x_jk . Wbias_h ; s_ijk = q_ij . k_ik + 1e9 (mask_ik - 1) + b^h_jk
+//   o_ij = sum_k softmax_k(s) v_ik ; delta_ij = W_o (sigmoid(x Wg^T + bg) * o) + bo
+//   z <- z + delta (ending node: delta transposed back).
+//
+// Three launches per call, all in "y" coordinates (y = z, or z^T for the
+// ending node, addressed through transposed reads; nothing is copied):
+//  1. proj: LN + [Wq;Wk;Wv] GEMM (tcgen05, 128 x 384 per tile) + the 4-head
+//     pair bias on CUDA cores in FP32; writes q,k as [i][h][j][d], v as
+//     [i][h][d][k] (K-major for PV), bias [h][j][k], mask bias [i][k].
+//  2. attn: one CTA per (128 queries, head, row i); key tiles of 64 stream by
+//     TMA; S = Q K^T in TMEM (double-buffered), online softmax by the 128
+//     row threads (FP32, SFU exp2), P -> shared memory, P V on tcgen05 into
+//     TMEM, rescaled accumulation in registers.
+//  3. out: LN(z) Wg^T (GEMM 1) -> gate; A2 = sigmoid(.) * o -> W_o (GEMM 2),
+//     + bias, residual add in place.
+#include "kernels.h"
+#include "rowgemm.cuh"
+
+namespace fpb {
+
+constexpr int kHeads = 4;
+constexpr int kHeadDim = 32;
+constexpr float kMaskInf = 1e9f;
+
+// ============================================================================
+// 1. projection
+// ============================================================================
+struct AttnProjArgs {
+  const float* z;
+  const float* mask;  // nullable
+  int n;
+  float eps;
+  const float* ln_w;
+  const float* ln_b;
+  const float* w_bias;  // [4][128]
+  float q_scale;
+  void* q_hi;
+  void* q_lo;
+  void* k_hi;
+  void* k_lo;
+  void* v_hi;
+  void* v_lo;
+  int ldv;          // keys pitch of v^T
+  float* bias;      // [4][n][ldb]
+  int ldb;
+  float* mbias;     // [n][ldb] or null
+  int* status;
+};
+
+template <bool kStrict>
+constexpr int attn_proj_smem_bytes() {
+  using C = RowCfg<kStrict>;
+  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 2 * 4 * 128 * 4, 512);
+}
+
+template <bool kStrict, bool kTrans>
+__global__ void __launch_bounds__(192, 1)
+    attn_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
+                     const __grid_constant__ CUtensorMap w_lo, AttnProjArgs p) {
+  using C = RowCfg<kStrict>;
+  constexpr int WSTAGES = 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* A = smem;
+  uint8_t* W = smem + C::A_BYTES;
+  float* bias_tile = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // [4][128]
+  float* wb = bias_tile + 4 * 128;                                              // [4][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wb + 4 * 128);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = bars + WSTAGES;
+  uint64_t* a_full = bars + 2 * WSTAGES;
+  uint64_t* done = a_full + 1;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.n;
+  const long long npairs = (long long)n * n;
+  const long long p0 = (long long)blockIdx.x * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(a_full, 128);
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) wb[i] = p.w_bias[i];
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+  const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
+  constexpr int NLOADS = 3 * C::NKA;
+
+  if (warp < 4) {
+    const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
+    const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
+    float4 wbh[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) wbh[h] = reinterpret_cast<const float4*>(wb + h * 128)[lane];
+    const float4* z4 = reinterpret_cast<const float4*>(p.z);
+#pragma unroll 1
+    for (int rr = 0; rr < 32; rr += 4) {
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long pr = p0 + warp * 32 + rr + u;
+        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (pr < npairs) {
+          const long long r = pr / n, s = pr - r * n;
+          x[u] = __ldg(z4 + (kTrans ? (s * n + r) : pr) * 32 + lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = warp * 32 + rr + u;
+        const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
+        a_store4<kStrict>(A, row, lane * 4, y.x, y.y, y.z, y.w);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float b = warp_sum(y.x * wbh[h].x + y.y * wbh[h].y + y.z * wbh[h].z +
+                                   y.w * wbh[h].w);
+          if (lane == h) bias_tile[h * 128 + row] = b;
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(a_full);
+    // named barrier over the 128 row threads: bias_tile complete
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+
+    const int t = warp * 32 + lane;
+    const long long pr = p0 + t;
+    const bool valid = pr < npairs;
+    long long r = 0, s = 0;
+    if (valid) {
+      r = pr / n;
+      s = pr - r * n;
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        p.bias[((size_t)h * n + r) * p.ldb + s] = bias_tile[h * 128 + t];
+      if (p.mbias) {
+        const float m = __ldg(p.mask + (kTrans ? (s * n + r) : pr));
+        p.mbias[(size_t)r * p.ldb + s] = kMaskInf * (m - 1.0f);
+      }
+    }
+    if (mbar_wait(done, 0, g, 3)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int part = 0; part < 3; ++part) {
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          float v[32];
+          tmem_row32(tmem, warp, part * 128 + h * 32, v);
+          if (!valid) continue;
+          const size_t ih = (size_t)r * kHeads + h;
+          if (part < 2) {
+            const float sc = part == 0 ? p.q_scale : 1.0f;
+            const size_t row = ih * n + s;  // [i][h][j] row of 32
+            void* dh = part == 0 ? p.q_hi : p.k_hi;
+            void* dl = part == 0 ? p.q_lo : p.k_lo;
+            if constexpr (kStrict) {
+              float4* oh = reinterpret_cast<float4*>(static_cast<float*>(dh) + row * 32);
+              float4* ol = reinterpret_cast<float4*>(static_cast<float*>(dl) + row * 32);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float h0, l0, h1, l1, h2, l2, h3, l3;
+                split_tf32(v[4 * e] * sc, h0, l0);
+                split_tf32(v[4 * e + 1] * sc, h1, l1);
+                split_tf32(v[4 * e + 2] * sc, h2, l2);
+                split_tf32(v[4 * e + 3] * sc, h3, l3);
+                oh[e] = make_float4(h0, h1, h2, h3);
+                ol[e] = make_float4(l0, l1, l2, l3);
+              }
+            } else {
+              uint4* oh = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dh) + row * 32);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * e + 2 * u] * sc,
+                                                            v[8 * e + 2 * u + 1] * sc);
+                  w4[u] = *reinterpret_cast<uint32_t*>(&b2);
+                }
+                oh[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              }
+            }
+          } else {
+            // v^T: [i][h][d][k]
+#pragma unroll
+            for (int d = 0; d < 32; ++d) {
+              const size_t idx = (ih * 32 + d) * p.ldv + s;
+              if constexpr (kStrict) {
+                float hh, ll;
+                split_tf32(v[d], hh, ll);
+                static_cast<float*>(p.v_hi)[idx] = hh;
+                static_cast<float*>(p.v_lo)[idx] = ll;
+              } else {
+                static_cast<__nv_bfloat16*>(p.v_hi)[idx] = __float2bfloat16_rn(v[d]);
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int q = 0; q < NLOADS; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
+        ++issued;
+      }
+      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+    }
+  } else {
+    if (lane == 0) {
+      const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
+      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
+      bool ok = mbar_wait(a_full, 0, g, 4);
+      if (ok) tc_fence_after();
+      for (int q = 0; q < NLOADS && ok; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        const uint32_t w = wring_wait(ring, q, g);
+        if (!w) {
+          ok = false;
+          break;
+        }
+        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
+                            w, w + C::ATOM_BYTES, idesc, ka == 0);
+        wring_release(ring, q);
+      }
+      if (ok) {
+        umma_commit(done);
+      } else {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================
+// 2. attention core
+// ============================================================================
+struct AttnCoreArgs {
+  int n;
+  const float* bias;   // [4][n][ldb]
+  const float* mbias;  // [n][ldb] or null
+  int ldb;
+  void* o;             // [n*n][128] fp32 (strict) / bf16 (fast), y coordinates
+  int* status;
+};
+
+template <bool kStrict>
+struct AttnCfg {
+  static constexpr int BQ = 128;
+  static constexpr int BKV = 64;
+  static constexpr int ESZ = kStrict ? 4 : 2;
+  static constexpr int NSPLIT = kStrict ? 2 : 1;
+  static constexpr int QK_ROW = 32 * ESZ;                 // bytes per q/k row (128 / 64)
+  static constexpr int Q_BYTES = BQ * QK_ROW;             // per split
+  static constexpr int K_BYTES = BKV * QK_ROW;            // per split
+  static constexpr int V_ATOM_KEYS = 128 / ESZ;           // 32 / 64 keys per 128-byte row
+  static constexpr int V_ATOMS = BKV / V_ATOM_KEYS;       // 2 / 1
+  static constexpr int V_BYTES = V_ATOMS * 32 * 128;      // per split
+  static constexpr int KV_STAGE = NSPLIT * (K_BYTES + V_BYTES);
+  static constexpr int KV_STAGES = kStrict ? 2 : 3;
+  static constexpr int P_ATOMS = BKV / V_ATOM_KEYS;       // K atoms of P
+  static constexpr int P_BYTES = P_ATOMS * BQ * 128;      // per split
+  static constexpr int SMEM =
+      tmem_safe_smem(NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + NSPLIT * P_BYTES + 1024 + 256, 256);
+};
+
+template <bool kStrict>
+__device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
+  if constexpr (kStrict)
+    return umma_desc_sw128(addr);
+  else
+    return umma_desc_sw64(addr);
+}
+
+template <bool kStrict>
+__global__ void __launch_bounds__(192, 1)
+    attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
+                     const __grid_constant__ CUtensorMap mq_lo,
+                     const __grid_constant__ CUtensorMap mk_hi,
+                     const __grid_constant__ CUtensorMap mk_lo,
+                     const __grid_constant__ CUtensorMap mv_hi,
+                     const __grid_constant__ CUtensorMap mv_lo, AttnCoreArgs p) {
+  using C = AttnCfg<kStrict>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* Q = smem;                                   // [split][BQ x QK_ROW]
+  uint8_t* KV = Q + C::NSPLIT * C::Q_BYTES;            // stages
+  uint8_t* P = KV + C::KV_STAGES * C::KV_STAGE;        // [split][P_ATOMS][BQ x 128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(P + C::NSPLIT * C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + C::KV_STAGES;
+  uint64_t* s_full = kv_empty + C::KV_STAGES;   // [2]
+  uint64_t* s_free = s_full + 2;                // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_full = p_full + 1;
+  uint64_t* drain = pv_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.n;
+  const int jt = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
+  const int ih = i * kHeads + h;
+  const int nt = (n + C::BKV - 1) / C::BKV;
+  // TMEM columns: S[0] 0..63, S[1] 64..127, PV 128..159
+  constexpr uint32_t kS0 = 0, kPV = 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::KV_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, C::NSPLIT * C::Q_BYTES);
+      tma_load_3d(Q, &mq_hi, q_full, 0, jt * C::BQ, ih);
+      if constexpr (kStrict) tma_load_3d(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih);
+      int issued = 0;
+      for (int t = 0; t < nt; ++t) {
+        const int s = t % C::KV_STAGES;
+        const uint32_t ph = (t / C::KV_STAGES) & 1;
+        if (t >= C::KV_STAGES && !mbar_wait(&kv_empty[s], ph ^ 1, g, 21)) break;
+        uint8_t* st = KV + s * C::KV_STAGE;
+        mbar_arrive_expect_tx(&kv_full[s], C::KV_STAGE);
+        tma_load_3d(st, &mk_hi, &kv_full[s], 0, t * C::BKV, ih);
+        uint8_t* vst = st + C::NSPLIT * C::K_BYTES;
+#pragma unroll
+        for (int a = 0; a < C::V_ATOMS; ++a)
+          tma_load_3d(vst + a * 4096, &mv_hi, &kv_full[s], t * C::BKV + a * C::V_ATOM_KEYS, 0, ih);
+        if constexpr (kStrict) {
+          tma_load_3d(st + C::K_BYTES, &mk_lo, &kv_full[s], 0, t * C::BKV, ih);
+#pragma unroll
+          for (int a = 0; a < C::V_ATOMS; ++a)
+            tma_load_3d(vst + C::V_BYTES + a * 4096, &mv_lo, &kv_full[s],
+                        t * C::BKV + a * C::V_ATOM_KEYS, 0, ih);
+        }
+        ++issued;
+      }
+      if (g.aborted()) {
+        for (int t = (issued > C::KV_STAGES ? issued - C::KV_STAGES : 0); t < issued; ++t)
+          (void)mbar_wait(&kv_full[t % C::KV_STAGES], (t / C::KV_STAGES) & 1,
+                          Guard{nullptr, abort_flag}, 0);
+        (void)mbar_wait(q_full, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t id_s = kStrict ? idesc_tf32(128, C::BKV) : idesc_bf16(128, C::BKV);
+      const uint32_t id_o = kStrict ? idesc_tf32(128, 32) : idesc_bf16(128, 32);
+      const uint32_t q_hi = smem_u32(Q), q_lo = smem_u32(Q + C::Q_BYTES);
+      const uint32_t p_hi = smem_u32(P), p_lo = smem_u32(P + C::P_BYTES);
+      constexpr int QK_STEPS = C::QK_ROW / 32;  // 4 (fp32) or 2 (bf16) K steps over d
+      bool ok = mbar_wait(q_full, 0, g, 22);
+      auto issue_pv = [&](int u) -> bool {
+        if (!mbar_wait(p_full, u & 1, g, 23)) return false;
+        tc_fence_after();
+        const uint32_t vst = smem_u32(KV + (u % C::KV_STAGES) * C::KV_STAGE +
+                                      C::NSPLIT * C::K_BYTES);
+        // K = 64 keys, in P_ATOMS atoms of 128 bytes, 4 x 32-byte steps each
+#pragma unroll
+        for (int a = 0; a < C::P_ATOMS; ++a) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t off = a * (C::BQ * 128) + kk * 32;
+            const uint32_t voff = a * 4096 + kk * 32;
+            const uint32_t acc = (a == 0 && kk == 0) ? 0u : 1u;
+            const uint64_t dph = umma_desc_sw128(p_hi + off);
+            const uint64_t dvh = umma_desc_sw128(vst + voff);
+            if constexpr (kStrict) {
+              const uint64_t dpl = umma_desc_sw128(p_lo + off);
+              const uint64_t dvl = umma_desc_sw128(vst + C::V_BYTES + voff);
+              umma_tf32(tmem + kPV, dph, dvh, id_o, acc);
+              umma_tf32(tmem + kPV, dph, dvl, id_o, 1u);
+              umma_tf32(tmem + kPV, dpl, dvh, id_o, 1u);
+            } else {
+              umma_bf16(tmem + kPV, dph, dvh, id_o, acc);
+            }
+          }
+        }
+        umma_commit(pv_full);
+        umma_commit(&kv_empty[u % C::KV_STAGES]);
+        return true;
+      };
+      if (ok) tc_fence_after();
+      for (int t = 0; t < nt && ok; ++t) {
+        const int s = t % C::KV_STAGES;
+        if (!mbar_wait(&kv_full[s], (t / C::KV_STAGES) & 1, g, 24)) {
+          ok = false;
+          break;
+        }
+        if (t >= 2 && !mbar_wait(&s_free[t & 1], ((t - 2) >> 1) & 1, g, 25)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kst = smem_u32(KV + s * C::KV_STAGE);
+        const uint32_t sbuf = tmem + kS0 + (t & 1) * C::BKV;
+#pragma unroll
+        for (int kk = 0; kk < QK_STEPS; ++kk) {
+          const uint32_t off = kk * 32;
+          const uint64_t dqh = qk_desc<kStrict>(q_hi + off);
+          const uint64_t dkh = qk_desc<kStrict>(kst + off);
+          const uint32_t acc = kk == 0 ? 0u : 1u;
+          if constexpr (kStrict) {
+            const uint64_t dql = qk_desc<kStrict>(q_lo + off);
+            const uint64_t dkl = qk_desc<kStrict>(kst + C::K_BYTES + off);
+            umma_tf32(sbuf, dqh, dkh, id_s, acc);
+            umma_tf32(sbuf, dqh, dkl, id_s, 1u);
+            umma_tf32(sbuf, dql, dkh, id_s, 1u);
+          } else {
+            umma_bf16(sbuf, dqh, dkh, id_s, acc);
+          }
+        }
+        umma_commit(&s_full[t & 1]);
+        if (t >= 1 && !issue_pv(t - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nt >= 1) ok = issue_pv(nt - 1);
+      if (!ok) {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t_row = warp * 32 + lane;  // TMEM lane / query row in tile
+    const int j = jt * C::BQ + t_row;
+    const bool jvalid = j < n;
+    const float* brow = p.bias + ((size_t)h * n + (jvalid ? j : 0)) * p.ldb;
+    const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
+    constexpr float kLog2e = 1.4426950408889634f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+    float o[32];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] = 0.f;
+    bool ok = true;
+    for (int t = 0; t < nt && ok; ++t) {
+      float sv[C::BKV];
+      if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, g, 26)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      {
+        float tmp[32];
+        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, 0, tmp);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = tmp[e];
+        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, 32, tmp);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[32 + e] = tmp[e];
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[t & 1]);
+      const int k0 = t * C::BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
+        const int k = k0 + 4 * e4;
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), mb = make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool full4 = (k + 4 <= n);
+        if (full4) {
+          if (jvalid) bb = __ldg(reinterpret_cast<const float4*>(brow + k));
+          if (mrow) mb = __ldg(reinterpret_cast<const float4*>(mrow + k));
+        } else {
+          float btmp[4] = {0.f, 0.f, 0.f, 0.f}, mtmp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (k + u < n) {
+              if (jvalid) btmp[u] = brow[k + u];
+              if (mrow) mtmp[u] = mrow[k + u];
+            }
+          bb = make_float4(btmp[0], btmp[1], btmp[2], btmp[3]);
+          mb = make_float4(mtmp[0], mtmp[1], mtmp[2], mtmp[3]);
+        }
+        // reference order: (q.k + mask bias) + triangle bias
+        float* s4 = sv + 4 * e4;
+        s4[0] = (k + 0 < n) ? (s4[0] + mb.x) + bb.x : -INFINITY;
+        s4[1] = (k + 1 < n) ? (s4[1] + mb.y) + bb.y : -INFINITY;
+        s4[2] = (k + 2 < n) ? (s4[2] + mb.z) + bb.z : -INFINITY;
+        s4[3] = (k + 3 < n) ? (s4[3] + mb.w) + bb.w : -INFINITY;
+        mx = fmaxf(mx, fmaxf(fmaxf(s4[0], s4[1]), fmaxf(s4[2], s4[3])));
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first tile
+      float lsum = 0.f;
+#pragma unroll
+      for (int e = 0; e < C::BKV; ++e) {
+        sv[e] = ex2_approx((sv[e] - m_new) * kLog2e);
+        lsum += sv[e];
+      }
+      l_run = l_run * alpha + lsum;
+      m_run = m_new;
+      // fold the previous tile's P V (its MMA also released the P buffer)
+      if (t >= 1) {
+        if (!mbar_wait(pv_full, (t - 1) & 1, g, 27)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float pv[32];
+        tmem_row32(tmem + kPV, warp, 0, pv);
+#pragma unroll
+        for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha_prev + pv[d];
+      }
+      alpha_prev = alpha;
+      // P -> shared memory (A operand of P V, K-major, 128-byte swizzle)
+#pragma unroll
+      for (int c = 0; c < C::BKV; c += 4) {
+        const int byte = (c * C::ESZ) % 128;
+        uint8_t* dst = P + (c / C::V_ATOM_KEYS) * (C::BQ * 128) + sw128_offset(t_row, byte);
+        if constexpr (kStrict) {
+          float h0, l0, h1, l1, h2, l2, h3, l3;
+          split_tf32(sv[c], h0, l0);
+          split_tf32(sv[c + 1], h1, l1);
+          split_tf32(sv[c + 2], h2, l2);
+          split_tf32(sv[c + 3], h3, l3);
+          *reinterpret_cast<float4*>(dst) = make_float4(h0, h1, h2, h3);
+          *reinterpret_cast<float4*>(dst + C::P_BYTES) = make_float4(l0, l1, l2, l3);
+        } else {
+          __nv_bfloat162 a = __floats2bfloat162_rn(sv[c], sv[c + 1]);
+          __nv_bfloat162 b = __floats2bfloat162_rn(sv[c + 2], sv[c + 3]);
+          uint2 w;
+          w.x = *reinterpret_cast<uint32_t*>(&a);
+          w.y = *reinterpret_cast<uint32_t*>(&b);
+          *reinterpret_cast<uint2*>(dst) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && nt >= 1 && mbar_wait(pv_full, (nt - 1) & 1, g, 28)) {
+      tc_fence_after();
+      float pv[32];
+      tmem_row32(tmem + kPV, warp, 0, pv);
+      const float inv = 1.0f / l_run;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) o[d] = (o[d] * alpha_prev + pv[d]) * inv;
+      if (jvalid) {
+        const size_t orow = (size_t)i * n + j;
+        if constexpr (kStrict) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * 128 + h * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dst[e] = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * 128 +
+                                                h * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * e + 2 * u], o[8 * e + 2 * u + 1]);
+              w4[u] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            dst[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ============================================================================
+// 3. gate + output projection + residual
+// ============================================================================
+struct AttnOutArgs {
+  float* z;
+  int n;
+  float eps;
+  const float* ln_w;
+  const float* ln_b;
+  const float* b_g;  // [128] or null
+  const float* b_o;  // [128] or null
+  const void* o;     // [n*n][128] y coordinates
+  int* status;
+};
+
+template <bool kStrict>
+constexpr int attn_out_smem_bytes() {
+  using C = RowCfg<kStrict>;
+  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
+}
+
+template <bool kStrict, bool kTrans>
+__global__ void __launch_bounds__(192, 1)
+    attn_out_kernel(const __grid_constant__ CUtensorMap w_hi,
+                    const __grid_constant__ CUtensorMap w_lo, AttnOutArgs p) {
+  using C = RowCfg<kStrict>;
+  constexpr int WSTAGES = 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* A = smem;
+  uint8_t* W = smem + C::A_BYTES;
+  float* bvec = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // b_g, b_o
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bvec + 256);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = bars + WSTAGES;
+  uint64_t* a_full = bars + 2 * WSTAGES;
+  uint64_t* g_done = a_full + 1;
+  uint64_t* done = g_done + 1;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = p.n;
+  const long long npairs = (long long)n * n;
+  const long long p0 = (long long)blockIdx.x * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(a_full, 128);
+    mbar_init(g_done, 1);
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 128) {
+    bvec[threadIdx.x] = p.b_g ? p.b_g[threadIdx.x] : 0.f;
+    bvec[128 + threadIdx.x] = p.b_o ? p.b_o[threadIdx.x] : 0.f;
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+  const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
+  constexpr int NLOADS = 2 * C::NKA;
+
+  if (warp < 4) {
+    {
+      const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
+      const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
+      const float4* z4 = reinterpret_cast<const float4*>(p.z);
+#pragma unroll 1
+      for (int rr = 0; rr < 32; rr += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long pr = p0 + warp * 32 + rr + u;
+          x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (pr < npairs) {
+            const long long r = pr / n, s = pr - r * n;
+            x[u] = z4[(kTrans ? (s * n + r) : pr) * 32 + lane];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
+          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+    }
+    const int t = warp * 32 + lane;
+    const long long pr = p0 + t;
+    const bool valid = pr < npairs;
+    long long zrow_idx = 0;
+    if (valid) {
+      const long long r = pr / n, s = pr - r * n;
+      zrow_idx = kTrans ? (s * n + r) : pr;
+    }
+    // gate from GEMM 1, times o -> A2 (after GEMM 1 retired)
+    if (mbar_wait(g_done, 0, g, 5)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float gv[32];
+        tmem_row32(tmem, warp, cc * 32, gv);
+        float ov[32];
+        if (valid) {
+          if constexpr (kStrict) {
+            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.o) +
+                                                                pr * 128 + cc * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float4 v = src[e];
+              ov[4 * e] = v.x;
+              ov[4 * e + 1] = v.y;
+              ov[4 * e + 2] = v.z;
+              ov[4 * e + 3] = v.w;
+            }
+          } else {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                static_cast<const __nv_bfloat16*>(p.o) + pr * 128 + cc * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 v = src[e];
+              const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+                ov[8 * e + 2 * u] = __bfloat162float(b2.x);
+                ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const int c = cc * 32 + e;
+          a_store4<kStrict>(A, t, c, sigmoidf_(gv[e] + bvec[c]) * ov[e],
+                            sigmoidf_(gv[e + 1] + bvec[c + 1]) * ov[e + 1],
+                            sigmoidf_(gv[e + 2] + bvec[c + 2]) * ov[e + 2],
+                            sigmoidf_(gv[e + 3] + bvec[c + 3]) * ov[e + 3]);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(a_full);
+    if (mbar_wait(done, 0, g, 3)) {
+      tc_fence_after();
+      float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float yv[32];
+        tmem_row32(tmem, warp, 128 + cc * 32, yv);
+        if (valid) {
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 o = zrow[cc * 8 + v4];
+            const int c = cc * 32 + 4 * v4;
+            o.x += yv[4 * v4] + bvec[128 + c];
+            o.y += yv[4 * v4 + 1] + bvec[129 + c];
+            o.z += yv[4 * v4 + 2] + bvec[130 + c];
+            o.w += yv[4 * v4 + 3] + bvec[131 + c];
+            zrow[cc * 8 + v4] = o;
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int q = 0; q < NLOADS; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
+        ++issued;
+      }
+      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+    }
+  } else {
+    if (lane == 0) {
+      const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
+      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
+      bool ok = true;
+      for (int q = 0; q < NLOADS && ok; ++q) {
+        const int nc = q / C::NKA, ka = q % C::NKA;
+        if (ka == 0) {
+          if (nc == 1) umma_commit(g_done);
+          if (!mbar_wait(a_full, nc & 1, g, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t w = wring_wait(ring, q, g);
+        if (!w) {
+          ok = false;
+          break;
+        }
+        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
+                            w, w + C::ATOM_BYTES, idesc, ka == 0);
+        wring_release(ring, q);
+      }
+      if (ok) {
+        umma_commit(done);
+      } else {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ============================================================================
+// host
+// ============================================================================
+template <class Alloc>
+struct TriAttnPlan {
+  void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
+  void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr;
+  void *v_hi = nullptr, *v_lo = nullptr, *o = nullptr;
+  float *bias = nullptr, *mbias = nullptr;
+  int ldv = 0, ldb = 0;
+  void plan(Alloc& al, int n, bool strict, bool with_mask) {
+    auto take = [&](size_t c) -> void* {
+      return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
+    };
+    wp_hi = take(384 * 128);
+    if (strict) wp_lo = take(384 * 128);
+    wo_hi = take(256 * 128);
+    if (strict) wo_lo = take(256 * 128);
+    const size_t qk = (size_t)n * n * 128;
+    q_hi = take(qk);
+    k_hi = take(qk);
+    if (strict) {
+      q_lo = take(qk);
+      k_lo = take(qk);
+    }
+    ldv = padded_ld(n, strict ? 4 : 2);
+    const size_t vc = (size_t)n * kHeads * 32 * ldv;
+    v_hi = take(vc);
+    if (strict) v_lo = take(vc);
+    ldb = padded_ld(n, 4);
+    bias = al.template take<float>((size_t)kHeads * n * ldb);
+    if (with_mask) mbias = al.template take<float>((size_t)n * ldb);
+    o = take((size_t)n * n * 128);
+  }
+};
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head_dim,
+                                             int precision, int with_mask) {
+  if (n <= 0 || c_z != 128 || heads != kHeads || head_dim != kHeadDim) return 0;
+  if (precision != 0 && precision != 1) return 0;
+  WsCounter cnt;
+  TriAttnPlan<WsCounter> pl;
+  pl.plan(cnt, n, precision == 0, with_mask != 0);
+  return cnt.used;
+}
+
+extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head_dim,
+                           const float* ln_w, const float* ln_b, const float* w_q,
+                           const float* w_k, const float* w_v, const float* w_bias,
+                           const float* w_g, const float* b_g, const float* w_o,
+                           const float* b_o, float eps, int starting, int precision,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!z || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias || !w_g || !w_o || !workspace)
+    return kErrArg;
+  if (c_z != 128 || heads != kHeads || head_dim != kHeadDim || n <= 0) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
+    return kErrAlign;
+  const bool strict = precision == 0;
+  const bool with_mask = mask != nullptr;
+  if (workspace_bytes <
+      fpb_triattn_workspace_size(n, c_z, heads, head_dim, precision, with_mask ? 1 : 0))
+    return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  TriAttnPlan<WsCursor> pl;
+  pl.plan(cur, n, strict, with_mask);
+  if (!cur.ok) return kErrWorkspace;
+  int* status = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  int st;
+  if ((st = pack_weights(PackSrc{{w_q, w_k, w_v, nullptr}, 3, 128}, pl.wp_hi, pl.wp_lo, strict,
+                         stream)))
+    return st;
+  if ((st = pack_weights(PackSrc{{w_g, w_o, nullptr, nullptr}, 2, 128}, pl.wo_hi, pl.wo_lo,
+                         strict, stream)))
+    return st;
+  CUtensorMap mph, mpl, moh, mol;
+  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl) ||
+      !make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol))
+    return kErrArg;
+  const bool trans = !starting;
+  const long long npairs = (long long)n * n;
+  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+
+  // 1. projection
+  AttnProjArgs pa{z, mask, n, eps, ln_w, ln_b, w_bias, 1.0f / sqrtf((float)kHeadDim),
+                  pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, pl.ldv, pl.bias, pl.ldb,
+                  pl.mbias, status};
+  {
+    const int smem = strict ? attn_proj_smem_bytes<true>() : attn_proj_smem_bytes<false>();
+    auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
+                    : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<tiles, 192, smem, stream>>>(mph, mpl, pa);
+    if ((st = launch_status())) return st;
+  }
+  // 2. attention core
+  {
+    const int esz = strict ? 4 : 2;
+    const CUtensorMapDataType dt =
+        strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const uint64_t rowb = 32ull * esz;
+    CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+    const uint64_t nh = (uint64_t)n * kHeads;
+    bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+              make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, 64, 1, qsw) &&
+              make_map_3d(&mvh, pl.v_hi, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
+                          (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
+    if (strict)
+      ok = ok && make_map_3d(&mql, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+           make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, 64, 1, qsw) &&
+           make_map_3d(&mvl, pl.v_lo, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
+                       (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
+    else {
+      mql = mqh;
+      mkl = mkh;
+      mvl = mvh;
+    }
+    if (!ok) return kErrArg;
+    AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, pl.o, status};
+    dim3 grid((n + 127) / 128, kHeads, n);
+    if (strict) {
+      auto k = attn_core_kernel<true>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
+      k<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca);
+    } else {
+      auto k = attn_core_kernel<false>;
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
+      k<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca);
+    }
+    if ((st = launch_status())) return st;
+  }
+  // 3. gate + output projection + residual
+  AttnOutArgs oa{z, n, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
+  {
+    const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
+    auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
+                    : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<tiles, 192, smem, stream>>>(moh, mol, oa);
+    if ((st = launch_status())) return st;
+  }
+  return kOk;
+}

@@ -40,10 +40,7 @@ struct TriMulProjArgs {
 template <bool kStrict>
 constexpr int proj_smem_bytes() {
   using C = RowCfg<kStrict>;
-  // fast mode requests extra shared memory so that only one CTA (and one
-  // 512-column TMEM allocation) is resident per SM.
-  const int need = C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256;
-  return need < 120 * 1024 ? 120 * 1024 : need;
+  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256, 512);
 }
 
 template <bool kStrict, bool kTrans>
@@ -227,7 +224,7 @@ struct TriMulOutArgs {
 template <bool kStrict>
 constexpr int out_smem_bytes() {
   using C = RowCfg<kStrict>;
-  return C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024 /*ln_out params*/;
+  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
 }
 
 template <bool kStrict>
@@ -430,12 +427,6 @@ __global__ void __launch_bounds__(192, 1)
 // weight packing: concatenate up to 4 [rows][128] FP32 matrices and split
 // them into tf32 hi/lo (strict) or convert to BF16 (fast).
 // ----------------------------------------------------------------------------
-struct PackSrc {
-  const float* m[4];
-  int count;
-  int rows_each;
-};
-
 __global__ void pack_weights_kernel(PackSrc src, void* hi, void* lo, int strict) {
   const int total = src.count * src.rows_each * 128;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {

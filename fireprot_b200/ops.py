@@ -103,3 +103,44 @@ def trimul(z: torch.Tensor, mask, w: dict, *, outgoing: bool, add: bool = True,
                               int(bool(add)), p, ws.data_ptr(), ws.numel(),
                               _stream_ptr(z.device)), "fpb_trimul")
     return (z, ws) if return_workspace else z
+
+
+TRIATTN_WEIGHTS = ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias", "w_g", "b_g", "w_o", "b_o")
+
+
+def triattn(z: torch.Tensor, mask, w: dict, *, starting: bool = True, precision="strict",
+            eps: float = 1e-5, return_workspace: bool = False):
+    """Triangle attention update added in place to ``z`` ``[n, n, 128]``
+    (H=4, d=32). ``w`` holds ``ln_w, ln_b, w_q, w_k, w_v, w_bias, w_g, w_o``
+    and optional ``b_g`` / ``b_o``. Returns ``z`` (same storage)."""
+    _require_cuda(z, mask)
+    if z.dtype != torch.float32 or z.ndim != 3 or z.shape[0] != z.shape[1] or z.shape[2] != 128:
+        raise RuntimeError("triattn takes a float32 [n, n, 128] pair tensor")
+    if not z.is_contiguous() or z.data_ptr() % 16:
+        raise RuntimeError("triattn needs a contiguous, 16-byte aligned z")
+    n = z.shape[0]
+    if mask is not None:
+        if tuple(mask.shape) != (n, n):
+            raise RuntimeError("mask must be [n, n]")
+        mask = mask.to(torch.float32).contiguous()
+    ptrs = []
+    keep = []
+    for k in TRIATTN_WEIGHTS:
+        t = w.get(k)
+        if t is None:
+            if k in ("b_g", "b_o"):
+                ptrs.append(0)
+                continue
+            raise RuntimeError(f"missing weight {k}")
+        t = _f32(t, k)
+        _require_cuda(t)
+        keep.append(t)
+        ptrs.append(t.data_ptr())
+    lib = _lib.load()
+    p = precision_code(precision)
+    ws = workspace(lib.fpb_triattn_workspace_size(n, 128, 4, 32, p, int(mask is not None)),
+                   z.device)
+    _lib.check(lib.fpb_triattn(z.data_ptr(), 0 if mask is None else mask.data_ptr(), n, 128, 4, 32,
+                               *ptrs, float(eps), int(bool(starting)), p, ws.data_ptr(),
+                               ws.numel(), _stream_ptr(z.device)), "fpb_triattn")
+    return (z, ws) if return_workspace else z

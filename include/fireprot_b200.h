@@ -70,6 +70,27 @@ int fpb_trimul(float* z, const float* mask, int n, int c_z, const float* ln_in_w
                const float* w_z, float eps, int outgoing, int add, int precision, void* workspace,
                size_t workspace_bytes, cudaStream_t stream);
 
+/* Triangle attention (starting node when starting = 1, ending node when 0),
+ * whole operator, residual added in place: z <- z + delta with
+ *   x = LN(y), y = z (start) or z^T (end, mask^T);
+ *   s_ijk = (x_ij Wq_h^T/sqrt(d)) . (x_ik Wk_h^T) + 1e9 (mask_ik - 1) + x_jk . Wbias_h
+ *   o_ij = sum_k softmax_k(s) (x_ik Wv_h^T); delta = W_o (sigmoid(x Wg^T + b_g) * o) + b_o
+ * (end node: delta transposed back). heads = 4, head_dim = 32, c_z = 128;
+ * w_q/w_k/w_v/w_g [128,128], w_bias [4,128], w_o [128,128]; b_g, b_o nullable.
+ * Replaces dispatch_triangle_attention + the QKV / gate hooks
+ * (python/fireprot/backends/amd/triangle_attention.py:199-256,
+ * qkv_projection.py:54-66, attention_gate.py:28-56) and their kernels
+ * project_qkv / ck_attention* / sigmoid_mul_out (kernels/amd/fireprot_amd_ops.cu:
+ * 537-565,871-955; kernels/amd/fireprot_ck_attention.cpp:34-121).
+ * The mask bias follows patches/protenix/0005-...patch:35-38 (inf = 1e9). */
+size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head_dim, int precision,
+                                  int with_mask);
+int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head_dim,
+                const float* ln_w, const float* ln_b, const float* w_q, const float* w_k,
+                const float* w_v, const float* w_bias, const float* w_g, const float* b_g,
+                const float* w_o, const float* b_o, float eps, int starting, int precision,
+                void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,9 @@ SIGNATURES = {
     "fpb_triattn_workspace_size": (c_size_t, [c_int] * 6),
     "fpb_triattn": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int] + [c_void_p] * 10
                     + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_transition_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "fpb_transition": (c_int, [c_void_p, ctypes.c_longlong, c_int, c_int] + [c_void_p] * 5
+                       + [c_float, c_int, c_void_p, c_size_t, c_void_p]),
 }
 
 ABI_VERSION = 1

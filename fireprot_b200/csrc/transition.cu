@@ -1,0 +1,413 @@
+// Pair transition (SwiGLU, 4x expansion), fused on sm_100a.
+//
+// Reference: Protenix Transition as dispatched by
+// python/fireprot/backends/amd/recycle.py:203-227,360 (projection kernel
+// kernels/amd/fireprot_amd_ops.cu:1106-1183):
+//   x = LN(z); h = silu(x Wa^T) * (x Wb^T)   (Wa, Wb [512,128])
+//   z <- z + h Wout^T                        (Wout [128,512])
+//
+// One kernel per 128-row tile. The hidden dimension is processed in chunks of
+// HC = one 128-byte K atom (32 fp32 / 64 bf16): GEMM 1 computes [a_c | b_c]
+// (N = 2*HC) into a double-buffered TMEM region, the row threads form
+// h_c = silu(a_c) * b_c and write it to shared memory as the A operand of
+// GEMM 2, which accumulates h_c Wout[:, c]^T into a 128-column TMEM
+// accumulator. The 4x-wide intermediate never reaches HBM.
+#include "kernels.h"
+#include "rowgemm.cuh"
+
+namespace fpb {
+
+template <bool kStrict>
+struct TransCfg {
+  using R = RowCfg<kStrict>;
+  static constexpr int HC = R::KATOM;          // hidden chunk = one K atom
+  static constexpr int NCH = 512 / HC;         // 16 / 8 chunks
+  static constexpr int G1N = 2 * HC;           // GEMM 1 width (a_c | b_c)
+  static constexpr int G1_STAGE = G1N * 128 * R::NSPLIT;   // bytes of one GEMM-1 W stage
+  static constexpr int G2_STAGE = 128 * 128 * R::NSPLIT;   // bytes of one GEMM-2 W stage
+  static constexpr int STAGE = G1_STAGE > G2_STAGE ? G1_STAGE : G2_STAGE;
+  static constexpr int STAGES = kStrict ? 2 : 3;
+  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows
+  static constexpr int TMEM_COLS = kStrict ? 256 : 512;    // 2*G1N + 128 rounded up
+  static constexpr int SMEM = tmem_safe_smem(R::A_BYTES + H_BYTES + STAGES * STAGE + 1024 + 256,
+                                             TMEM_COLS);
+};
+
+struct TransArgs {
+  float* z;
+  int n_rows;
+  float eps;
+  const float* ln_w;
+  const float* ln_b;
+  int* status;
+};
+
+template <bool kStrict>
+__global__ void __launch_bounds__(192, 1)
+    transition_kernel(const __grid_constant__ CUtensorMap w1_hi,
+                      const __grid_constant__ CUtensorMap w1_lo,
+                      const __grid_constant__ CUtensorMap w2_hi,
+                      const __grid_constant__ CUtensorMap w2_lo, TransArgs p) {
+  using R = RowCfg<kStrict>;
+  using C = TransCfg<kStrict>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* A = smem;
+  uint8_t* H = A + R::A_BYTES;
+  uint8_t* W = H + C::H_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(W + C::STAGES * C::STAGE);
+  uint64_t* wfull = bars;
+  uint64_t* wempty = wfull + C::STAGES;
+  uint64_t* a_full = wempty + C::STAGES;
+  uint64_t* g1_full = a_full + 1;   // [2]
+  uint64_t* g1_free = g1_full + 2;  // [2]
+  uint64_t* h_full = g1_free + 2;
+  uint64_t* h_free = h_full + 1;
+  uint64_t* done = h_free + 1;
+  uint64_t* drain = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long rows = p.n_rows;
+  const long long p0 = (long long)blockIdx.x * 128;
+  constexpr uint32_t kAcc = 2 * C::G1N;  // accumulator columns [kAcc, kAcc + 128)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    mbar_init(a_full, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&g1_full[b], 1);
+      mbar_init(&g1_free[b], 128);
+    }
+    mbar_init(h_full, 128);
+    mbar_init(h_free, 1);
+    mbar_init(done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const Guard g{p.status, abort_flag};
+
+  // Weight-load sequence shared by the TMA and MMA threads:
+  // G1(0), then for c = 0..NCH-1: [G1(c+1)], G2(c). G1 chunk = R::NKA loads.
+  // seq index -> (is_g2, chunk, atom)
+  if (warp < 4) {
+    {
+      const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
+      const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
+      const float4* z4 = reinterpret_cast<const float4*>(p.z);
+#pragma unroll 1
+      for (int rr = 0; rr < 32; rr += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long pr = p0 + warp * 32 + rr + u;
+          x[u] = pr < rows ? __ldg(z4 + pr * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
+          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+    }
+    const int t = warp * 32 + lane;
+    bool ok = true;
+#pragma unroll 1
+    for (int c = 0; c < C::NCH && ok; ++c) {
+      const int b = c & 1;
+      if (!mbar_wait(&g1_full[b], (c >> 1) & 1, g, 31)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float hv[C::HC];
+#pragma unroll
+      for (int q = 0; q < C::HC / 32; ++q) {
+        float av[32], bv[32];
+        tmem_row32(tmem + b * C::G1N, warp, q * 32, av);
+        tmem_row32(tmem + b * C::G1N, warp, C::HC + q * 32, bv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) hv[q * 32 + e] = av[e] * sigmoidf_(av[e]) * bv[e];
+      }
+      tc_fence_before();
+      mbar_arrive(&g1_free[b]);
+      if (c >= 1 && !mbar_wait(h_free, (c - 1) & 1, g, 32)) {
+        ok = false;
+        break;
+      }
+      // H row t: one K atom (HC elements)
+#pragma unroll
+      for (int e = 0; e < C::HC; e += 4) {
+        uint8_t* dst = H + sw128_offset(t, e * R::ESZ);
+        if constexpr (kStrict) {
+          float h0, l0, h1, l1, h2, l2, h3, l3;
+          split_tf32(hv[e], h0, l0);
+          split_tf32(hv[e + 1], h1, l1);
+          split_tf32(hv[e + 2], h2, l2);
+          split_tf32(hv[e + 3], h3, l3);
+          *reinterpret_cast<float4*>(dst) = make_float4(h0, h1, h2, h3);
+          *reinterpret_cast<float4*>(dst + R::ATOM_BYTES) = make_float4(l0, l1, l2, l3);
+        } else {
+          __nv_bfloat162 x0 = __floats2bfloat162_rn(hv[e], hv[e + 1]);
+          __nv_bfloat162 x1 = __floats2bfloat162_rn(hv[e + 2], hv[e + 3]);
+          uint2 w;
+          w.x = *reinterpret_cast<uint32_t*>(&x0);
+          w.y = *reinterpret_cast<uint32_t*>(&x1);
+          *reinterpret_cast<uint2*>(dst) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(h_full);
+    }
+    if (ok && mbar_wait(done, 0, g, 3)) {
+      tc_fence_after();
+      const long long pr = p0 + t;
+      float4* zrow = reinterpret_cast<float4*>(p.z) + (pr < rows ? pr : 0) * 32;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float yv[32];
+        tmem_row32(tmem + kAcc, warp, cc * 32, yv);
+        if (pr < rows) {
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 o = zrow[cc * 8 + v4];
+            o.x += yv[4 * v4];
+            o.y += yv[4 * v4 + 1];
+            o.z += yv[4 * v4 + 2];
+            o.w += yv[4 * v4 + 3];
+            zrow[cc * 8 + v4] = o;
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int seq = 0;
+      bool ok = true;
+      auto push = [&](bool g2, int c, int atom) -> bool {
+        const int s = seq % C::STAGES;
+        const uint32_t ph = (seq / C::STAGES) & 1;
+        if (seq >= C::STAGES && !mbar_wait(&wempty[s], ph ^ 1, g, 33)) return false;
+        uint8_t* st = W + s * C::STAGE;
+        if (g2) {
+          mbar_arrive_expect_tx(&wfull[s], C::G2_STAGE);
+          tma_load_3d(st, &w2_hi, &wfull[s], c * C::HC, 0, 0);
+          if constexpr (kStrict) tma_load_3d(st + R::ATOM_BYTES, &w2_lo, &wfull[s], c * C::HC, 0, 0);
+        } else {
+          mbar_arrive_expect_tx(&wfull[s], C::G1_STAGE);
+          tma_load_3d(st, &w1_hi, &wfull[s], atom * R::KATOM, c * C::G1N, 0);
+          if constexpr (kStrict)
+            tma_load_3d(st + C::G1N * 128, &w1_lo, &wfull[s], atom * R::KATOM, c * C::G1N, 0);
+        }
+        ++seq;
+        return true;
+      };
+      for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, 0, a);
+      for (int c = 0; c < C::NCH && ok; ++c) {
+        if (c + 1 < C::NCH)
+          for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, c + 1, a);
+        if (ok) ok = push(true, c, 0);
+      }
+      if (g.aborted()) {
+        for (int q = (seq > C::STAGES ? seq - C::STAGES : 0); q < seq; ++q)
+          (void)mbar_wait(&wfull[q % C::STAGES], (q / C::STAGES) & 1, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  } else {
+    if (lane == 0) {
+      const uint32_t id1 = kStrict ? idesc_tf32(128, C::G1N) : idesc_bf16(128, C::G1N);
+      const uint32_t id2 = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
+      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + R::A_SPLIT_BYTES);
+      const uint32_t h_hi = smem_u32(H), h_lo = smem_u32(H + R::ATOM_BYTES);
+      int seq = 0;
+      auto take = [&]() -> uint32_t {
+        const int s = seq % C::STAGES;
+        if (!mbar_wait(&wfull[s], (seq / C::STAGES) & 1, g, 34)) return 0;
+        tc_fence_after();
+        return smem_u32(W + s * C::STAGE);
+      };
+      auto release = [&]() {
+        umma_commit(&wempty[seq % C::STAGES]);
+        ++seq;
+      };
+      auto gemm1 = [&](int c) -> bool {
+        const int b = c & 1;
+        if (c >= 2 && !mbar_wait(&g1_free[b], ((c - 2) >> 1) & 1, g, 35)) return false;
+        tc_fence_after();
+        for (int a = 0; a < R::NKA; ++a) {
+          const uint32_t w = take();
+          if (!w) return false;
+          mma_k_atom<kStrict>(tmem + b * C::G1N, a_hi + a * R::ATOM_BYTES,
+                              a_lo + a * R::ATOM_BYTES, w, w + C::G1N * 128, id1, a == 0);
+          release();
+        }
+        umma_commit(&g1_full[b]);
+        return true;
+      };
+      bool ok = mbar_wait(a_full, 0, g, 36);
+      if (ok) tc_fence_after();
+      if (ok) ok = gemm1(0);
+      for (int c = 0; c < C::NCH && ok; ++c) {
+        if (c + 1 < C::NCH && !(ok = gemm1(c + 1))) break;
+        if (!mbar_wait(h_full, c & 1, g, 37)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t w = take();
+        if (!w) {
+          ok = false;
+          break;
+        }
+        mma_k_atom<kStrict>(tmem + kAcc, h_hi, h_lo, w, w + R::ATOM_BYTES, id2, c == 0);
+        release();
+        umma_commit(h_free);
+      }
+      if (ok) {
+        umma_commit(done);
+      } else {
+        umma_commit(drain);
+        (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Pack [Wa; Wb] chunk-interleaved: chunk c = rows Wa[c*HC..), Wb[c*HC..).
+__global__ void pack_transition_w1(const float* __restrict__ wa, const float* __restrict__ wb,
+                                   int hc, void* hi, void* lo, int strict) {
+  const int total = 1024 * 128;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int row = i / 128, k = i % 128;
+    const int c = row / (2 * hc), r = row % (2 * hc);
+    const float v = r < hc ? wa[(c * hc + r) * 128 + k] : wb[(c * hc + r - hc) * 128 + k];
+    if (strict) {
+      float h, l;
+      split_tf32(v, h, l);
+      static_cast<float*>(hi)[i] = h;
+      static_cast<float*>(lo)[i] = l;
+    } else {
+      static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+__global__ void pack_plain(const float* __restrict__ w, int count, void* hi, void* lo, int strict) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+    const float v = w[i];
+    if (strict) {
+      float h, l;
+      split_tf32(v, h, l);
+      static_cast<float*>(hi)[i] = h;
+      static_cast<float*>(lo)[i] = l;
+    } else {
+      static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+template <class Alloc>
+struct TransPlan {
+  void *w1_hi = nullptr, *w1_lo = nullptr, *w2_hi = nullptr, *w2_lo = nullptr;
+  void plan(Alloc& al, bool strict) {
+    auto take = [&](size_t c) -> void* {
+      return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
+    };
+    w1_hi = take(1024 * 128);
+    if (strict) w1_lo = take(1024 * 128);
+    w2_hi = take(128 * 512);
+    if (strict) w2_lo = take(128 * 512);
+  }
+};
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" size_t fpb_transition_workspace_size(int c_z, int expansion, int precision) {
+  if (c_z != 128 || expansion != 4 || (precision != 0 && precision != 1)) return 0;
+  WsCounter cnt;
+  TransPlan<WsCounter> pl;
+  pl.plan(cnt, precision == 0);
+  return cnt.used;
+}
+
+extern "C" int fpb_transition(float* z, long long rows, int c_z, int expansion, const float* ln_w,
+                              const float* ln_b, const float* w_a, const float* w_b,
+                              const float* w_out, float eps, int precision, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream) {
+  if (!z || !ln_w || !ln_b || !w_a || !w_b || !w_out || !workspace) return kErrArg;
+  if (c_z != 128 || expansion != 4 || rows <= 0) return kErrShape;
+  if (rows > 0x7fffffffll) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
+    return kErrAlign;
+  if (workspace_bytes < fpb_transition_workspace_size(c_z, expansion, precision))
+    return kErrWorkspace;
+  const bool strict = precision == 0;
+  WsCursor cur(workspace, workspace_bytes);
+  TransPlan<WsCursor> pl;
+  pl.plan(cur, strict);
+  if (!cur.ok) return kErrWorkspace;
+  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  const int hc = strict ? TransCfg<true>::HC : TransCfg<false>::HC;
+  pack_transition_w1<<<128, 256, 0, stream>>>(w_a, w_b, hc, pl.w1_hi, pl.w1_lo, strict ? 1 : 0);
+  pack_plain<<<64, 256, 0, stream>>>(w_out, 128 * 512, pl.w2_hi, pl.w2_lo, strict ? 1 : 0);
+  int st;
+  if ((st = launch_status())) return st;
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap m1h, m1l, m2h, m2l;
+  bool ok = make_map_3d(&m1h, pl.w1_hi, dt, 128, 1024, 1, 128ull * esz, 128ull * esz * 1024,
+                        128 / esz, 2 * hc, 1) &&
+            make_map_3d(&m2h, pl.w2_hi, dt, 512, 128, 1, 512ull * esz, 512ull * esz * 128,
+                        128 / esz, 128, 1);
+  if (strict)
+    ok = ok &&
+         make_map_3d(&m1l, pl.w1_lo, dt, 128, 1024, 1, 128ull * esz, 128ull * esz * 1024,
+                     128 / esz, 2 * hc, 1) &&
+         make_map_3d(&m2l, pl.w2_lo, dt, 512, 128, 1, 512ull * esz, 512ull * esz * 128, 128 / esz,
+                     128, 1);
+  else {
+    m1l = m1h;
+    m2l = m2h;
+  }
+  if (!ok) return kErrArg;
+  TransArgs ta{z, (int)rows, eps, ln_w, ln_b, static_cast<int*>(workspace)};
+  const unsigned tiles = (unsigned)((rows + 127) / 128);
+  if (strict) {
+    auto k = transition_kernel<true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
+    k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+  } else {
+    auto k = transition_kernel<false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
+    k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+  }
+  return launch_status();
+}

@@ -144,3 +144,26 @@ def triattn(z: torch.Tensor, mask, w: dict, *, starting: bool = True, precision=
                                *ptrs, float(eps), int(bool(starting)), p, ws.data_ptr(),
                                ws.numel(), _stream_ptr(z.device)), "fpb_triattn")
     return (z, ws) if return_workspace else z
+
+
+def transition(z: torch.Tensor, w: dict, *, precision="strict", eps: float = 1e-5,
+               return_workspace: bool = False):
+    """Pair transition update added in place to ``z`` ``[..., 128]``; ``w``
+    holds ``ln_w, ln_b, w_a, w_b, w_out`` (4x expansion). Returns ``z``."""
+    _require_cuda(z)
+    if z.dtype != torch.float32 or z.shape[-1] != 128:
+        raise RuntimeError("transition takes float32 [..., 128] rows")
+    if not z.is_contiguous() or z.data_ptr() % 16:
+        raise RuntimeError("transition needs a contiguous, 16-byte aligned z")
+    ts = [_f32(w[k], k) for k in ("ln_w", "ln_b", "w_a", "w_b", "w_out")]
+    _require_cuda(*ts)
+    if tuple(ts[2].shape) != (512, 128) or tuple(ts[4].shape) != (128, 512):
+        raise RuntimeError("transition supports c=128 with 4x expansion")
+    lib = _lib.load()
+    p = precision_code(precision)
+    ws = workspace(lib.fpb_transition_workspace_size(128, 4, p), z.device)
+    rows = z.numel() // 128
+    _lib.check(lib.fpb_transition(z.data_ptr(), rows, 128, 4, *[t.data_ptr() for t in ts],
+                                  float(eps), p, ws.data_ptr(), ws.numel(),
+                                  _stream_ptr(z.device)), "fpb_transition")
+    return (z, ws) if return_workspace else z

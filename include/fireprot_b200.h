@@ -91,6 +91,18 @@ int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head
                 const float* w_o, const float* b_o, float eps, int starting, int precision,
                 void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Pair transition, residual added in place on `rows` rows of 128 channels:
+ *   z <- z + (silu(LN(z) Wa^T) * (LN(z) Wb^T)) Wout^T
+ * expansion = 4: w_a, w_b [512,128], w_out [128,512], bias-free.
+ * Replaces dispatch_transition / _hip_transition
+ * (python/fireprot/backends/amd/recycle.py:203-227,360) and the
+ * project_transition kernel (kernels/amd/fireprot_amd_ops.cu:1106-1183). */
+size_t fpb_transition_workspace_size(int c_z, int expansion, int precision);
+int fpb_transition(float* z, long long rows, int c_z, int expansion, const float* ln_w,
+                   const float* ln_b, const float* w_a, const float* w_b, const float* w_out,
+                   float eps, int precision, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

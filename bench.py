@@ -1,0 +1,398 @@
+#!/usr/bin/env python
+"""Pairformer pair-block throughput on B200 (blocks/s at N=1536).
+
+One step = the pair stack of one Pairformer block (TriMul out, TriMul in,
+TriAttn start, TriAttn end, pair transition) on a synthetic pair tensor of
+BASELINE config 3's shape: N=1536, c_z=128, padding mask with valid length
+1480, seeded N(0,1) inputs and random-init N(0, 1/fan_in) weights. Consecutive
+steps chain (step k+1 runs on step k's output), i.e. a K-block stack.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--precision strict|fast]
+  python bench.py --impl reference ...   # the native math on host CPU cores
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own independent
+pair stack (data-parallel replicas, weak scaling); device time is the max over
+ranks and ``value`` is the total blocks/s of all ranks.
+
+Printed on rank 0: one JSON line (see ``_result``) with device-timed
+``value``, end-to-end ``e2e`` (host buffers, copies inside the timed region),
+per-kernel device times measured live with CUDA events, the roofline of the
+dominant kernel, the CPU baseline and the SM clocks sampled during the timed
+region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Pairformer blocks/s at N=1536 (strict/fast) at 1/2/4/8 B200; % TC roofline"
+C = 128
+
+
+def block_flops(n: int) -> float:
+    """Algorithmic FLOPs of one pair block: 1536 N^3 + 1,116,160 N^2."""
+    return 1536.0 * n ** 3 + 1_116_160.0 * n ** 2
+
+
+def kernel_flops(name: str, n: int) -> float:
+    """Algorithmic FLOPs of ONE launch of each library kernel at size n."""
+    n2 = float(n) * n
+    return {
+        "contract_strict": 2.0 * n ** 3 * C,
+        "contract_fast": 2.0 * n ** 3 * C,
+        "trimul_proj": 2.0 * n2 * C * 4 * C,
+        "trimul_out": 2.0 * n2 * C * 2 * C,
+        "triattn_proj": 2.0 * n2 * C * (3 * C + 4),
+        "triattn_core": 4.0 * n ** 3 * C,
+        "triattn_out": 2.0 * n2 * C * 2 * C,
+        "transition": 2.0 * n2 * (C * 8 * C + 4 * C * C),
+    }.get(name, 0.0)
+
+
+def peaks(precision: str):
+    """Tensor peak (TFLOP/s) and HBM (GB/s) used as roofline denominators."""
+    src = "MEASURED_PEAKS.json"
+    try:
+        mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        bf16, hbm = float(mp["bf16_tflops"]), float(mp["hbm_gbs"])
+    except Exception:
+        bf16, hbm, src = 1590.0, 6650.0, "fallback"
+    if precision == "strict":
+        # tf32 = bf16 / 2 (not measured); 3xTF32 issues three tf32 MMAs per product
+        return bf16 / 6.0, hbm, f"{src} bf16 {bf16} / 2 (tf32) / 3 (3xTF32), of measured"
+    return bf16, hbm, f"{src} bf16 {bf16}, of measured"
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"fpb_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sms, maxs, reasons, power = [], [], set(), []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            # bus ids differ in domain width between torch and nvidia-smi
+            if self.bus_id and f[1].lower()[-7:] != self.bus_id[-7:]:
+                continue
+            try:
+                sms.append(float(f[2]))
+                maxs.append(float(f[3]))
+                power.append(float(f[4]))
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                  "sw_power_cap"), f[6:10]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(maxs) if maxs else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sms), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# distributed helpers
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the native math on host cores (oracle port)
+# ---------------------------------------------------------------------------
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    from oracle.cpu_baseline import sampled_block_seconds
+    secs = []
+    sample = threads = None
+    for i in range(args.warmup + args.steps):
+        tot, _, sample, threads = sampled_block_seconds(args.n, args.valid, row_sample=8,
+                                                        chan_sample=4, seed=i)
+        if i >= args.warmup:
+            secs.append(tot)
+    mean = statistics.mean(secs)
+    value = 1.0 / mean
+    return {
+        "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": _config(args),
+        "cpu_baseline": {"value": value, "unit": "blocks/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "blocks/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def _config(args):
+    return {"workload": (f"pair stack of one Pairformer block (TriMul out/in, TriAttn start/end, "
+                         f"pair transition), N={args.n}, c_z=128, H=4, d=32, {args.precision} "
+                         f"precision, padding mask valid {args.valid}"),
+            "n": args.n, "c_z": C, "precision": args.precision, "valid_length": args.valid,
+            "l2": "inputs larger than L2 (z alone is %.2f GB)" % (args.n ** 2 * C * 4 / 1e9),
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    from fireprot_b200 import ops
+    from fireprot_b200.modules import PairformerPairBlock
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = args.n
+    gen = torch.Generator().manual_seed(1000 + rank)
+    z_host = torch.randn(n, n, C, generator=gen).pin_memory()
+    valid = torch.arange(n) < args.valid
+    mask_host = (valid[:, None] & valid[None, :]).float().pin_memory()
+    block = PairformerPairBlock().init_random_(seed=1 + rank).to(dev)
+    cw = block.c_weights()
+    z = z_host.to(dev)
+    mask = mask_host.to(dev)
+    ws = ops.pair_block_workspace(n, args.precision, True, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(zz):
+        ops.pair_block(zz, mask, cw, precision=args.precision, workspace=ws)
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        step(z)
+    torch.cuda.synchronize(dev)
+    st = ops.workspace_status(ws)
+    if st != 0:
+        raise RuntimeError(f"device status {st} after warm-up")
+
+    # ---- timed region: K chained blocks, inputs resident in HBM
+    bus = None
+    try:
+        props = torch.cuda.get_device_properties(dev)
+        # nvidia-smi prints "DDDDDDDD:BB:DD.F"; match on "bb:dd.f"
+        bus = "%02x:%02x.0" % (int(props.pci_bus_id), int(props.pci_device_id))
+    except Exception:
+        bus = None
+    clocks = ClockSampler(bus)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    time.sleep(0.3)
+    ops.timing_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(z)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    kernels = ops.timing_collect()
+    ops.timing_enable(False)
+    clk = clocks.stop()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world, dev)
+    ms_per_step = ms_max / args.steps
+    value = world * args.steps / (ms_max / 1e3)
+    if not torch.isfinite(z).all():
+        raise RuntimeError("non-finite pair tensor after the timed steps")
+
+    # ---- end to end: pinned host z in, result out, through the public API
+    e2e_steps = max(1, args.e2e_steps)
+    out_host = torch.empty_like(z_host).pin_memory()
+    zz = torch.empty_like(z)
+    mm = torch.empty_like(mask)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        zz.copy_(z_host, non_blocking=True)
+        mm.copy_(mask_host, non_blocking=True)
+        step(zz)
+        out_host.copy_(zz, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world, dev)
+    e2e_value = world * e2e_steps / (e2e_ms / 1e3)
+    h2d = z_host.numel() * 4 + mask_host.numel() * 4
+    d2h = out_host.numel() * 4
+
+    # ---- fast-mode side measurement (strict is the headline)
+    side = None
+    if args.precision == "strict" and not args.no_side:
+        ws_f = ops.pair_block_workspace(n, "fast", True, dev)
+        zf = z_host.to(dev)
+        for _ in range(2):
+            ops.pair_block(zf, mask, cw, precision="fast", workspace=ws_f)
+        torch.cuda.synchronize(dev)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            ops.pair_block(zf, mask, cw, precision="fast", workspace=ws_f)
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        fms = max_over_ranks(g0.elapsed_time(g1), world, dev) / args.steps
+        pf, _, _ = peaks("fast")
+        side = {"precision": "fast", "value": world * 1e3 / fms, "unit": "blocks/s",
+                "ms_per_step": fms,
+                "tc_frac_block": block_flops(n) / (fms / 1e3) / 1e12 / pf}
+        del ws_f, zf
+
+    if rank != 0:
+        return None
+
+    # ---- roofline of the dominant kernel (live CUDA-event durations)
+    peak_tc, peak_hbm, peak_src = peaks(args.precision)
+    per_kernel = {}
+    for name, rec in kernels.items():
+        avg = rec["total_ms"] / rec["launches"]
+        fl = kernel_flops(name, n)
+        per_kernel[name] = {"launches": rec["launches"], "avg_ms": round(avg, 4),
+                            "share": round(rec["total_ms"] / max(1e-9, sum(
+                                r["total_ms"] for r in kernels.values())), 4),
+                            "tflops": round(fl / (avg / 1e3) / 1e12, 2) if fl else None}
+    dom = max(kernels, key=lambda k: kernels[k]["total_ms"])
+    dom_avg_s = kernels[dom]["total_ms"] / kernels[dom]["launches"] / 1e3
+    achieved = kernel_flops(dom, n) / dom_avg_s / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get(f"{dom}:{args.precision}:{n}")
+        except Exception:
+            traffic = None
+    launches = sum(r["launches"] for r in kernels.values())
+
+    # ---- CPU baseline (rank 0, N=1 only): bounded sample of the same workload
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        from oracle.cpu_baseline import sampled_block_seconds
+        tot, parts, sample, threads = sampled_block_seconds(n, args.valid, row_sample=8,
+                                                            chan_sample=4)
+        cpu = {"value": 1.0 / tot, "unit": "blocks/s", "cores": threads, "kind": "port",
+               "sample": sample, "seconds_per_block": round(tot, 2),
+               "breakdown_s": {k: round(v, 2) for k, v in parts.items()}}
+
+    return {
+        "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (3xTF32 tensor cores)" if args.precision == "strict" else "bf16 (f32 acc)",
+        "data": "synthetic (seeded N(0,1) pair tensor, random-init weights)",
+        "config": _config(args),
+        "tc_frac_block": block_flops(n) / (ms_per_step / 1e3) / 1e12 / peak_tc,
+        "e2e": {"value": e2e_value, "unit": "blocks/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak_tc,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tc, "traffic": traffic,
+                     "peak_source": peak_src},
+        "kernels": per_kernel,
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "side": side,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["strict", "fast"], default="strict")
+    ap.add_argument("--n", type=int, default=1536)
+    ap.add_argument("--valid", type=int, default=1480)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if world > 1 and args.gpus != world:
+        args.gpus = world
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, world, rank)
+        else:
+            res = run_ours(args, world, rank, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

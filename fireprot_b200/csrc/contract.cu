@@ -241,17 +241,17 @@ int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaSt
     auto k = contract_kernel<true, float>;
     const int smem = ContractCfg<true>::SMEM_BYTES;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args);
+    FPB_LAUNCH("contract_strict", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
   } else {
     const int smem = ContractCfg<false>::SMEM_BYTES;
     if (args.out_bf16) {
       auto k = contract_kernel<false, __nv_bfloat16>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args);
+      FPB_LAUNCH("contract_fast", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
     } else {
       auto k = contract_kernel<false, float>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args);
+      FPB_LAUNCH("contract_fast", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
     }
   }
   return launch_status();
@@ -353,14 +353,18 @@ extern "C" int fpb_packed_bmm(const float* a, const float* b, float* out, int ba
   const int tr = outgoing ? 0 : 1;
   dim3 pg((n + 31) / 32, (n + 31) / 32, batch), pb(32, 8);
   if (strict) {
-    prep_operand_kernel<true><<<pg, pb, 0, stream>>>(a, n, tr, a_hi, a_lo, ld, cs);
-    prep_operand_kernel<true><<<pg, pb, 0, stream>>>(b, n, tr, b_hi, b_lo, ld, cs);
+    FPB_LAUNCH("prep_operand", stream,
+               prep_operand_kernel<true><<<pg, pb, 0, stream>>>(a, n, tr, a_hi, a_lo, ld, cs));
+    FPB_LAUNCH("prep_operand", stream,
+               prep_operand_kernel<true><<<pg, pb, 0, stream>>>(b, n, tr, b_hi, b_lo, ld, cs));
   } else {
-    prep_operand_kernel<false><<<pg, pb, 0, stream>>>(a, n, tr, a_hi, nullptr, ld, cs);
-    prep_operand_kernel<false><<<pg, pb, 0, stream>>>(b, n, tr, b_hi, nullptr, ld, cs);
+    FPB_LAUNCH("prep_operand", stream,
+               prep_operand_kernel<false><<<pg, pb, 0, stream>>>(a, n, tr, a_hi, nullptr, ld, cs));
+    FPB_LAUNCH("prep_operand", stream,
+               prep_operand_kernel<false><<<pg, pb, 0, stream>>>(b, n, tr, b_hi, nullptr, ld, cs));
   }
   if (cudaGetLastError() != cudaSuccess) return kErrCuda;
-  cudaMemsetAsync(workspace, 0, kWsHeader, stream);
+  if (reset_status(workspace, stream)) return kErrCuda;
   ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, cs, batch, strict};
   ContractArgs args{};
   args.n = n;

@@ -29,6 +29,26 @@ struct ContractArgs {
 
 int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream);
 
+// Zero the workspace status word at the start of a public call, unless the
+// call runs inside a composite call (fpb_pair_block) that owns the word.
+int reset_status(void* workspace, cudaStream_t stream);
+struct CompositeCall {
+  CompositeCall();
+  ~CompositeCall();
+};
+
+// Launch timing (timing.cu): bracket a kernel launch with CUDA events when
+// timing is enabled on this thread.
+int timing_begin(cudaStream_t s);
+void timing_end(int idx, cudaStream_t s, const char* name);
+
+#define FPB_LAUNCH(name, stream, ...)                  \
+  do {                                                 \
+    const int fpb_t_ = ::fpb::timing_begin(stream);    \
+    __VA_ARGS__;                                       \
+    ::fpb::timing_end(fpb_t_, stream, name);           \
+  } while (0)
+
 // Concatenate up to 4 [rows_each][128] FP32 weight matrices and split them
 // into tf32 hi/lo (strict) or convert them to BF16 (fast).
 struct PackSrc {

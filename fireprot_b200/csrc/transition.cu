@@ -373,10 +373,14 @@ extern "C" int fpb_transition(float* z, long long rows, int c_z, int expansion, 
   TransPlan<WsCursor> pl;
   pl.plan(cur, strict);
   if (!cur.ok) return kErrWorkspace;
-  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  if (reset_status(workspace, stream)) return kErrCuda;
   const int hc = strict ? TransCfg<true>::HC : TransCfg<false>::HC;
-  pack_transition_w1<<<128, 256, 0, stream>>>(w_a, w_b, hc, pl.w1_hi, pl.w1_lo, strict ? 1 : 0);
-  pack_plain<<<64, 256, 0, stream>>>(w_out, 128 * 512, pl.w2_hi, pl.w2_lo, strict ? 1 : 0);
+  FPB_LAUNCH("pack_weights", stream,
+             pack_transition_w1<<<128, 256, 0, stream>>>(w_a, w_b, hc, pl.w1_hi, pl.w1_lo,
+                                                         strict ? 1 : 0));
+  FPB_LAUNCH("pack_weights", stream,
+             pack_plain<<<64, 256, 0, stream>>>(w_out, 128 * 512, pl.w2_hi, pl.w2_lo,
+                                                strict ? 1 : 0));
   int st;
   if ((st = launch_status())) return st;
   const int esz = strict ? 4 : 2;
@@ -403,11 +407,13 @@ extern "C" int fpb_transition(float* z, long long rows, int c_z, int expansion, 
   if (strict) {
     auto k = transition_kernel<true>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
-    k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+    FPB_LAUNCH("transition", stream,
+               k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   } else {
     auto k = transition_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
-    k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+    FPB_LAUNCH("transition", stream,
+               k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   }
   return launch_status();
 }

@@ -937,7 +937,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
   pl.plan(cur, n, strict, with_mask);
   if (!cur.ok) return kErrWorkspace;
   int* status = static_cast<int*>(workspace);
-  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  if (reset_status(workspace, stream)) return kErrCuda;
   int st;
   if ((st = pack_weights(PackSrc{{w_q, w_k, w_v, nullptr}, 3, 128}, pl.wp_hi, pl.wp_lo, strict,
                          stream)))
@@ -962,7 +962,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
                     : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<tiles, 192, smem, stream>>>(mph, mpl, pa);
+    FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
     if ((st = launch_status())) return st;
   }
   // 2. attention core
@@ -994,11 +994,13 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     if (strict) {
       auto k = attn_core_kernel<true>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
-      k<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca);
+      FPB_LAUNCH("triattn_core", stream,
+                 k<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
     } else {
       auto k = attn_core_kernel<false>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
-      k<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca);
+      FPB_LAUNCH("triattn_core", stream,
+                 k<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
     }
     if ((st = launch_status())) return st;
   }
@@ -1009,7 +1011,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
                     : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<tiles, 192, smem, stream>>>(moh, mol, oa);
+    FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
     if ((st = launch_status())) return st;
   }
   return kOk;

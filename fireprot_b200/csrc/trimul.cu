@@ -445,7 +445,8 @@ __global__ void pack_weights_kernel(PackSrc src, void* hi, void* lo, int strict)
 }
 
 int pack_weights(const PackSrc& src, void* hi, void* lo, bool strict, cudaStream_t stream) {
-  pack_weights_kernel<<<64, 256, 0, stream>>>(src, hi, lo, strict ? 1 : 0);
+  FPB_LAUNCH("pack_weights", stream,
+             pack_weights_kernel<<<64, 256, 0, stream>>>(src, hi, lo, strict ? 1 : 0));
   return launch_status();
 }
 
@@ -524,7 +525,7 @@ extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const flo
   pl.plan(cur, n, strict);
   if (!cur.ok) return kErrWorkspace;
   int* status = static_cast<int*>(workspace);
-  if (cudaMemsetAsync(workspace, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  if (reset_status(workspace, stream)) return kErrCuda;
 
   int st = pack_weights(PackSrc{{w_a_p, w_a_g, w_b_p, w_b_g}, 4, 128}, pl.wp_hi, pl.wp_lo, strict,
                         stream);
@@ -547,7 +548,7 @@ extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const flo
                     : (outgoing ? trimul_proj_kernel<false, false>
                                 : trimul_proj_kernel<false, true>);
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<tiles, 192, smem, stream>>>(mph, mpl, pa);
+    FPB_LAUNCH("trimul_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
     if ((st = launch_status())) return st;
   }
   ContractOperands op{pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo, pl.ld, pl.cs, 128, strict};
@@ -565,7 +566,7 @@ extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const flo
     const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
     auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<tiles, 192, smem, stream>>>(moh, mol, oa);
+    FPB_LAUNCH("trimul_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
     if ((st = launch_status())) return st;
   }
   return kOk;

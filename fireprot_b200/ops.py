@@ -7,6 +7,8 @@ fallback in this package.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -167,3 +169,50 @@ def transition(z: torch.Tensor, w: dict, *, precision="strict", eps: float = 1e-
                                   float(eps), p, ws.data_ptr(), ws.numel(),
                                   _stream_ptr(z.device)), "fpb_transition")
     return (z, ws) if return_workspace else z
+
+
+def pair_block_workspace(n: int, precision, with_mask: bool, device) -> torch.Tensor:
+    lib = _lib.load()
+    nbytes = lib.fpb_pair_block_workspace_size(n, precision_code(precision), int(with_mask))
+    if nbytes == 0:
+        raise RuntimeError(f"unsupported pair block size n={n}")
+    return workspace(nbytes, device)
+
+
+def pair_block(z: torch.Tensor, mask, c_weights, *, precision="strict", eps: float = 1e-5,
+               workspace=None, return_workspace: bool = False):
+    """Pair stack of one Pairformer block in place on ``z`` ``[n, n, 128]``.
+
+    ``c_weights`` is a ``modules.PairBlockWeights`` ctypes struct (see
+    ``PairformerPairBlock.c_weights``). ``workspace`` may be passed to reuse
+    one allocation across blocks.
+    """
+    _require_cuda(z, mask)
+    if z.dtype != torch.float32 or z.ndim != 3 or z.shape[0] != z.shape[1] or z.shape[2] != 128:
+        raise RuntimeError("pair_block takes a float32 [n, n, 128] pair tensor")
+    if not z.is_contiguous() or z.data_ptr() % 16:
+        raise RuntimeError("pair_block needs a contiguous, 16-byte aligned z")
+    n = z.shape[0]
+    if mask is not None:
+        if tuple(mask.shape) != (n, n) or mask.dtype != torch.float32 or not mask.is_contiguous():
+            raise RuntimeError("mask must be a contiguous float32 [n, n] tensor")
+    lib = _lib.load()
+    p = precision_code(precision)
+    ws = workspace if workspace is not None else pair_block_workspace(n, p, mask is not None,
+                                                                      z.device)
+    _lib.check(lib.fpb_pair_block(z.data_ptr(), 0 if mask is None else mask.data_ptr(), n,
+                                  ctypes.byref(c_weights), float(eps), p, ws.data_ptr(),
+                                  ws.numel(), _stream_ptr(z.device)), "fpb_pair_block")
+    return (z, ws) if return_workspace else z
+
+
+def timing_enable(on: bool = True) -> None:
+    _lib.load().fpb_timing_enable(int(bool(on)))
+
+
+def timing_collect() -> dict:
+    """Per-kernel launches and total device milliseconds since timing_enable."""
+    import json
+    buf = ctypes.create_string_buffer(1 << 16)
+    _lib.check(_lib.load().fpb_timing_collect(buf, len(buf)), "fpb_timing_collect")
+    return json.loads(buf.value.decode())

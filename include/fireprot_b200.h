@@ -103,6 +103,39 @@ int fpb_transition(float* z, long long rows, int c_z, int expansion, const float
                    float eps, int precision, void* workspace, size_t workspace_bytes,
                    cudaStream_t stream);
 
+/* Weights of the five pair operators of one block (torch Linear layouts). */
+typedef struct {
+  const float *ln_in_w, *ln_in_b, *w_a_p, *w_a_g, *w_b_p, *w_b_g, *w_g, *ln_out_w, *ln_out_b,
+      *w_z;
+} fpb_trimul_weights;
+typedef struct {
+  const float *ln_w, *ln_b, *w_q, *w_k, *w_v, *w_bias, *w_g, *b_g, *w_o, *b_o;
+} fpb_triattn_weights;
+typedef struct {
+  const float *ln_w, *ln_b, *w_a, *w_b, *w_out;
+} fpb_transition_weights;
+typedef struct {
+  fpb_trimul_weights tri_mul_out, tri_mul_in;
+  fpb_triattn_weights tri_att_start, tri_att_end;
+  fpb_transition_weights transition;
+} fpb_pair_block_weights;
+
+/* Pair stack of one Pairformer block, in place on z [n, n, 128]:
+ * TriMul outgoing, TriMul incoming, TriAttn starting node, TriAttn ending
+ * node, pair transition, each z += update (Protenix PairformerBlock with the
+ * fireprot kernels, patches/protenix/0006-...patch:14-37). One workspace and
+ * one status word for the whole block. */
+size_t fpb_pair_block_workspace_size(int n, int precision, int with_mask);
+int fpb_pair_block(float* z, const float* mask, int n, const fpb_pair_block_weights* weights,
+                   float eps, int precision, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream);
+
+/* Per-launch device timing on the calling thread (CUDA events around every
+ * kernel launch of this library). fpb_timing_collect synchronises and writes
+ * {"kernel": {"launches": L, "total_ms": T}, ...} as JSON. */
+int fpb_timing_enable(int on);
+int fpb_timing_collect(char* out, size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

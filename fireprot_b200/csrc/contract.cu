@@ -154,14 +154,21 @@ __global__ void __launch_bounds__(192, 1)
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
       const int row = it * C::BM + q * 32 + lane;
-      OutT* out = reinterpret_cast<OutT*>(args.out) + (size_t)ch * args.out_channel_stride +
-                  (size_t)row * args.ldo;
 #pragma unroll 1
       for (int cb = 0; cb < C::BN / 32; ++cb) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cb * 32, r);
         tmem_ld_wait();
         const int col0 = jt * C::BN + cb * 32;
+        // `out` points at column 0 of this (channel, row) run, so that
+        // out + col0 addresses columns col0..col0+31 in either layout
+        OutT* out;
+        if (args.blocked)
+          out = reinterpret_cast<OutT*>(args.out) +
+                ((((size_t)row * args.njb + (col0 >> 7)) * 128 + ch) << 7) + (col0 & 127) - col0;
+        else
+          out = reinterpret_cast<OutT*>(args.out) + (size_t)ch * args.out_channel_stride +
+                (size_t)row * args.ldo;
         if (row < n && col0 < n) {
           const bool vec = (col0 + 32 <= n) &&
                            ((reinterpret_cast<uintptr_t>(out + col0) & 15u) == 0u);

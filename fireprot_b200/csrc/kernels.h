@@ -20,11 +20,16 @@ struct ContractOperands {
 
 struct ContractArgs {
   int n;
-  void* out;                  // [channels][n][ldo] fp32 or bf16
+  void* out;                  // [channels][n][ldo] fp32 or bf16 (plain layout)
   int ldo;
   size_t out_channel_stride;  // elements
   int out_bf16;
   int* status;
+  // blocked layout (when blocked != 0): out[i][j / 128][c][j % 128] with
+  // njb = ceil(n / 128) column blocks; one pair-row tile of the output
+  // kernel (128 columns x 128 channels) is then one contiguous block.
+  int blocked;
+  int njb;
 };
 
 int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream);

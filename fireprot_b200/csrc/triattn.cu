@@ -281,7 +281,9 @@ struct AttnCoreArgs {
 template <bool kStrict>
 struct AttnCfg {
   static constexpr int BQ = 128;
-  static constexpr int BKV = 64;
+  // key tile: one 128-byte atom of P per tile (32 fp32 keys in strict mode,
+  // 64 bf16 keys in fast mode); small enough for two CTAs per SM
+  static constexpr int BKV = kStrict ? 32 : 64;
   static constexpr int ESZ = kStrict ? 4 : 2;
   static constexpr int NSPLIT = kStrict ? 2 : 1;
   static constexpr int QK_ROW = 32 * ESZ;                 // bytes per q/k row (128 / 64)
@@ -294,8 +296,10 @@ struct AttnCfg {
   static constexpr int KV_STAGES = kStrict ? 2 : 3;
   static constexpr int P_ATOMS = BKV / V_ATOM_KEYS;       // K atoms of P
   static constexpr int P_BYTES = P_ATOMS * BQ * 128;      // per split
-  static constexpr int SMEM =
-      tmem_safe_smem(NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + NSPLIT * P_BYTES + 1024 + 256, 256);
+  // TMEM: S double buffer (2 x BKV columns) + P V (32 columns)
+  static constexpr int TMEM_COLS = (2 * BKV + 32) <= 128 ? 128 : 256;
+  static constexpr int SMEM = tmem_safe_smem(
+      NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + NSPLIT * P_BYTES + 1024 + 256, TMEM_COLS);
 };
 
 template <bool kStrict>
@@ -307,7 +311,7 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
 }
 
 template <bool kStrict>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
                      const __grid_constant__ CUtensorMap mq_lo,
                      const __grid_constant__ CUtensorMap mk_hi,
@@ -338,8 +342,8 @@ __global__ void __launch_bounds__(192, 1)
   const int jt = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int ih = i * kHeads + h;
   const int nt = (n + C::BKV - 1) / C::BKV;
-  // TMEM columns: S[0] 0..63, S[1] 64..127, PV 128..159
-  constexpr uint32_t kS0 = 0, kPV = 128;
+  // TMEM columns: S[0] [0, BKV), S[1] [BKV, 2 BKV), P V [2 BKV, 2 BKV + 32)
+  constexpr uint32_t kS0 = 0, kPV = 2 * C::BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -494,54 +498,68 @@ __global__ void __launch_bounds__(192, 1)
     float o[32];
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] = 0.f;
+    // additive term of key tile t: mask bias + triangle bias, -inf past n.
+    // Adding (mask + bias) to q.k equals the reference's (q.k + mask) + bias
+    // for 0/1 masks: -1e9 absorbs any |x| < 32 in FP32 either way.
+    auto load_add = [&](int t, float (&cv)[C::BKV]) {
+      const int k0 = t * C::BKV;
+#pragma unroll
+      for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
+        const int k = k0 + 4 * e4;
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), mb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k + 4 <= n) {
+          if (jvalid) bb = __ldg(reinterpret_cast<const float4*>(brow + k));
+          if (mrow) mb = __ldg(reinterpret_cast<const float4*>(mrow + k));
+          cv[4 * e4] = mb.x + bb.x;
+          cv[4 * e4 + 1] = mb.y + bb.y;
+          cv[4 * e4 + 2] = mb.z + bb.z;
+          cv[4 * e4 + 3] = mb.w + bb.w;
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float v = -INFINITY;
+            if (k + u < n) v = (mrow ? mrow[k + u] : 0.f) + (jvalid ? brow[k + u] : 0.f);
+            cv[4 * e4 + u] = v;
+          }
+        }
+      }
+    };
+    // strict (32-key tiles): the next tile's additive terms are prefetched
+    // into registers while the current tile is processed; fast (64-key
+    // tiles) loads them in place to stay within 168 registers.
+    constexpr bool kPrefetch = kStrict;
+    float cadd[kPrefetch ? C::BKV : 1];
+    if constexpr (kPrefetch) load_add(0, cadd);
     bool ok = true;
     for (int t = 0; t < nt && ok; ++t) {
       float sv[C::BKV];
+      if constexpr (!kPrefetch) load_add(t, sv);
       if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, g, 26)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      {
+#pragma unroll
+      for (int q = 0; q < C::BKV / 32; ++q) {
         float tmp[32];
-        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, 0, tmp);
+        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, q * 32, tmp);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) sv[e] = tmp[e];
-        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, 32, tmp);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) sv[32 + e] = tmp[e];
+        for (int e = 0; e < 32; ++e) {
+          if constexpr (kPrefetch)
+            sv[q * 32 + e] = tmp[e] + cadd[q * 32 + e];
+          else
+            sv[q * 32 + e] = tmp[e] + sv[q * 32 + e];
+        }
       }
       tc_fence_before();
       mbar_arrive(&s_free[t & 1]);
-      const int k0 = t * C::BKV;
+      // prefetch the next tile's additive terms while this tile is processed
+      if constexpr (kPrefetch) {
+        if (t + 1 < nt) load_add(t + 1, cadd);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
-        const int k = k0 + 4 * e4;
-        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), mb = make_float4(0.f, 0.f, 0.f, 0.f);
-        const bool full4 = (k + 4 <= n);
-        if (full4) {
-          if (jvalid) bb = __ldg(reinterpret_cast<const float4*>(brow + k));
-          if (mrow) mb = __ldg(reinterpret_cast<const float4*>(mrow + k));
-        } else {
-          float btmp[4] = {0.f, 0.f, 0.f, 0.f}, mtmp[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (k + u < n) {
-              if (jvalid) btmp[u] = brow[k + u];
-              if (mrow) mtmp[u] = mrow[k + u];
-            }
-          bb = make_float4(btmp[0], btmp[1], btmp[2], btmp[3]);
-          mb = make_float4(mtmp[0], mtmp[1], mtmp[2], mtmp[3]);
-        }
-        // reference order: (q.k + mask bias) + triangle bias
-        float* s4 = sv + 4 * e4;
-        s4[0] = (k + 0 < n) ? (s4[0] + mb.x) + bb.x : -INFINITY;
-        s4[1] = (k + 1 < n) ? (s4[1] + mb.y) + bb.y : -INFINITY;
-        s4[2] = (k + 2 < n) ? (s4[2] + mb.z) + bb.z : -INFINITY;
-        s4[3] = (k + 3 < n) ? (s4[3] + mb.w) + bb.w : -INFINITY;
-        mx = fmaxf(mx, fmaxf(fmaxf(s4[0], s4[1]), fmaxf(s4[2], s4[3])));
-      }
+      for (int e = 0; e < C::BKV; ++e) mx = fmaxf(mx, sv[e]);
       const float m_new = fmaxf(m_run, mx);
       const float alpha = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first tile
       float lsum = 0.f;
@@ -627,7 +645,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -741,69 +759,88 @@ __global__ void __launch_bounds__(192, 1)
       const long long r = pr / n, s = pr - r * n;
       zrow_idx = kTrans ? (s * n + r) : pr;
     }
-    // gate from GEMM 1, times o -> A2 (after GEMM 1 retired)
+    // attention output chunk cc (32 channels) of this thread's row
+    auto load_o = [&](int cc, float (&ov)[32]) {
+      if (!valid) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+        return;
+      }
+      if constexpr (kStrict) {
+        const float4* src =
+            reinterpret_cast<const float4*>(static_cast<const float*>(p.o) + pr * 128 + cc * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 v = __ldg(src + e);
+          ov[4 * e] = v.x;
+          ov[4 * e + 1] = v.y;
+          ov[4 * e + 2] = v.z;
+          ov[4 * e + 3] = v.w;
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.o) +
+                                                          pr * 128 + cc * 32);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint4 v = __ldg(src + e);
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+            ov[8 * e + 2 * u] = __bfloat162float(b2.x);
+            ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
+          }
+        }
+      }
+    };
+    // gate from GEMM 1, times o -> A2 (after GEMM 1 retired); o chunks are
+    // loaded one step ahead, the first one while GEMM 1 is still running
+    float ocur[32];
+    load_o(0, ocur);
     if (mbar_wait(g_done, 0, g, 5)) {
       tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
+        float onext[32];
+        if (cc < 3) load_o(cc + 1, onext);
         float gv[32];
         tmem_row32(tmem, warp, cc * 32, gv);
-        float ov[32];
-        if (valid) {
-          if constexpr (kStrict) {
-            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.o) +
-                                                                pr * 128 + cc * 32);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float4 v = src[e];
-              ov[4 * e] = v.x;
-              ov[4 * e + 1] = v.y;
-              ov[4 * e + 2] = v.z;
-              ov[4 * e + 3] = v.w;
-            }
-          } else {
-            const uint4* src = reinterpret_cast<const uint4*>(
-                static_cast<const __nv_bfloat16*>(p.o) + pr * 128 + cc * 32);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint4 v = src[e];
-              const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-                ov[8 * e + 2 * u] = __bfloat162float(b2.x);
-                ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
-              }
-            }
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
-        }
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
           const int c = cc * 32 + e;
-          a_store4<kStrict>(A, t, c, sigmoidf_(gv[e] + bvec[c]) * ov[e],
-                            sigmoidf_(gv[e + 1] + bvec[c + 1]) * ov[e + 1],
-                            sigmoidf_(gv[e + 2] + bvec[c + 2]) * ov[e + 2],
-                            sigmoidf_(gv[e + 3] + bvec[c + 3]) * ov[e + 3]);
+          a_store4<kStrict>(A, t, c, sigmoidf_(gv[e] + bvec[c]) * ocur[e],
+                            sigmoidf_(gv[e + 1] + bvec[c + 1]) * ocur[e + 1],
+                            sigmoidf_(gv[e + 2] + bvec[c + 2]) * ocur[e + 2],
+                            sigmoidf_(gv[e + 3] + bvec[c + 3]) * ocur[e + 3]);
+        }
+        if (cc < 3) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ocur[e] = onext[e];
         }
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(a_full);
+    // residual: z chunks loaded one step ahead, the first before GEMM 2 ends
+    float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
+    float4 zc[8];
+#pragma unroll
+    for (int v4 = 0; v4 < 8; ++v4) zc[v4] = valid ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
-      float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
+        float4 zn[8];
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4)
+          zn[v4] = (cc < 3 && valid) ? zrow[(cc + 1) * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
         float yv[32];
         tmem_row32(tmem, warp, 128 + cc * 32, yv);
         if (valid) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
-            float4 o = zrow[cc * 8 + v4];
+            float4 o = zc[v4];
             const int c = cc * 32 + 4 * v4;
             o.x += yv[4 * v4] + bvec[128 + c];
             o.y += yv[4 * v4 + 1] + bvec[129 + c];
@@ -812,6 +849,8 @@ __global__ void __launch_bounds__(192, 1)
             zrow[cc * 8 + v4] = o;
           }
         }
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4) zc[v4] = zn[v4];
       }
     }
   } else if (warp == 4) {
@@ -974,13 +1013,14 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     const uint64_t rowb = 32ull * esz;
     CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
     const uint64_t nh = (uint64_t)n * kHeads;
+    const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
     bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-              make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, 64, 1, qsw) &&
+              make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
               make_map_3d(&mvh, pl.v_hi, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
                           (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
     if (strict)
       ok = ok && make_map_3d(&mql, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-           make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, 64, 1, qsw) &&
+           make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
            make_map_3d(&mvl, pl.v_lo, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
                        (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
     else {

@@ -214,12 +214,20 @@ struct TriMulOutArgs {
   const float* ln_in_b;
   const float* ln_out_w;
   const float* ln_out_b;
-  const void* x;  // [128][n][ldx] fp32 (strict) or bf16 (fast)
-  int ldx;
-  size_t xcs;
+  const void* x;  // blocked [n][njb][128 c][128 j] fp32 (strict) or bf16 (fast)
+  int njb;
   int add;
   int* status;
 };
+
+// Element (channel c, tile row t) of a blocked x tile.
+template <bool kStrict>
+__device__ __forceinline__ float x_at(const void* tile, int c, int t) {
+  if constexpr (kStrict)
+    return __ldg(static_cast<const float*>(tile) + c * 128 + t);
+  else
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(tile)[c * 128 + t]);
+}
 
 template <bool kStrict>
 constexpr int out_smem_bytes() {
@@ -251,8 +259,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  const long long npairs = (long long)n * n;
-  const long long p0 = (long long)blockIdx.x * 128;
+  // tile = (pair row i, 128-column block jb): rows never straddle i
+  const int ti = blockIdx.x / p.njb, jb = blockIdx.x % p.njb;
+  const int jvalid = min(128, n - jb * 128);             // valid rows of this tile
+  const long long p0 = (long long)ti * n + jb * 128;     // pair index of tile row 0
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -293,8 +303,8 @@ __global__ void __launch_bounds__(192, 1)
         float4 x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const long long pr = p0 + warp * 32 + rr + u;
-          x[u] = pr < npairs ? z4[pr * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const int row = warp * 32 + rr + u;
+          x[u] = row < jvalid ? z4[(p0 + row) * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -305,64 +315,67 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }
-    // ---- A2 = LN_out(x) (thread-per-row: x is channel-first)
+    // ---- A2 = LN_out(x). The x tile is one contiguous [128 c][128 rows]
+    // block; thread t owns row t. Pass 1 streams it for shifted sums (a
+    // stable variance with no row kept in registers), pass 2 re-reads it
+    // (L1/L2 resident) to normalise into the A tile.
     const int t = warp * 32 + lane;
-    const long long pr = p0 + t;
-    const bool valid = pr < npairs;
-    const long long r = valid ? pr / n : 0, s = valid ? pr - (pr / n) * n : 0;
+    const bool valid = t < jvalid;
     {
-      float v[128];
-      const size_t pos = (size_t)r * p.ldx + (size_t)s;
-#pragma unroll
+      const size_t tile_elems = (size_t)blockIdx.x * 128 * 128;
+      const void* xt = kStrict ? (const void*)(static_cast<const float*>(p.x) + tile_elems)
+                               : (const void*)(static_cast<const __nv_bfloat16*>(p.x) + tile_elems);
+      const float shift = x_at<kStrict>(xt, 0, t);
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll 16
       for (int c = 0; c < 128; ++c) {
-        float val = 0.f;
-        if (valid) {
-          if constexpr (kStrict)
-            val = static_cast<const float*>(p.x)[(size_t)c * p.xcs + pos];
-          else
-            val = __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[(size_t)c * p.xcs + pos]);
-        }
-        v[c] = val;
+        const float d = x_at<kStrict>(xt, c, t) - shift;
+        s1 += d;
+        s2 += d * d;
       }
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) sum += v[c];
-      const float mean = sum * (1.0f / 128.0f);
-      float sq = 0.f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float d = v[c] - mean;
-        sq += d * d;
-      }
-      const float rs = rsqrtf(sq * (1.0f / 128.0f) + p.eps_out);
+      const float m1 = s1 * (1.0f / 128.0f);
+      const float mean = shift + m1;
+      const float var = fmaxf(s2 * (1.0f / 128.0f) - m1 * m1, 0.f);
+      const float rs = rsqrtf(var + p.eps_out);
       // the MMAs of GEMM 1 must have finished reading A before it is reused
       const bool ok = mbar_wait(a_free, 0, g, 5);
       if (ok) {
-#pragma unroll
+#pragma unroll 4
         for (int c = 0; c < 128; c += 4) {
-          a_store4<kStrict>(A, t, c, (v[c] - mean) * rs * lnp[c] + lnp[128 + c],
-                            (v[c + 1] - mean) * rs * lnp[c + 1] + lnp[129 + c],
-                            (v[c + 2] - mean) * rs * lnp[c + 2] + lnp[130 + c],
-                            (v[c + 3] - mean) * rs * lnp[c + 3] + lnp[131 + c]);
+          const float v0 = x_at<kStrict>(xt, c, t), v1 = x_at<kStrict>(xt, c + 1, t);
+          const float v2 = x_at<kStrict>(xt, c + 2, t), v3 = x_at<kStrict>(xt, c + 3, t);
+          a_store4<kStrict>(A, t, c, (v0 - mean) * rs * lnp[c] + lnp[128 + c],
+                            (v1 - mean) * rs * lnp[c + 1] + lnp[129 + c],
+                            (v2 - mean) * rs * lnp[c + 2] + lnp[130 + c],
+                            (v3 - mean) * rs * lnp[c + 3] + lnp[131 + c]);
         }
       }
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }
-    // ---- epilogue: delta = sigmoid(G) * Y, z <- [z +] delta
+    // ---- epilogue: delta = sigmoid(G) * Y, z <- [z +] delta; the z chunk
+    // of the next step is loaded before the current one is processed
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
-      float4* zrow = reinterpret_cast<float4*>(p.z) + (valid ? pr : 0) * 32;
+      float4* zrow = reinterpret_cast<float4*>(p.z) + (p0 + (valid ? t : 0)) * 32;
+      float4 zc[8];
+#pragma unroll
+      for (int v4 = 0; v4 < 8; ++v4)
+        zc[v4] = (valid && p.add) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
+        float4 zn[8];
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4)
+          zn[v4] = (cc < 3 && valid && p.add) ? zrow[(cc + 1) * 8 + v4]
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
         float gv[32], yv[32];
         tmem_row32(tmem, warp, cc * 32, gv);
         tmem_row32(tmem, warp, 128 + cc * 32, yv);
         if (valid) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
-            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.add) o = zrow[cc * 8 + v4];
+            float4 o = zc[v4];
             o.x += sigmoidf_(gv[4 * v4]) * yv[4 * v4];
             o.y += sigmoidf_(gv[4 * v4 + 1]) * yv[4 * v4 + 1];
             o.z += sigmoidf_(gv[4 * v4 + 2]) * yv[4 * v4 + 2];
@@ -370,6 +383,8 @@ __global__ void __launch_bounds__(192, 1)
             zrow[cc * 8 + v4] = o;
           }
         }
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4) zc[v4] = zn[v4];
       }
     }
   } else if (warp == 4) {
@@ -469,8 +484,8 @@ template <class Alloc>
 struct TriMulPlan {
   void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
   void *a_hi = nullptr, *a_lo = nullptr, *b_hi = nullptr, *b_lo = nullptr, *x = nullptr;
-  int ld = 0, ldx = 0;
-  size_t cs = 0, xcs = 0;
+  int ld = 0, njb = 0;
+  size_t cs = 0;
   void plan(Alloc& al, int n, bool strict) {
     auto takef = [&](size_t c) -> void* { return al.template take<float>(c); };
     auto takeh = [&](size_t c) -> void* { return al.template take<__nv_bfloat16>(c); };
@@ -487,9 +502,8 @@ struct TriMulPlan {
       a_lo = take(128 * cs);
       b_lo = take(128 * cs);
     }
-    ldx = padded_ld(n, strict ? 4 : 2);
-    xcs = (size_t)n * ldx;
-    x = take(128 * xcs);
+    njb = (n + 127) / 128;
+    x = take((size_t)n * njb * 128 * 128);  // blocked [n][njb][128 c][128 j]
   }
 };
 
@@ -555,18 +569,19 @@ extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const flo
   ContractArgs ca{};
   ca.n = n;
   ca.out = pl.x;
-  ca.ldo = pl.ldx;
-  ca.out_channel_stride = pl.xcs;
   ca.out_bf16 = strict ? 0 : 1;
   ca.status = status;
+  ca.blocked = 1;
+  ca.njb = pl.njb;
   if ((st = launch_contract(op, ca, stream))) return st;
-  TriMulOutArgs oa{z, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, pl.x, pl.ldx, pl.xcs,
+  TriMulOutArgs oa{z, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, pl.x, pl.njb,
                    add ? 1 : 0, status};
   {
     const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
     auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    FPB_LAUNCH("trimul_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
+    const unsigned out_tiles = (unsigned)(n * pl.njb);
+    FPB_LAUNCH("trimul_out", stream, k<<<out_tiles, 192, smem, stream>>>(moh, mol, oa));
     if ((st = launch_status())) return st;
   }
   return kOk;

@@ -18,6 +18,10 @@ LIB_PATH = Path(os.environ.get("FIREPROT_B200_LIBRARY",
                                Path(__file__).resolve().parent / "libfireprot_b200.so"))
 
 c_int, c_size_t, c_void_p, c_float = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float
+c_char_p = ctypes.c_char_p
+
+# capability callback of the registry core: (signature_json, user, reason, cap) -> int
+CAPABILITY_FN = ctypes.CFUNCTYPE(c_int, c_char_p, c_void_p, c_void_p, c_size_t)
 
 # name -> (restype, argtypes); must match include/fireprot_b200.h
 SIGNATURES = {
@@ -32,16 +36,29 @@ SIGNATURES = {
     "fpb_trimul": (c_int, [c_void_p, c_void_p, c_int, c_int] + [c_void_p] * 10
                    + [c_float, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_triattn_workspace_size": (c_size_t, [c_int] * 6),
-    "fpb_triattn": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int] + [c_void_p] * 10
+    "fpb_triattn": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+                    + [c_void_p] * 10
                     + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_transition_workspace_size": (c_size_t, [c_int, c_int, c_int]),
-    "fpb_transition": (c_int, [c_void_p, ctypes.c_longlong, c_int, c_int] + [c_void_p] * 5
+    "fpb_transition": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_int]
+                       + [c_void_p] * 5
                        + [c_float, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_pair_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "fpb_pair_block": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_float, c_int, c_void_p,
                                c_size_t, c_void_p]),
     "fpb_timing_enable": (c_int, [c_int]),
     "fpb_timing_collect": (c_int, [ctypes.c_char_p, c_size_t]),
+    "fpb_attention_core_workspace_size": (c_size_t, [c_int] * 6),
+    "fpb_attention_core": (c_int, [c_void_p, c_void_p] * 3 + [c_int] * 4
+                           + [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                              c_size_t, c_void_p]),
+    "fpb_registry_new": (c_void_p, []),
+    "fpb_registry_free": (None, [c_void_p]),
+    "fpb_registry_register": (c_int, [c_void_p, c_char_p, CAPABILITY_FN, c_void_p]),
+    "fpb_registry_unregister": (c_int, [c_void_p, c_char_p, c_char_p]),
+    "fpb_registry_resolve": (c_int, [c_void_p, c_char_p, c_char_p, c_size_t]),
+    "fpb_registry_manifest": (c_int, [c_void_p, c_char_p, c_size_t]),
+    "fpb_registry_clear_runtime_state": (c_int, [c_void_p]),
 }
 
 ABI_VERSION = 1

@@ -56,12 +56,12 @@ extern "C" int fpb_pair_block(float* z, const float* mask, int n,
   const fpb_triattn_weights* ta[2] = {&w->tri_att_start, &w->tri_att_end};
   for (int d = 0; d < 2; ++d) {
     const fpb_triattn_weights& a = *ta[d];
-    st = fpb_triattn(z, mask, n, 128, 4, 32, a.ln_w, a.ln_b, a.w_q, a.w_k, a.w_v, a.w_bias, a.w_g,
+    st = fpb_triattn(z, nullptr, mask, n, 128, 4, 32, a.ln_w, a.ln_b, a.w_q, a.w_k, a.w_v, a.w_bias, a.w_g,
                      a.b_g, a.w_o, a.b_o, eps, d == 0 ? 1 : 0, precision, workspace,
                      workspace_bytes, stream);
     if (st) return st;
   }
   const fpb_transition_weights& tr = w->transition;
-  return fpb_transition(z, (long long)n * n, 128, 4, tr.ln_w, tr.ln_b, tr.w_a, tr.w_b, tr.w_out,
+  return fpb_transition(z, nullptr, (long long)n * n, 128, 4, tr.ln_w, tr.ln_b, tr.w_a, tr.w_b, tr.w_out,
                         eps, precision, workspace, workspace_bytes, stream);
 }

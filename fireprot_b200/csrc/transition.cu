@@ -35,6 +35,7 @@ struct TransCfg {
 
 struct TransArgs {
   float* z;
+  float* delta;  // when non-null: write the update here and leave z unchanged
   int n_rows;
   float eps;
   const float* ln_w;
@@ -179,20 +180,27 @@ __global__ void __launch_bounds__(192, 1)
     if (ok && mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
       const long long pr = p0 + t;
-      float4* zrow = reinterpret_cast<float4*>(p.z) + (pr < rows ? pr : 0) * 32;
+      const long long rsafe = pr < rows ? pr : 0;
+      float4* zrow = reinterpret_cast<float4*>(p.z) + rsafe * 32;
+      float4* drow = p.delta ? reinterpret_cast<float4*>(p.delta) + rsafe * 32 : zrow;
+      const bool residual = p.delta == nullptr;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
+        float4 zc[8];
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4)
+          zc[v4] = (residual && pr < rows) ? zrow[cc * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
         float yv[32];
         tmem_row32(tmem + kAcc, warp, cc * 32, yv);
         if (pr < rows) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
-            float4 o = zrow[cc * 8 + v4];
+            float4 o = zc[v4];
             o.x += yv[4 * v4];
             o.y += yv[4 * v4 + 1];
             o.z += yv[4 * v4 + 2];
             o.w += yv[4 * v4 + 3];
-            zrow[cc * 8 + v4] = o;
+            drow[cc * 8 + v4] = o;
           }
         }
       }
@@ -356,11 +364,12 @@ extern "C" size_t fpb_transition_workspace_size(int c_z, int expansion, int prec
   return cnt.used;
 }
 
-extern "C" int fpb_transition(float* z, long long rows, int c_z, int expansion, const float* ln_w,
-                              const float* ln_b, const float* w_a, const float* w_b,
-                              const float* w_out, float eps, int precision, void* workspace,
-                              size_t workspace_bytes, cudaStream_t stream) {
+extern "C" int fpb_transition(float* z, float* delta_out, long long rows, int c_z, int expansion,
+                              const float* ln_w, const float* ln_b, const float* w_a,
+                              const float* w_b, const float* w_out, float eps, int precision,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!z || !ln_w || !ln_b || !w_a || !w_b || !w_out || !workspace) return kErrArg;
+  if (delta_out && !aligned16(delta_out)) return kErrAlign;
   if (c_z != 128 || expansion != 4 || rows <= 0) return kErrShape;
   if (rows > 0x7fffffffll) return kErrShape;
   if (precision != 0 && precision != 1) return kErrArg;
@@ -402,7 +411,7 @@ extern "C" int fpb_transition(float* z, long long rows, int c_z, int expansion, 
     m2l = m2h;
   }
   if (!ok) return kErrArg;
-  TransArgs ta{z, (int)rows, eps, ln_w, ln_b, static_cast<int*>(workspace)};
+  TransArgs ta{z, delta_out, (int)rows, eps, ln_w, ln_b, static_cast<int*>(workspace)};
   const unsigned tiles = (unsigned)((rows + 127) / 128);
   if (strict) {
     auto k = transition_kernel<true>;

@@ -272,10 +272,11 @@ __global__ void __launch_bounds__(192, 1)
 struct AttnCoreArgs {
   int n;
   const float* bias;   // [4][n][ldb]
-  const float* mbias;  // [n][ldb] or null
+  const float* mbias;  // [rows][ldb] or null
   int ldb;
-  void* o;             // [n*n][128] fp32 (strict) / bf16 (fast), y coordinates
+  void* o;             // [rows*n][128] fp32 (strict or o_f32) / bf16 (fast)
   int* status;
+  int o_f32;           // write fp32 output in fast mode too
 };
 
 template <bool kStrict>
@@ -618,7 +619,7 @@ __global__ void __launch_bounds__(192, 2)
       for (int d = 0; d < 32; ++d) o[d] = (o[d] * alpha_prev + pv[d]) * inv;
       if (jvalid) {
         const size_t orow = (size_t)i * n + j;
-        if constexpr (kStrict) {
+        if (kStrict || p.o_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * 128 + h * 32);
 #pragma unroll
           for (int e = 0; e < 8; ++e)
@@ -654,6 +655,7 @@ __global__ void __launch_bounds__(192, 2)
 // ============================================================================
 struct AttnOutArgs {
   float* z;
+  float* delta;  // when non-null: write the update here and leave z unchanged
   int n;
   float eps;
   const float* ln_w;
@@ -823,10 +825,14 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_before();
     mbar_arrive(a_full);
     // residual: z chunks loaded one step ahead, the first before GEMM 2 ends
+    // (delta mode: the update is written to p.delta and z is not read)
+    const bool residual = p.delta == nullptr;
     float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
+    float4* drow = residual ? zrow : reinterpret_cast<float4*>(p.delta) + zrow_idx * 32;
     float4 zc[8];
 #pragma unroll
-    for (int v4 = 0; v4 < 8; ++v4) zc[v4] = valid ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int v4 = 0; v4 < 8; ++v4)
+      zc[v4] = (valid && residual) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
 #pragma unroll 1
@@ -834,7 +840,8 @@ __global__ void __launch_bounds__(192, 1)
         float4 zn[8];
 #pragma unroll
         for (int v4 = 0; v4 < 8; ++v4)
-          zn[v4] = (cc < 3 && valid) ? zrow[(cc + 1) * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
+          zn[v4] = (cc < 3 && valid && residual) ? zrow[(cc + 1) * 8 + v4]
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         float yv[32];
         tmem_row32(tmem, warp, 128 + cc * 32, yv);
         if (valid) {
@@ -846,7 +853,7 @@ __global__ void __launch_bounds__(192, 1)
             o.y += yv[4 * v4 + 1] + bvec[129 + c];
             o.z += yv[4 * v4 + 2] + bvec[130 + c];
             o.w += yv[4 * v4 + 3] + bvec[131 + c];
-            zrow[cc * 8 + v4] = o;
+            drow[cc * 8 + v4] = o;
           }
         }
 #pragma unroll
@@ -954,7 +961,8 @@ extern "C" size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head
   return cnt.used;
 }
 
-extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head_dim,
+extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n, int c_z,
+                           int heads, int head_dim,
                            const float* ln_w, const float* ln_b, const float* w_q,
                            const float* w_k, const float* w_v, const float* w_bias,
                            const float* w_g, const float* b_g, const float* w_o,
@@ -966,6 +974,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
   if (precision != 0 && precision != 1) return kErrArg;
   if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
     return kErrAlign;
+  if (delta_out && !aligned16(delta_out)) return kErrAlign;
   const bool strict = precision == 0;
   const bool with_mask = mask != nullptr;
   if (workspace_bytes <
@@ -1029,7 +1038,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
       mvl = mvh;
     }
     if (!ok) return kErrArg;
-    AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, pl.o, status};
+    AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, pl.o, status, 0};
     dim3 grid((n + 127) / 128, kHeads, n);
     if (strict) {
       auto k = attn_core_kernel<true>;
@@ -1045,7 +1054,7 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     if ((st = launch_status())) return st;
   }
   // 3. gate + output projection + residual
-  AttnOutArgs oa{z, n, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
+  AttnOutArgs oa{z, delta_out, n, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
   {
     const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
     auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
@@ -1055,4 +1064,226 @@ extern "C" int fpb_triattn(float* z, const float* mask, int n, int c_z, int head
     if ((st = launch_status())) return st;
   }
   return kOk;
+}
+
+// ============================================================================
+// attention core at the reference's q/k/v boundary
+// ============================================================================
+namespace fpb {
+
+// q or k [B, H, N, 32] (any strides) -> [(b*H + h)*N + j][32] split / bf16.
+template <bool kStrict>
+__global__ void pack_qk_kernel(const float* __restrict__ src, long long s0, long long s1,
+                               long long s2, long long s3, int batch, int n, void* hi, void* lo) {
+  const long long total = (long long)batch * kHeads * n * 32;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(e & 31);
+    const long long row = e >> 5;  // (b*H + h)*n + j
+    const int j = (int)(row % n);
+    const long long bh = row / n;
+    const int h = (int)(bh % kHeads);
+    const long long b = bh / kHeads;
+    const float v = src[b * s0 + h * s1 + j * s2 + d * s3];
+    if constexpr (kStrict) {
+      float vh, vl;
+      split_tf32(v, vh, vl);
+      static_cast<float*>(hi)[e] = vh;
+      static_cast<float*>(lo)[e] = vl;
+    } else {
+      static_cast<__nv_bfloat16*>(hi)[e] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// v [B, H, N, 32] (any strides) -> v^T [(b*H + h)*32 + d][ldv], 32x32 tiles.
+template <bool kStrict>
+__global__ void pack_vt_kernel(const float* __restrict__ src, long long s0, long long s1,
+                               long long s2, long long s3, int n, int ldv, void* hi, void* lo) {
+  __shared__ float tile[32][33];
+  const long long bh = blockIdx.y;
+  const int k0 = blockIdx.x * 32;
+  const long long b = bh / kHeads;
+  const int h = (int)(bh % kHeads);
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const int k = k0 + y;
+    tile[y][threadIdx.x] = k < n ? src[b * s0 + h * s1 + k * s2 + threadIdx.x * s3] : 0.f;
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {  // y = d
+    const int k = k0 + threadIdx.x;
+    if (k < n) {
+      const size_t idx = ((size_t)bh * 32 + y) * ldv + k;
+      const float v = tile[threadIdx.x][y];
+      if constexpr (kStrict) {
+        float vh, vl;
+        split_tf32(v, vh, vl);
+        static_cast<float*>(hi)[idx] = vh;
+        static_cast<float*>(lo)[idx] = vl;
+      } else {
+        static_cast<__nv_bfloat16*>(hi)[idx] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+}
+
+// triangle bias [1, H, N, N] -> [h][j][ldb]; mask bias [B, 1, 1, N] -> [b][ldb]
+__global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, long long t2,
+                                 long long t3, const float* __restrict__ mb, long long m0,
+                                 long long m3, int batch, int n, int ldb, float* bias,
+                                 float* mbias) {
+  const long long nb = (long long)kHeads * n * n;
+  const long long nm = mb ? (long long)batch * n : 0;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < nb + nm;
+       e += (long long)gridDim.x * blockDim.x) {
+    if (e < nb) {
+      const int k = (int)(e % n);
+      const long long hj = e / n;
+      const int j = (int)(hj % n);
+      const int h = (int)(hj / n);
+      bias[((size_t)h * n + j) * ldb + k] = tb[h * t1 + j * t2 + k * t3];
+    } else {
+      const long long f = e - nb;
+      const int k = (int)(f % n);
+      const long long b = f / n;
+      mbias[(size_t)b * ldb + k] = mb[b * m0 + k * m3];
+    }
+  }
+}
+
+template <class Alloc>
+struct CorePlan {
+  void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr, *v_hi = nullptr,
+       *v_lo = nullptr;
+  float *bias = nullptr, *mbias = nullptr;
+  int ldv = 0, ldb = 0;
+  void plan(Alloc& al, int batch, int n, bool strict, bool with_mask) {
+    auto take = [&](size_t c) -> void* {
+      return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
+    };
+    const size_t qk = (size_t)batch * kHeads * n * 32;
+    q_hi = take(qk);
+    k_hi = take(qk);
+    if (strict) {
+      q_lo = take(qk);
+      k_lo = take(qk);
+    }
+    ldv = padded_ld(n, strict ? 4 : 2);
+    const size_t vc = (size_t)batch * kHeads * 32 * ldv;
+    v_hi = take(vc);
+    if (strict) v_lo = take(vc);
+    ldb = padded_ld(n, 4);
+    bias = al.template take<float>((size_t)kHeads * n * ldb);
+    if (with_mask) mbias = al.template take<float>((size_t)batch * ldb);
+  }
+};
+
+}  // namespace fpb
+
+extern "C" size_t fpb_attention_core_workspace_size(int batch, int n, int heads, int head_dim,
+                                                    int precision, int with_mask) {
+  if (batch <= 0 || n <= 0 || heads != kHeads || head_dim != kHeadDim) return 0;
+  if (precision != 0 && precision != 1) return 0;
+  WsCounter cnt;
+  CorePlan<WsCounter> pl;
+  pl.plan(cnt, batch, n, precision == 0, with_mask != 0);
+  return cnt.used;
+}
+
+extern "C" int fpb_attention_core(const float* q, const long long* q_strides, const float* k,
+                                  const long long* k_strides, const float* v,
+                                  const long long* v_strides, int batch, int n, int heads,
+                                  int head_dim, const float* tri_bias,
+                                  const long long* tri_bias_strides, const float* mask_bias,
+                                  const long long* mask_bias_strides, float* out, int precision,
+                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!q || !k || !v || !q_strides || !k_strides || !v_strides || !tri_bias ||
+      !tri_bias_strides || !out || !workspace || (mask_bias && !mask_bias_strides))
+    return kErrArg;
+  if (heads != kHeads || head_dim != kHeadDim || batch <= 0 || n <= 0) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(out) || !aligned16(workspace)) return kErrAlign;
+  const bool strict = precision == 0;
+  const bool with_mask = mask_bias != nullptr;
+  if (workspace_bytes <
+      fpb_attention_core_workspace_size(batch, n, heads, head_dim, precision, with_mask))
+    return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  CorePlan<WsCursor> pl;
+  pl.plan(cur, batch, n, strict, with_mask);
+  if (!cur.ok) return kErrWorkspace;
+  if (reset_status(workspace, stream)) return kErrCuda;
+  int st;
+  const long long* qs = q_strides;
+  const long long* ks = k_strides;
+  const long long* vs = v_strides;
+  if (strict) {
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_qk_kernel<true><<<1184, 256, 0, stream>>>(q, qs[0], qs[1], qs[2], qs[3], batch,
+                                                              n, pl.q_hi, pl.q_lo));
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_qk_kernel<true><<<1184, 256, 0, stream>>>(k, ks[0], ks[1], ks[2], ks[3], batch,
+                                                              n, pl.k_hi, pl.k_lo));
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_vt_kernel<true><<<dim3((n + 31) / 32, batch * kHeads), dim3(32, 8), 0,
+                                      stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv,
+                                                pl.v_hi, pl.v_lo));
+  } else {
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_qk_kernel<false><<<1184, 256, 0, stream>>>(q, qs[0], qs[1], qs[2], qs[3],
+                                                               batch, n, pl.q_hi, nullptr));
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_qk_kernel<false><<<1184, 256, 0, stream>>>(k, ks[0], ks[1], ks[2], ks[3],
+                                                               batch, n, pl.k_hi, nullptr));
+    FPB_LAUNCH("pack_qkv", stream,
+               pack_vt_kernel<false><<<dim3((n + 31) / 32, batch * kHeads), dim3(32, 8), 0,
+                                       stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv,
+                                                 pl.v_hi, nullptr));
+  }
+  const long long* tb = tri_bias_strides;
+  const long long* mbs = mask_bias_strides;
+  FPB_LAUNCH("pack_qkv", stream,
+             pack_bias_kernel<<<1184, 256, 0, stream>>>(tri_bias, tb[1], tb[2], tb[3], mask_bias,
+                                                        with_mask ? mbs[0] : 0,
+                                                        with_mask ? mbs[3] : 0, batch, n, pl.ldb,
+                                                        pl.bias, pl.mbias));
+  if ((st = launch_status())) return st;
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const uint64_t rowb = 32ull * esz;
+  const uint64_t nh = (uint64_t)batch * kHeads;
+  const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
+  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+  bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+            make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
+            make_map_3d(&mvh, pl.v_hi, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
+                        (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
+  if (strict)
+    ok = ok && make_map_3d(&mql, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+         make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
+         make_map_3d(&mvl, pl.v_lo, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
+                     (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
+  else {
+    mql = mqh;
+    mkl = mkh;
+    mvl = mvh;
+  }
+  if (!ok) return kErrArg;
+  // this boundary returns FP32 [B, N, H, D] in both precision modes
+  AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1};
+  dim3 grid((n + 127) / 128, kHeads, batch);
+  if (strict) {
+    auto kk = attn_core_kernel<true>;
+    cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
+    FPB_LAUNCH("triattn_core", stream,
+               kk<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
+  } else {
+    auto kk = attn_core_kernel<false>;
+    cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
+    FPB_LAUNCH("triattn_core", stream,
+               kk<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
+  }
+  return launch_status();
 }

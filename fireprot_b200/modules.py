@@ -82,6 +82,7 @@ class TriangleAttention(nn.Module):
         self.layer_norm = nn.LayerNorm(c_in)
         self.linear = _linear(c_in, no_heads)
         self.mha = nn.Module()
+        self.mha.no_heads, self.mha.c_hidden = no_heads, c_hidden
         hd = c_hidden * no_heads
         self.mha.linear_q = _linear(c_in, hd)
         self.mha.linear_k = _linear(c_in, hd)

@@ -111,10 +111,12 @@ TRIATTN_WEIGHTS = ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias", "w_g", "b_g", 
 
 
 def triattn(z: torch.Tensor, mask, w: dict, *, starting: bool = True, precision="strict",
-            eps: float = 1e-5, return_workspace: bool = False):
+            eps: float = 1e-5, return_workspace: bool = False, delta_out=None):
     """Triangle attention update added in place to ``z`` ``[n, n, 128]``
     (H=4, d=32). ``w`` holds ``ln_w, ln_b, w_q, w_k, w_v, w_bias, w_g, w_o``
-    and optional ``b_g`` / ``b_o``. Returns ``z`` (same storage)."""
+    and optional ``b_g`` / ``b_o``. Returns ``z`` (same storage), or, when
+    ``delta_out`` (a float32 tensor like ``z``) is given, writes the update
+    there, leaves ``z`` unchanged and returns ``delta_out``."""
     _require_cuda(z, mask)
     if z.dtype != torch.float32 or z.ndim != 3 or z.shape[0] != z.shape[1] or z.shape[2] != 128:
         raise RuntimeError("triattn takes a float32 [n, n, 128] pair tensor")
@@ -142,16 +144,24 @@ def triattn(z: torch.Tensor, mask, w: dict, *, starting: bool = True, precision=
     p = precision_code(precision)
     ws = workspace(lib.fpb_triattn_workspace_size(n, 128, 4, 32, p, int(mask is not None)),
                    z.device)
-    _lib.check(lib.fpb_triattn(z.data_ptr(), 0 if mask is None else mask.data_ptr(), n, 128, 4, 32,
-                               *ptrs, float(eps), int(bool(starting)), p, ws.data_ptr(),
-                               ws.numel(), _stream_ptr(z.device)), "fpb_triattn")
-    return (z, ws) if return_workspace else z
+    dptr = 0
+    if delta_out is not None:
+        if (delta_out.shape != z.shape or delta_out.dtype != torch.float32
+                or not delta_out.is_contiguous() or delta_out.device != z.device):
+            raise RuntimeError("delta_out must be a contiguous float32 tensor shaped like z")
+        dptr = delta_out.data_ptr()
+    _lib.check(lib.fpb_triattn(z.data_ptr(), dptr, 0 if mask is None else mask.data_ptr(), n,
+                               128, 4, 32, *ptrs, float(eps), int(bool(starting)), p,
+                               ws.data_ptr(), ws.numel(), _stream_ptr(z.device)), "fpb_triattn")
+    res = z if delta_out is None else delta_out
+    return (res, ws) if return_workspace else res
 
 
 def transition(z: torch.Tensor, w: dict, *, precision="strict", eps: float = 1e-5,
-               return_workspace: bool = False):
+               return_workspace: bool = False, delta_out=None):
     """Pair transition update added in place to ``z`` ``[..., 128]``; ``w``
-    holds ``ln_w, ln_b, w_a, w_b, w_out`` (4x expansion). Returns ``z``."""
+    holds ``ln_w, ln_b, w_a, w_b, w_out`` (4x expansion). Returns ``z``, or
+    writes the update alone to ``delta_out`` (``z`` unchanged) when given."""
     _require_cuda(z)
     if z.dtype != torch.float32 or z.shape[-1] != 128:
         raise RuntimeError("transition takes float32 [..., 128] rows")
@@ -165,10 +175,65 @@ def transition(z: torch.Tensor, w: dict, *, precision="strict", eps: float = 1e-
     p = precision_code(precision)
     ws = workspace(lib.fpb_transition_workspace_size(128, 4, p), z.device)
     rows = z.numel() // 128
-    _lib.check(lib.fpb_transition(z.data_ptr(), rows, 128, 4, *[t.data_ptr() for t in ts],
+    dptr = 0
+    if delta_out is not None:
+        if (delta_out.shape != z.shape or delta_out.dtype != torch.float32
+                or not delta_out.is_contiguous() or delta_out.device != z.device):
+            raise RuntimeError("delta_out must be a contiguous float32 tensor shaped like z")
+        dptr = delta_out.data_ptr()
+    _lib.check(lib.fpb_transition(z.data_ptr(), dptr, rows, 128, 4, *[t.data_ptr() for t in ts],
                                   float(eps), p, ws.data_ptr(), ws.numel(),
                                   _stream_ptr(z.device)), "fpb_transition")
-    return (z, ws) if return_workspace else z
+    res = z if delta_out is None else delta_out
+    return (res, ws) if return_workspace else res
+
+
+def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
+                   precision="strict", return_workspace: bool = False):
+    """``softmax(q k^T + sum(biases)) v`` at the reference's dispatch boundary.
+
+    q (pre-scaled), k, v: ``[B, 4, N, 32]`` float32, any strides; ``biases``
+    is ``[triangle_bias]`` or ``[mask_bias, triangle_bias]`` with
+    ``mask_bias [B, 1, 1, N]`` and ``triangle_bias [1, 4, N, N]``. Returns
+    ``[B, N, 4, 32]`` (``triangle_attention.py:129``).
+    """
+    _require_cuda(q, k, v, *biases)
+    if q.ndim != 4 or q.shape[1] != 4 or q.shape[3] != 32 or q.shape != k.shape \
+            or q.shape != v.shape:
+        raise RuntimeError("attention_core takes q, k, v of shape [B, 4, N, 32]")
+    batch, _, n, _ = q.shape
+    if any(t.dtype != torch.float32 for t in (q, k, v, *biases)):
+        raise RuntimeError("attention_core takes float32 tensors")
+    if len(biases) == 1:
+        mask_bias, tri = None, biases[0]
+    elif len(biases) == 2:
+        mask_bias, tri = biases
+    else:
+        raise RuntimeError("attention_core takes one or two biases")
+    if tuple(tri.shape) != (1, 4, n, n):
+        raise RuntimeError("triangle bias must be [1, 4, N, N]")
+    if mask_bias is not None and tuple(mask_bias.shape) != (batch, 1, 1, n):
+        raise RuntimeError("mask bias must be [B, 1, 1, N]")
+    lib = _lib.load()
+    p = precision_code(precision)
+    out = torch.empty(batch, n, 4, 32, dtype=torch.float32, device=q.device)
+    ws = workspace(lib.fpb_attention_core_workspace_size(batch, n, 4, 32, p,
+                                                         int(mask_bias is not None)), q.device)
+
+    keep = []
+
+    def strides(t):
+        arr = (ctypes.c_longlong * 4)(*t.stride())
+        keep.append(arr)
+        return ctypes.cast(arr, ctypes.c_void_p)
+
+    qs, ks, vs, ts = strides(q), strides(k), strides(v), strides(tri)
+    ms = strides(mask_bias) if mask_bias is not None else None
+    _lib.check(lib.fpb_attention_core(
+        q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, batch, n, 4, 32, tri.data_ptr(), ts,
+        0 if mask_bias is None else mask_bias.data_ptr(), ms, out.data_ptr(), p, ws.data_ptr(),
+        ws.numel(), _stream_ptr(q.device)), "fpb_attention_core")
+    return (out, ws) if return_workspace else out
 
 
 def pair_block_workspace(n: int, precision, with_mask: bool, device) -> torch.Tensor:

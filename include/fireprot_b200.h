@@ -75,7 +75,9 @@ int fpb_trimul(float* z, const float* mask, int n, int c_z, const float* ln_in_w
  *   x = LN(y), y = z (start) or z^T (end, mask^T);
  *   s_ijk = (x_ij Wq_h^T/sqrt(d)) . (x_ik Wk_h^T) + 1e9 (mask_ik - 1) + x_jk . Wbias_h
  *   o_ij = sum_k softmax_k(s) (x_ik Wv_h^T); delta = W_o (sigmoid(x Wg^T + b_g) * o) + b_o
- * (end node: delta transposed back). heads = 4, head_dim = 32, c_z = 128;
+ * (end node: delta transposed back). With delta_out non-null the update is
+ * written there ([n, n, 128], the reference module's return value) and z is
+ * left unchanged. heads = 4, head_dim = 32, c_z = 128;
  * w_q/w_k/w_v/w_g [128,128], w_bias [4,128], w_o [128,128]; b_g, b_o nullable.
  * Replaces dispatch_triangle_attention + the QKV / gate hooks
  * (python/fireprot/backends/amd/triangle_attention.py:199-256,
@@ -85,7 +87,8 @@ int fpb_trimul(float* z, const float* mask, int n, int c_z, const float* ln_in_w
  * The mask bias follows patches/protenix/0005-...patch:35-38 (inf = 1e9). */
 size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head_dim, int precision,
                                   int with_mask);
-int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head_dim,
+int fpb_triattn(float* z, float* delta_out, const float* mask, int n, int c_z, int heads,
+                int head_dim,
                 const float* ln_w, const float* ln_b, const float* w_q, const float* w_k,
                 const float* w_v, const float* w_bias, const float* w_g, const float* b_g,
                 const float* w_o, const float* b_o, float eps, int starting, int precision,
@@ -93,15 +96,50 @@ int fpb_triattn(float* z, const float* mask, int n, int c_z, int heads, int head
 
 /* Pair transition, residual added in place on `rows` rows of 128 channels:
  *   z <- z + (silu(LN(z) Wa^T) * (LN(z) Wb^T)) Wout^T
- * expansion = 4: w_a, w_b [512,128], w_out [128,512], bias-free.
+ * expansion = 4: w_a, w_b [512,128], w_out [128,512], bias-free. With delta_out
+ * non-null the update alone is written there (the reference's
+ * Transition.forward return value) and z is left unchanged.
  * Replaces dispatch_transition / _hip_transition
  * (python/fireprot/backends/amd/recycle.py:203-227,360) and the
  * project_transition kernel (kernels/amd/fireprot_amd_ops.cu:1106-1183). */
 size_t fpb_transition_workspace_size(int c_z, int expansion, int precision);
-int fpb_transition(float* z, long long rows, int c_z, int expansion, const float* ln_w,
-                   const float* ln_b, const float* w_a, const float* w_b, const float* w_out,
-                   float eps, int precision, void* workspace, size_t workspace_bytes,
-                   cudaStream_t stream);
+int fpb_transition(float* z, float* delta_out, long long rows, int c_z, int expansion,
+                   const float* ln_w, const float* ln_b, const float* w_a, const float* w_b,
+                   const float* w_out, float eps, int precision, void* workspace,
+                   size_t workspace_bytes, cudaStream_t stream);
+
+/* Triangle attention core at the reference's q/k/v boundary
+ * (dispatch_triangle_attention, python/fireprot/backends/amd/triangle_attention.py:199-256,
+ * replacing ck_attention* in kernels/amd/fireprot_ck_attention.cpp:34-121):
+ *   out[b, j, h, :] = sum_k softmax_k(q[b,h,j,:].k[b,h,k,:] + mask_bias[b,0,0,k]
+ *                                     + tri_bias[0,h,j,k]) v[b,h,k,:]
+ * q (already scaled), k, v: [batch, 4, n, 32] FP32 with element strides
+ * (4 entries each); tri_bias [1, 4, n, n], mask_bias [batch, 1, 1, n] or null,
+ * any strides; out [batch, n, 4, 32] contiguous FP32 (both precisions). */
+size_t fpb_attention_core_workspace_size(int batch, int n, int heads, int head_dim,
+                                         int precision, int with_mask);
+int fpb_attention_core(const float* q, const long long* q_strides, const float* k,
+                       const long long* k_strides, const float* v, const long long* v_strides,
+                       int batch, int n, int heads, int head_dim, const float* tri_bias,
+                       const long long* tri_bias_strides, const float* mask_bias,
+                       const long long* mask_bias_strides, float* out, int precision,
+                       void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Operator policy registry (host only), the counterpart of the reference's
+ * Rust core crates/fireprot-core/src/registry.rs:95-268 behind its bridge
+ * protocol (crates/fireprot-bridge/src/lib.rs:86-125): JSON metadata and
+ * signatures in, JSON selections and manifests out. Capability callbacks
+ * return 1 (supported), 0 (rejected, reason written) or -1 (interrupted). */
+typedef int (*fpb_capability_fn)(const char* signature_json, void* user, char* reason,
+                                 size_t cap);
+void* fpb_registry_new(void);
+void fpb_registry_free(void* registry);
+int fpb_registry_register(void* registry, const char* metadata_json, fpb_capability_fn fn,
+                          void* user);
+int fpb_registry_unregister(void* registry, const char* operation, const char* name);
+int fpb_registry_resolve(void* registry, const char* signature_json, char* out, size_t cap);
+int fpb_registry_manifest(void* registry, char* out, size_t cap);
+int fpb_registry_clear_runtime_state(void* registry);
 
 /* Weights of the five pair operators of one block (torch Linear layouts). */
 typedef struct {

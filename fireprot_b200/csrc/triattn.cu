@@ -282,25 +282,26 @@ struct AttnCoreArgs {
 template <bool kStrict>
 struct AttnCfg {
   static constexpr int BQ = 128;
-  // key tile: one 128-byte atom of P per tile (32 fp32 keys in strict mode,
-  // 64 bf16 keys in fast mode); small enough for two CTAs per SM
+  // key tile: one 128-byte row of V^T (32 fp32 keys strict / 64 bf16 fast)
   static constexpr int BKV = kStrict ? 32 : 64;
   static constexpr int ESZ = kStrict ? 4 : 2;
   static constexpr int NSPLIT = kStrict ? 2 : 1;
   static constexpr int QK_ROW = 32 * ESZ;                 // bytes per q/k row (128 / 64)
   static constexpr int Q_BYTES = BQ * QK_ROW;             // per split
   static constexpr int K_BYTES = BKV * QK_ROW;            // per split
-  static constexpr int V_ATOM_KEYS = 128 / ESZ;           // 32 / 64 keys per 128-byte row
-  static constexpr int V_ATOMS = BKV / V_ATOM_KEYS;       // 2 / 1
+  static constexpr int V_ATOM_KEYS = 128 / ESZ;           // keys per 128-byte row
+  static constexpr int V_ATOMS = BKV / V_ATOM_KEYS;       // 1
   static constexpr int V_BYTES = V_ATOMS * 32 * 128;      // per split
   static constexpr int KV_STAGE = NSPLIT * (K_BYTES + V_BYTES);
-  static constexpr int KV_STAGES = kStrict ? 2 : 3;
-  static constexpr int P_ATOMS = BKV / V_ATOM_KEYS;       // K atoms of P
-  static constexpr int P_BYTES = P_ATOMS * BQ * 128;      // per split
-  // TMEM: S double buffer (2 x BKV columns) + P V (32 columns)
-  static constexpr int TMEM_COLS = (2 * BKV + 32) <= 128 ? 128 : 256;
-  static constexpr int SMEM = tmem_safe_smem(
-      NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + NSPLIT * P_BYTES + 1024 + 256, TMEM_COLS);
+  static constexpr int KV_STAGES = kStrict ? 4 : 6;
+  // TMEM columns: S[2] (BKV each), P V[2] (32 each), P[2] (P_COLS each:
+  // tf32 hi | lo in strict mode, bf16 pairs in fast mode)
+  static constexpr int P_COLS = kStrict ? 2 * BKV : BKV / 2;
+  static constexpr uint32_t kS = 0, kPV = 2 * BKV, kP = 2 * BKV + 64;
+  static constexpr int TMEM_COLS = 256;
+  static_assert(2 * BKV + 64 + 2 * P_COLS <= TMEM_COLS, "TMEM budget");
+  static constexpr int SMEM =
+      tmem_safe_smem(NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + 1024 + 256, TMEM_COLS);
 };
 
 template <bool kStrict>
@@ -311,6 +312,12 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
     return umma_desc_sw64(addr);
 }
 
+// Pipeline per CTA (one MMA thread, one TMA thread, 128 softmax threads):
+//   MMA:     S(t) = Q K_t^T -> S[t%2];  P V(t-1) = P[(t-1)%2] (TMEM) x V_{t-1}
+//   softmax: read S(t), online max/exp/sum, fold P V(t-2) into registers,
+//            write P(t) to TMEM P[t%2]
+// P and P V are double-buffered, so the softmax of tile t never waits for
+// the P V product of tile t-1; it folds the one of tile t-2.
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 2)
     attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
@@ -325,16 +332,16 @@ __global__ void __launch_bounds__(192, 2)
                                              ~uintptr_t(1023));
   uint8_t* Q = smem;                                   // [split][BQ x QK_ROW]
   uint8_t* KV = Q + C::NSPLIT * C::Q_BYTES;            // stages
-  uint8_t* P = KV + C::KV_STAGES * C::KV_STAGE;        // [split][P_ATOMS][BQ x 128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(P + C::NSPLIT * C::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(KV + C::KV_STAGES * C::KV_STAGE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + C::KV_STAGES;
   uint64_t* s_full = kv_empty + C::KV_STAGES;   // [2]
   uint64_t* s_free = s_full + 2;                // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* pv_full = p_full + 1;
-  uint64_t* drain = pv_full + 1;
+  uint64_t* p_full = s_free + 2;                // [2]
+  uint64_t* pv_full = p_full + 2;               // [2]
+  uint64_t* pv_free = pv_full + 2;              // [2]
+  uint64_t* drain = pv_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -343,8 +350,6 @@ __global__ void __launch_bounds__(192, 2)
   const int jt = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int ih = i * kHeads + h;
   const int nt = (n + C::BKV - 1) / C::BKV;
-  // TMEM columns: S[0] [0, BKV), S[1] [BKV, 2 BKV), P V [2 BKV, 2 BKV + 32)
-  constexpr uint32_t kS0 = 0, kPV = 2 * C::BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -355,9 +360,10 @@ __global__ void __launch_bounds__(192, 2)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 128);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&pv_full[b], 1);
+      mbar_init(&pv_free[b], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -387,15 +393,10 @@ __global__ void __launch_bounds__(192, 2)
         mbar_arrive_expect_tx(&kv_full[s], C::KV_STAGE);
         tma_load_3d(st, &mk_hi, &kv_full[s], 0, t * C::BKV, ih);
         uint8_t* vst = st + C::NSPLIT * C::K_BYTES;
-#pragma unroll
-        for (int a = 0; a < C::V_ATOMS; ++a)
-          tma_load_3d(vst + a * 4096, &mv_hi, &kv_full[s], t * C::BKV + a * C::V_ATOM_KEYS, 0, ih);
+        tma_load_3d(vst, &mv_hi, &kv_full[s], t * C::BKV, 0, ih);
         if constexpr (kStrict) {
           tma_load_3d(st + C::K_BYTES, &mk_lo, &kv_full[s], 0, t * C::BKV, ih);
-#pragma unroll
-          for (int a = 0; a < C::V_ATOMS; ++a)
-            tma_load_3d(vst + C::V_BYTES + a * 4096, &mv_lo, &kv_full[s],
-                        t * C::BKV + a * C::V_ATOM_KEYS, 0, ih);
+          tma_load_3d(vst + C::V_BYTES, &mv_lo, &kv_full[s], t * C::BKV, 0, ih);
         }
         ++issued;
       }
@@ -412,36 +413,31 @@ __global__ void __launch_bounds__(192, 2)
       const uint32_t id_s = kStrict ? idesc_tf32(128, C::BKV) : idesc_bf16(128, C::BKV);
       const uint32_t id_o = kStrict ? idesc_tf32(128, 32) : idesc_bf16(128, 32);
       const uint32_t q_hi = smem_u32(Q), q_lo = smem_u32(Q + C::Q_BYTES);
-      const uint32_t p_hi = smem_u32(P), p_lo = smem_u32(P + C::P_BYTES);
-      constexpr int QK_STEPS = C::QK_ROW / 32;  // 4 (fp32) or 2 (bf16) K steps over d
+      constexpr int QK_STEPS = C::QK_ROW / 32;  // 32-byte K steps over d
       bool ok = mbar_wait(q_full, 0, g, 22);
       auto issue_pv = [&](int u) -> bool {
-        if (!mbar_wait(p_full, u & 1, g, 23)) return false;
+        const int b = u & 1;
+        if (!mbar_wait(&p_full[b], (u >> 1) & 1, g, 23)) return false;
+        if (u >= 2 && !mbar_wait(&pv_free[b], ((u - 2) >> 1) & 1, g, 29)) return false;
         tc_fence_after();
-        const uint32_t vst = smem_u32(KV + (u % C::KV_STAGES) * C::KV_STAGE +
-                                      C::NSPLIT * C::K_BYTES);
-        // K = 64 keys, in P_ATOMS atoms of 128 bytes, 4 x 32-byte steps each
+        const uint32_t vst =
+            smem_u32(KV + (u % C::KV_STAGES) * C::KV_STAGE + C::NSPLIT * C::K_BYTES);
+        const uint32_t pa = tmem + C::kP + b * C::P_COLS;
+        const uint32_t dpv = tmem + C::kPV + b * 32;
 #pragma unroll
-        for (int a = 0; a < C::P_ATOMS; ++a) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t off = a * (C::BQ * 128) + kk * 32;
-            const uint32_t voff = a * 4096 + kk * 32;
-            const uint32_t acc = (a == 0 && kk == 0) ? 0u : 1u;
-            const uint64_t dph = umma_desc_sw128(p_hi + off);
-            const uint64_t dvh = umma_desc_sw128(vst + voff);
-            if constexpr (kStrict) {
-              const uint64_t dpl = umma_desc_sw128(p_lo + off);
-              const uint64_t dvl = umma_desc_sw128(vst + C::V_BYTES + voff);
-              umma_tf32(tmem + kPV, dph, dvh, id_o, acc);
-              umma_tf32(tmem + kPV, dph, dvl, id_o, 1u);
-              umma_tf32(tmem + kPV, dpl, dvh, id_o, 1u);
-            } else {
-              umma_bf16(tmem + kPV, dph, dvh, id_o, acc);
-            }
+        for (int kk = 0; kk < 4; ++kk) {  // 4 x 32-byte K steps over the tile's keys
+          const uint32_t acc = kk == 0 ? 0u : 1u;
+          const uint64_t dvh = umma_desc_sw128(vst + kk * 32);
+          if constexpr (kStrict) {
+            const uint64_t dvl = umma_desc_sw128(vst + C::V_BYTES + kk * 32);
+            umma_tf32_ts(dpv, pa + kk * 8, dvh, id_o, acc);             // P_hi V_hi
+            umma_tf32_ts(dpv, pa + kk * 8, dvl, id_o, 1u);              // P_hi V_lo
+            umma_tf32_ts(dpv, pa + C::BKV + kk * 8, dvh, id_o, 1u);     // P_lo V_hi
+          } else {
+            umma_bf16_ts(dpv, pa + kk * 8, dvh, id_o, acc);
           }
         }
-        umma_commit(pv_full);
+        umma_commit(&pv_full[b]);
         umma_commit(&kv_empty[u % C::KV_STAGES]);
         return true;
       };
@@ -458,7 +454,7 @@ __global__ void __launch_bounds__(192, 2)
         }
         tc_fence_after();
         const uint32_t kst = smem_u32(KV + s * C::KV_STAGE);
-        const uint32_t sbuf = tmem + kS0 + (t & 1) * C::BKV;
+        const uint32_t sbuf = tmem + C::kS + (t & 1) * C::BKV;
 #pragma unroll
         for (int kk = 0; kk < QK_STEPS; ++kk) {
           const uint32_t off = kk * 32;
@@ -494,8 +490,10 @@ __global__ void __launch_bounds__(192, 2)
     const bool jvalid = j < n;
     const float* brow = p.bias + ((size_t)h * n + (jvalid ? j : 0)) * p.ldb;
     const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    float a1 = 0.f, a2 = 0.f;  // alpha of the previous / second previous tile
     float o[32];
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] = 0.f;
@@ -525,6 +523,19 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
     };
+    // fold P V(u) (scale factor alpha_u) into the register accumulator
+    auto fold = [&](int u, float alpha) -> bool {
+      const int b = u & 1;
+      if (!mbar_wait(&pv_full[b], (u >> 1) & 1, g, 27)) return false;
+      tc_fence_after();
+      float pv[32];
+      tmem_row32(tmem + C::kPV + b * 32, warp, 0, pv);
+      tc_fence_before();
+      mbar_arrive(&pv_free[b]);
+#pragma unroll
+      for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
+      return true;
+    };
     // strict (32-key tiles): the next tile's additive terms are prefetched
     // into registers while the current tile is processed; fast (64-key
     // tiles) loads them in place to stay within 168 registers.
@@ -543,7 +554,7 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int q = 0; q < C::BKV / 32; ++q) {
         float tmp[32];
-        tmem_row32(tmem + kS0 + (t & 1) * C::BKV, warp, q * 32, tmp);
+        tmem_row32(tmem + C::kS + (t & 1) * C::BKV, warp, q * 32, tmp);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           if constexpr (kPrefetch)
@@ -554,7 +565,6 @@ __global__ void __launch_bounds__(192, 2)
       }
       tc_fence_before();
       mbar_arrive(&s_free[t & 1]);
-      // prefetch the next tile's additive terms while this tile is processed
       if constexpr (kPrefetch) {
         if (t + 1 < nt) load_add(t + 1, cadd);
       }
@@ -571,52 +581,51 @@ __global__ void __launch_bounds__(192, 2)
       }
       l_run = l_run * alpha + lsum;
       m_run = m_new;
-      // fold the previous tile's P V (its MMA also released the P buffer)
-      if (t >= 1) {
-        if (!mbar_wait(pv_full, (t - 1) & 1, g, 27)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float pv[32];
-        tmem_row32(tmem + kPV, warp, 0, pv);
-#pragma unroll
-        for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha_prev + pv[d];
+      // P V of tile t-2 is done: fold it and release its buffers (its P
+      // buffer is the one P(t) overwrites)
+      if (t >= 2 && !fold(t - 2, a2)) {
+        ok = false;
+        break;
       }
-      alpha_prev = alpha;
-      // P -> shared memory (A operand of P V, K-major, 128-byte swizzle)
+      a2 = a1;
+      a1 = alpha;
+      // P(t) -> TMEM (A operand of P V)
+      const uint32_t pdst = tmem + lane_off + C::kP + (t & 1) * C::P_COLS;
+      if constexpr (kStrict) {
+        // hi at columns [0, 32), lo = x - hi (exact) at [32, 64), 16 at a time
 #pragma unroll
-      for (int c = 0; c < C::BKV; c += 4) {
-        const int byte = (c * C::ESZ) % 128;
-        uint8_t* dst = P + (c / C::V_ATOM_KEYS) * (C::BQ * 128) + sw128_offset(t_row, byte);
-        if constexpr (kStrict) {
-          float h0, l0, h1, l1, h2, l2, h3, l3;
-          split_tf32(sv[c], h0, l0);
-          split_tf32(sv[c + 1], h1, l1);
-          split_tf32(sv[c + 2], h2, l2);
-          split_tf32(sv[c + 3], h3, l3);
-          *reinterpret_cast<float4*>(dst) = make_float4(h0, h1, h2, h3);
-          *reinterpret_cast<float4*>(dst + C::P_BYTES) = make_float4(l0, l1, l2, l3);
-        } else {
-          __nv_bfloat162 a = __floats2bfloat162_rn(sv[c], sv[c + 1]);
-          __nv_bfloat162 b = __floats2bfloat162_rn(sv[c + 2], sv[c + 3]);
-          uint2 w;
-          w.x = *reinterpret_cast<uint32_t*>(&a);
-          w.y = *reinterpret_cast<uint32_t*>(&b);
-          *reinterpret_cast<uint2*>(dst) = w;
+        for (int half = 0; half < 2; ++half) {
+          uint32_t part[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            part[e] = __float_as_uint(sv[half * 16 + e]) & 0xFFFFE000u;
+          tmem_st16(pdst + half * 16, part);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float x = sv[half * 16 + e];
+            part[e] = __float_as_uint(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+          }
+          tmem_st16(pdst + C::BKV + half * 16, part);
         }
+      } else {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          __nv_bfloat162 b2 = __floats2bfloat162_rn(sv[2 * e], sv[2 * e + 1]);
+          pk[e] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        tmem_st32(pdst, pk);
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[t & 1]);
     }
-    if (ok && nt >= 1 && mbar_wait(pv_full, (nt - 1) & 1, g, 28)) {
-      tc_fence_after();
-      float pv[32];
-      tmem_row32(tmem + kPV, warp, 0, pv);
+    if (ok && nt >= 2) ok = fold(nt - 2, a2);
+    if (ok && nt >= 1) ok = fold(nt - 1, a1);
+    if (ok) {
       const float inv = 1.0f / l_run;
 #pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] = (o[d] * alpha_prev + pv[d]) * inv;
+      for (int d = 0; d < 32; ++d) o[d] *= inv;
       if (jvalid) {
         const size_t orow = (size_t)i * n + j;
         if (kStrict || p.o_f32) {

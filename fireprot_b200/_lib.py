@@ -52,6 +52,23 @@ SIGNATURES = {
     "fpb_attention_core": (c_int, [c_void_p, c_void_p] * 3 + [c_int] * 4
                            + [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                               c_size_t, c_void_p]),
+    "fpb_trimul_shard_workspace_size": (c_size_t, [c_int]),
+    "fpb_trimul_plane_ld": (c_size_t, [c_int, c_int]),
+    "fpb_trimul_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+                              + [c_void_p] * 6 + [c_float] + [c_void_p] * 4
+                              + [c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_shard_contract": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                          c_int, c_int, c_int, c_size_t, c_int, c_int, c_void_p,
+                                          c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_shard_finish": (c_int, [c_void_p, c_int, c_int, c_void_p] + [c_void_p] * 6
+                                + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_triattn_bias_ld": (c_size_t, [c_int]),
+    "fpb_triattn_shard_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "fpb_triattn_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int] + [c_void_p] * 6
+                               + [c_float, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_triattn_shard_finish": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
+                                 + [c_void_p] * 6
+                                 + [c_float, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_registry_new": (c_void_p, []),
     "fpb_registry_free": (None, [c_void_p]),
     "fpb_registry_register": (c_int, [c_void_p, c_char_p, CAPABILITY_FN, c_void_p]),

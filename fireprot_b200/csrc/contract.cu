@@ -19,16 +19,24 @@ namespace fpb {
 template <bool kStrict>
 struct ContractCfg {
   static constexpr int BM = 128;
-  static constexpr int BN = 256;
+  static constexpr int BN_MAX = 256;
   static constexpr int KATOM = kStrict ? 32 : 64;  // elements per 128-byte row
   static constexpr int NSPLIT = kStrict ? 2 : 1;
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = BN_MAX * 128;     // room for the widest tile
   static constexpr int STAGE_BYTES = NSPLIT * (A_BYTES + B_BYTES);
   static constexpr int STAGES = kStrict ? 2 : 4;
-  static constexpr int TMEM_COLS = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Column tile: the widest of 256/192/128/64/32 that divides the B chunk
+// (a tile never straddles two ranks' rows of an all-gather buffer).
+inline int contract_bn(int chunk_rows, bool chunked) {
+  if (!chunked) return 256;
+  for (int bn : {256, 192, 128, 64, 32})
+    if (chunk_rows % bn == 0) return bn;
+  return 0;
+}
 
 template <bool kStrict, class OutT>
 __global__ void __launch_bounds__(192, 1)
@@ -50,8 +58,13 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int jt = blockIdx.x, it = blockIdx.y, ch = blockIdx.z;
-  const int n = args.n;
-  const int nk = (n + C::KATOM - 1) / C::KATOM;
+  const int bn = args.bn;
+  const uint32_t tmem_cols = bn <= 32 ? 32u : bn <= 64 ? 64u : bn <= 128 ? 128u : 256u;
+  const int nk = (args.k + C::KATOM - 1) / C::KATOM;
+  const int j0 = jt * bn;
+  const int b_chunk = j0 / args.b_chunk_rows;
+  const int b_row = j0 - b_chunk * args.b_chunk_rows;
+  const uint32_t stage_tx = C::NSPLIT * (C::A_BYTES + bn * 128);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -64,7 +77,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -87,13 +100,13 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (kb / C::STAGES) & 1;
         if (kb >= C::STAGES && !mbar_wait(&empty[s], ph ^ 1, g, 1)) break;
         uint8_t* st = smem + s * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
         const int kx = kb * C::KATOM;
         tma_load_3d(st, &ma_hi, &full[s], kx, it * C::BM, ch);
-        tma_load_3d(st + C::A_BYTES, &mb_hi, &full[s], kx, jt * C::BN, ch);
+        tma_load_4d(st + C::A_BYTES, &mb_hi, &full[s], kx, b_row, ch, b_chunk);
         if (kStrict) {
           tma_load_3d(st + C::A_BYTES + C::B_BYTES, &ma_lo, &full[s], kx, it * C::BM, ch);
-          tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &mb_lo, &full[s], kx, jt * C::BN, ch);
+          tma_load_4d(st + 2 * C::A_BYTES + C::B_BYTES, &mb_lo, &full[s], kx, b_row, ch, b_chunk);
         }
         ++issued;
       }
@@ -106,7 +119,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = kStrict ? idesc_tf32(C::BM, C::BN) : idesc_bf16(C::BM, C::BN);
+      const uint32_t idesc = kStrict ? idesc_tf32(C::BM, bn) : idesc_bf16(C::BM, bn);
       uint32_t acc = 0;
       bool ok = true;
       for (int kb = 0; kb < nk && ok; ++kb) {
@@ -155,11 +168,11 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = it * C::BM + q * 32 + lane;
 #pragma unroll 1
-      for (int cb = 0; cb < C::BN / 32; ++cb) {
+      for (int cb = 0; cb < bn / 32; ++cb) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cb * 32, r);
         tmem_ld_wait();
-        const int col0 = jt * C::BN + cb * 32;
+        const int col0 = j0 + cb * 32;
         // `out` points at column 0 of this (channel, row) run, so that
         // out + col0 addresses columns col0..col0+31 in either layout
         OutT* out;
@@ -169,8 +182,8 @@ __global__ void __launch_bounds__(192, 1)
         else
           out = reinterpret_cast<OutT*>(args.out) + (size_t)ch * args.out_channel_stride +
                 (size_t)row * args.ldo;
-        if (row < n && col0 < n) {
-          const bool vec = (col0 + 32 <= n) &&
+        if (row < args.m && col0 < args.nn) {
+          const bool vec = (col0 + 32 <= args.nn) &&
                            ((reinterpret_cast<uintptr_t>(out + col0) & 15u) == 0u);
           if (vec) {
             if constexpr (sizeof(OutT) == 4) {
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
           } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-              if (col0 + e < n) {
+              if (col0 + e < args.nn) {
                 const float v = __uint_as_float(r[e]);
                 if constexpr (sizeof(OutT) == 4)
                   out[col0 + e] = v;
@@ -214,16 +227,26 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    tmem_dealloc(tmem, tmem_cols);
   }
 }
 
 // ----------------------------------------------------------------------------
 // host launcher
 // ----------------------------------------------------------------------------
-int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream) {
-  const int n = args.n;
-  if (n <= 0 || op.channels <= 0) return kErrShape;
+int launch_contract(const ContractOperands& op, const ContractArgs& args_in, cudaStream_t stream) {
+  if (op.m <= 0 || op.nn <= 0 || op.k <= 0 || op.channels <= 0 || op.b_chunks <= 0 ||
+      op.b_chunk_rows <= 0 || (long long)op.b_chunks * op.b_chunk_rows < op.nn)
+    return kErrShape;
+  const bool chunked = op.b_chunks > 1;
+  const int bn = contract_bn(op.b_chunk_rows, chunked);
+  if (bn == 0) return kErrShape;
+  ContractArgs args = args_in;
+  args.m = op.m;
+  args.nn = op.nn;
+  args.k = op.k;
+  args.bn = bn;
+  args.b_chunk_rows = op.b_chunk_rows;
   CUtensorMap mah{}, mal{}, mbh{}, mbl{};
   const bool strict = op.strict;
   const CUtensorMapDataType dt = strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -231,19 +254,25 @@ int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaSt
   const int esz = strict ? 4 : 2;
   const int katom = 128 / esz;
   const uint64_t s1 = (uint64_t)op.ld * esz;
-  const uint64_t s2 = (uint64_t)op.channel_stride * esz;
-  if (s1 % 16 || s2 % 16) return kErrAlign;
-  bool ok = make_map_3d(&mah, op.a_hi, dt, n, n, op.channels, s1, s2, katom, 128, 1) &&
-            make_map_3d(&mbh, op.b_hi, dt, n, n, op.channels, s1, s2, katom, 256, 1);
+  const uint64_t sa2 = (uint64_t)op.a_channel_stride * esz;
+  const uint64_t sb2 = (uint64_t)op.b_channel_stride * esz;
+  const uint64_t sb3 = (uint64_t)op.b_chunk_stride * esz;
+  if (s1 % 16 || sa2 % 16 || sb2 % 16 || (chunked && sb3 % 16)) return kErrAlign;
+  // an unchunked B still uses the 4-D map with one chunk
+  const uint64_t sb3m = chunked ? sb3 : sb2 * op.channels;
+  bool ok = make_map_3d(&mah, op.a_hi, dt, op.k, op.m, op.channels, s1, sa2, katom, 128, 1) &&
+            make_map_4d(&mbh, op.b_hi, dt, op.k, op.b_chunk_rows, op.channels, op.b_chunks, s1,
+                        sb2, sb3m, katom, bn, 1, 1);
   if (strict)
-    ok = ok && make_map_3d(&mal, op.a_lo, dt, n, n, op.channels, s1, s2, katom, 128, 1) &&
-         make_map_3d(&mbl, op.b_lo, dt, n, n, op.channels, s1, s2, katom, 256, 1);
+    ok = ok && make_map_3d(&mal, op.a_lo, dt, op.k, op.m, op.channels, s1, sa2, katom, 128, 1) &&
+         make_map_4d(&mbl, op.b_lo, dt, op.k, op.b_chunk_rows, op.channels, op.b_chunks, s1, sb2,
+                     sb3m, katom, bn, 1, 1);
   else {
     mal = mah;
     mbl = mbh;
   }
   if (!ok) return kErrArg;
-  dim3 grid((n + 255) / 256, (n + 127) / 128, op.channels);
+  dim3 grid((op.nn + bn - 1) / bn, (op.m + 127) / 128, op.channels);
   if (strict) {
     auto k = contract_kernel<true, float>;
     const int smem = ContractCfg<true>::SMEM_BYTES;
@@ -372,9 +401,8 @@ extern "C" int fpb_packed_bmm(const float* a, const float* b, float* out, int ba
   }
   if (cudaGetLastError() != cudaSuccess) return kErrCuda;
   if (reset_status(workspace, stream)) return kErrCuda;
-  ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, cs, batch, strict};
+  ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, cs, cs, n, n, n, n, 1, 0, batch, strict};
   ContractArgs args{};
-  args.n = n;
   args.out = out;
   args.ldo = n;
   args.out_channel_stride = (size_t)n * n;

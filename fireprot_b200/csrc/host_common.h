@@ -81,6 +81,23 @@ inline bool make_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType 
   return r == CUDA_SUCCESS;
 }
 
+// 4-D variant: dims {d0, d1, d2, d3}, byte strides {s1, s2, s3}.
+inline bool make_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                        uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint64_t s1,
+                        uint64_t s2, uint64_t s3, uint32_t b0, uint32_t b1, uint32_t b2,
+                        uint32_t b3, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {s1, s2, s3};
+  cuuint32_t box[4] = {b0, b1, b2, b3};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Leading dimension (elements) of a padded row of n entries so that every

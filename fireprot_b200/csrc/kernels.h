@@ -6,20 +6,31 @@
 
 namespace fpb {
 
-// Operands of the batched contraction X_c = A_c B_c^T (K-major, padded rows).
+// Operands of the batched contraction X_c = A_c B_c^T (K-major, padded rows):
+// A_c is [m][k], B_c is [nn][k]. B may be a rank-major all-gather buffer:
+// b_chunks chunks of b_chunk_rows rows each, b_chunk_stride elements apart,
+// each chunk laid out [channel][row][ld]; rows of the last chunk at or past
+// nn (padding of a ragged split) are read but never stored.
 struct ContractOperands {
   const void* a_hi;
   const void* a_lo;  // strict only
   const void* b_hi;
   const void* b_lo;  // strict only
-  int ld;                 // row pitch of A/B (elements)
-  size_t channel_stride;  // elements between channels
+  int ld;                   // row pitch of A and B (elements)
+  size_t a_channel_stride;  // elements between A channels
+  size_t b_channel_stride;  // elements between B channels (within a chunk)
+  int m, nn, k;
+  int b_chunk_rows;
+  int b_chunks;
+  size_t b_chunk_stride;
   int channels;
   bool strict;
 };
 
 struct ContractArgs {
-  int n;
+  int m, nn, k;  // filled by launch_contract from the operands
+  int bn;        // column tile (32..256)
+  int b_chunk_rows;
   void* out;                  // [channels][n][ldo] fp32 or bf16 (plain layout)
   int ldo;
   size_t out_channel_stride;  // elements

@@ -31,10 +31,14 @@ constexpr float kMaskInf = 1e9f;
 // ============================================================================
 // 1. projection
 // ============================================================================
+// Pair rows of y: yrows x n (y = z_loc rows, or z^T for the unsharded
+// ending node); r0 = global index of local row 0 (pair bias rows, mask).
 struct AttnProjArgs {
   const float* z;
-  const float* mask;  // nullable
+  const float* mask;  // nullable, [n][n] global
   int n;
+  int yrows;
+  int r0;
   float eps;
   const float* ln_w;
   const float* ln_b;
@@ -47,9 +51,9 @@ struct AttnProjArgs {
   void* v_hi;
   void* v_lo;
   int ldv;          // keys pitch of v^T
-  float* bias;      // [4][n][ldb]
+  float* bias;      // [n][4][ldb] (row j outermost), global rows
   int ldb;
-  float* mbias;     // [n][ldb] or null
+  float* mbias;     // [yrows][ldb] or null
   int* status;
 };
 
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  const long long npairs = (long long)n * n;
+  const long long npairs = (long long)p.yrows * n;
   const long long p0 = (long long)blockIdx.x * 128;
 
   if (threadIdx.x == 0) {
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(192, 1)
         x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (pr < npairs) {
           const long long r = pr / n, s = pr - r * n;
-          x[u] = __ldg(z4 + (kTrans ? (s * n + r) : pr) * 32 + lane);
+          x[u] = __ldg(z4 + (kTrans ? (s * n + r) : (r * n + s)) * 32 + lane);
         }
       }
 #pragma unroll
@@ -156,9 +160,10 @@ __global__ void __launch_bounds__(192, 1)
       s = pr - r * n;
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        p.bias[((size_t)h * n + r) * p.ldb + s] = bias_tile[h * 128 + t];
+        p.bias[(((size_t)(p.r0 + r)) * kHeads + h) * p.ldb + s] = bias_tile[h * 128 + t];
       if (p.mbias) {
-        const float m = __ldg(p.mask + (kTrans ? (s * n + r) : pr));
+        const float m =
+            __ldg(p.mask + (kTrans ? ((size_t)s * n + r) : ((size_t)(p.r0 + r) * n + s)));
         p.mbias[(size_t)r * p.ldb + s] = kMaskInf * (m - 1.0f);
       }
     }
@@ -271,7 +276,7 @@ __global__ void __launch_bounds__(192, 1)
 // ============================================================================
 struct AttnCoreArgs {
   int n;
-  const float* bias;   // [4][n][ldb]
+  const float* bias;   // [n][4][ldb] (row j outermost)
   const float* mbias;  // [rows][ldb] or null
   int ldb;
   void* o;             // [rows*n][128] fp32 (strict or o_f32) / bf16 (fast)
@@ -488,7 +493,7 @@ __global__ void __launch_bounds__(192, 2)
     const int t_row = warp * 32 + lane;  // TMEM lane / query row in tile
     const int j = jt * C::BQ + t_row;
     const bool jvalid = j < n;
-    const float* brow = p.bias + ((size_t)h * n + (jvalid ? j : 0)) * p.ldb;
+    const float* brow = p.bias + ((size_t)(jvalid ? j : 0) * kHeads + h) * p.ldb;
     const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
@@ -666,6 +671,7 @@ struct AttnOutArgs {
   float* z;
   float* delta;  // when non-null: write the update here and leave z unchanged
   int n;
+  int rows;      // pair rows of y owned by this call (n unsharded)
   float eps;
   const float* ln_w;
   const float* ln_b;
@@ -705,7 +711,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  const long long npairs = (long long)n * n;
+  const long long npairs = (long long)p.rows * n;
   const long long p0 = (long long)blockIdx.x * 128;
 
   if (threadIdx.x == 0) {
@@ -923,6 +929,9 @@ __global__ void __launch_bounds__(192, 1)
 // ============================================================================
 // host
 // ============================================================================
+// Workspace of one call: packed weights, q/k/v^T, mask bias, attention
+// output, and (unsharded calls only) the pair bias. `rows` = pair rows of y
+// owned by the call (n when unsharded).
 template <class Alloc>
 struct TriAttnPlan {
   void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
@@ -930,7 +939,7 @@ struct TriAttnPlan {
   void *v_hi = nullptr, *v_lo = nullptr, *o = nullptr;
   float *bias = nullptr, *mbias = nullptr;
   int ldv = 0, ldb = 0;
-  void plan(Alloc& al, int n, bool strict, bool with_mask) {
+  void plan(Alloc& al, int n, int rows, bool strict, bool with_mask, bool own_bias) {
     auto take = [&](size_t c) -> void* {
       return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
     };
@@ -938,7 +947,7 @@ struct TriAttnPlan {
     if (strict) wp_lo = take(384 * 128);
     wo_hi = take(256 * 128);
     if (strict) wo_lo = take(256 * 128);
-    const size_t qk = (size_t)n * n * 128;
+    const size_t qk = (size_t)rows * n * 128;
     q_hi = take(qk);
     k_hi = take(qk);
     if (strict) {
@@ -946,83 +955,55 @@ struct TriAttnPlan {
       k_lo = take(qk);
     }
     ldv = padded_ld(n, strict ? 4 : 2);
-    const size_t vc = (size_t)n * kHeads * 32 * ldv;
+    const size_t vc = (size_t)rows * kHeads * 32 * ldv;
     v_hi = take(vc);
     if (strict) v_lo = take(vc);
     ldb = padded_ld(n, 4);
-    bias = al.template take<float>((size_t)kHeads * n * ldb);
-    if (with_mask) mbias = al.template take<float>((size_t)n * ldb);
-    o = take((size_t)n * n * 128);
+    if (own_bias) bias = al.template take<float>((size_t)n * kHeads * ldb);
+    if (with_mask) mbias = al.template take<float>((size_t)rows * ldb);
+    o = take((size_t)rows * n * 128);
   }
 };
 
-}  // namespace fpb
-
-using namespace fpb;
-
-extern "C" size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head_dim,
-                                             int precision, int with_mask) {
-  if (n <= 0 || c_z != 128 || heads != kHeads || head_dim != kHeadDim) return 0;
-  if (precision != 0 && precision != 1) return 0;
-  WsCounter cnt;
-  TriAttnPlan<WsCounter> pl;
-  pl.plan(cnt, n, precision == 0, with_mask != 0);
-  return cnt.used;
-}
-
-extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n, int c_z,
-                           int heads, int head_dim,
-                           const float* ln_w, const float* ln_b, const float* w_q,
-                           const float* w_k, const float* w_v, const float* w_bias,
-                           const float* w_g, const float* b_g, const float* w_o,
-                           const float* b_o, float eps, int starting, int precision,
-                           void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  if (!z || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias || !w_g || !w_o || !workspace)
-    return kErrArg;
-  if (c_z != 128 || heads != kHeads || head_dim != kHeadDim || n <= 0) return kErrShape;
-  if (precision != 0 && precision != 1) return kErrArg;
-  if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
-    return kErrAlign;
-  if (delta_out && !aligned16(delta_out)) return kErrAlign;
-  const bool strict = precision == 0;
-  const bool with_mask = mask != nullptr;
-  if (workspace_bytes <
-      fpb_triattn_workspace_size(n, c_z, heads, head_dim, precision, with_mask ? 1 : 0))
-    return kErrWorkspace;
-  WsCursor cur(workspace, workspace_bytes);
-  TriAttnPlan<WsCursor> pl;
-  pl.plan(cur, n, strict, with_mask);
-  if (!cur.ok) return kErrWorkspace;
-  int* status = static_cast<int*>(workspace);
-  if (reset_status(workspace, stream)) return kErrCuda;
+// phase 1: LN + q/k/v projection of the call's rows, pair bias of those rows
+// (written at their global rows of `bias`), mask bias
+template <class Plan>
+int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int n, int rows,
+                     int r0, bool trans, const float* ln_w, const float* ln_b, const float* w_q,
+                     const float* w_k, const float* w_v, const float* w_bias, float eps,
+                     float* bias, bool strict, int* status, cudaStream_t stream) {
   int st;
   if ((st = pack_weights(PackSrc{{w_q, w_k, w_v, nullptr}, 3, 128}, pl.wp_hi, pl.wp_lo, strict,
                          stream)))
     return st;
+  CUtensorMap mph, mpl;
+  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl)) return kErrArg;
+  const long long npairs = (long long)rows * n;
+  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  AttnProjArgs pa{z_loc, mask, n, rows, r0, eps, ln_w, ln_b, w_bias,
+                  1.0f / sqrtf((float)kHeadDim), pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi,
+                  pl.v_lo, pl.ldv, bias, pl.ldb, pl.mbias, status};
+  const int smem = strict ? attn_proj_smem_bytes<true>() : attn_proj_smem_bytes<false>();
+  auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
+                  : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
+  return launch_status();
+}
+
+// phase 2: attention core over the call's rows (keys = all n) + gate, output
+// projection and residual (or delta) on those rows
+template <class Plan>
+int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, int rows,
+                       bool trans, const float* bias, const float* ln_w, const float* ln_b,
+                       const float* w_g, const float* b_g, const float* w_o, const float* b_o,
+                       float eps, bool strict, int* status, cudaStream_t stream) {
+  int st;
   if ((st = pack_weights(PackSrc{{w_g, w_o, nullptr, nullptr}, 2, 128}, pl.wo_hi, pl.wo_lo,
                          strict, stream)))
     return st;
-  CUtensorMap mph, mpl, moh, mol;
-  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl) ||
-      !make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol))
-    return kErrArg;
-  const bool trans = !starting;
-  const long long npairs = (long long)n * n;
-  const unsigned tiles = (unsigned)((npairs + 127) / 128);
-
-  // 1. projection
-  AttnProjArgs pa{z, mask, n, eps, ln_w, ln_b, w_bias, 1.0f / sqrtf((float)kHeadDim),
-                  pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, pl.ldv, pl.bias, pl.ldb,
-                  pl.mbias, status};
-  {
-    const int smem = strict ? attn_proj_smem_bytes<true>() : attn_proj_smem_bytes<false>();
-    auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
-                    : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
-    if ((st = launch_status())) return st;
-  }
-  // 2. attention core
+  CUtensorMap moh, mol;
+  if (!make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol)) return kErrArg;
   {
     const int esz = strict ? 4 : 2;
     const CUtensorMapDataType dt =
@@ -1030,7 +1011,7 @@ extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n,
     const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const uint64_t rowb = 32ull * esz;
     CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
-    const uint64_t nh = (uint64_t)n * kHeads;
+    const uint64_t nh = (uint64_t)rows * kHeads;
     const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
     bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
               make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
@@ -1047,8 +1028,8 @@ extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n,
       mvl = mvh;
     }
     if (!ok) return kErrArg;
-    AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, pl.o, status, 0};
-    dim3 grid((n + 127) / 128, kHeads, n);
+    AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0};
+    dim3 grid((n + 127) / 128, kHeads, rows);
     if (strict) {
       auto k = attn_core_kernel<true>;
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
@@ -1062,17 +1043,123 @@ extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n,
     }
     if ((st = launch_status())) return st;
   }
-  // 3. gate + output projection + residual
-  AttnOutArgs oa{z, delta_out, n, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
-  {
-    const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
-    auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
-                    : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
-    if ((st = launch_status())) return st;
-  }
-  return kOk;
+  AttnOutArgs oa{z_loc, delta_out, n, rows, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
+  const long long npairs = (long long)rows * n;
+  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
+  auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
+                  : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
+  return launch_status();
+}
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" size_t fpb_triattn_workspace_size(int n, int c_z, int heads, int head_dim,
+                                             int precision, int with_mask) {
+  if (n <= 0 || c_z != 128 || heads != kHeads || head_dim != kHeadDim) return 0;
+  if (precision != 0 && precision != 1) return 0;
+  WsCounter cnt;
+  TriAttnPlan<WsCounter> pl;
+  pl.plan(cnt, n, n, precision == 0, with_mask != 0, true);
+  return cnt.used;
+}
+
+extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n, int c_z,
+                           int heads, int head_dim, const float* ln_w, const float* ln_b,
+                           const float* w_q, const float* w_k, const float* w_v,
+                           const float* w_bias, const float* w_g, const float* b_g,
+                           const float* w_o, const float* b_o, float eps, int starting,
+                           int precision, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  if (!z || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias || !w_g || !w_o || !workspace)
+    return kErrArg;
+  if (c_z != 128 || heads != kHeads || head_dim != kHeadDim || n <= 0) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(z) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
+    return kErrAlign;
+  if (delta_out && !aligned16(delta_out)) return kErrAlign;
+  const bool strict = precision == 0;
+  const bool with_mask = mask != nullptr;
+  if (workspace_bytes <
+      fpb_triattn_workspace_size(n, c_z, heads, head_dim, precision, with_mask ? 1 : 0))
+    return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  TriAttnPlan<WsCursor> pl;
+  pl.plan(cur, n, n, strict, with_mask, true);
+  if (!cur.ok) return kErrWorkspace;
+  int* status = static_cast<int*>(workspace);
+  if (reset_status(workspace, stream)) return kErrCuda;
+  const bool trans = !starting;
+  int st = triattn_proj_run(pl, z, mask, n, n, 0, trans, ln_w, ln_b, w_q, w_k, w_v, w_bias, eps,
+                            pl.bias, strict, status, stream);
+  if (st) return st;
+  return triattn_finish_run(pl, z, delta_out, n, n, trans, pl.bias, ln_w, ln_b, w_g, b_g, w_o,
+                            b_o, eps, strict, status, stream);
+}
+
+// ---------------------------------------------------------------- row-sharded phases
+extern "C" size_t fpb_triattn_bias_ld(int n) { return (size_t)padded_ld(n, 4); }
+
+extern "C" size_t fpb_triattn_shard_workspace_size(int n, int rows, int precision,
+                                                   int with_mask) {
+  if (n <= 0 || rows <= 0 || (precision != 0 && precision != 1)) return 0;
+  WsCounter cnt;
+  TriAttnPlan<WsCounter> pl;
+  pl.plan(cnt, n, rows, precision == 0, with_mask != 0, false);
+  return cnt.used;
+}
+
+// Starting-node form on rows [r0, r0 + rows) of z (z_loc = those rows).
+// Writes this rank's rows of the j-major pair bias `bias_full` ([n][4][ldb],
+// ldb = fpb_triattn_bias_ld(n)); the caller all-gathers it before _finish.
+extern "C" int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int n, int rows,
+                                      int r0, const float* ln_w, const float* ln_b,
+                                      const float* w_q, const float* w_k, const float* w_v,
+                                      const float* w_bias, float eps, float* bias_full,
+                                      int precision, void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream) {
+  if (!z_loc || !bias_full || !workspace || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias)
+    return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
+  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
+    return kErrAlign;
+  const bool strict = precision == 0;
+  const bool with_mask = mask != nullptr;
+  if (workspace_bytes < fpb_triattn_shard_workspace_size(n, rows, precision, with_mask))
+    return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  TriAttnPlan<WsCursor> pl;
+  pl.plan(cur, n, rows, strict, with_mask, false);
+  if (reset_status(workspace, stream)) return kErrCuda;
+  return triattn_proj_run(pl, z_loc, mask, n, rows, r0, false, ln_w, ln_b, w_q, w_k, w_v, w_bias,
+                          eps, bias_full, strict, static_cast<int*>(workspace), stream);
+}
+
+extern "C" int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, int rows,
+                                        int with_mask, const float* bias_full, const float* ln_w,
+                                        const float* ln_b, const float* w_g, const float* b_g,
+                                        const float* w_o, const float* b_o, float eps,
+                                        int precision, void* workspace, size_t workspace_bytes,
+                                        cudaStream_t stream) {
+  if (!z_loc || !bias_full || !workspace || !ln_w || !ln_b || !w_g || !w_o) return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (n <= 0 || rows <= 0) return kErrShape;
+  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
+    return kErrAlign;
+  if (delta_out && !aligned16(delta_out)) return kErrAlign;
+  const bool strict = precision == 0;
+  if (workspace_bytes < fpb_triattn_shard_workspace_size(n, rows, precision, with_mask))
+    return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  TriAttnPlan<WsCursor> pl;
+  pl.plan(cur, n, rows, strict, with_mask != 0, false);
+  return triattn_finish_run(pl, z_loc, delta_out, n, rows, false, bias_full, ln_w, ln_b, w_g, b_g,
+                            w_o, b_o, eps, strict, static_cast<int*>(workspace), stream);
 }
 
 // ============================================================================
@@ -1136,7 +1223,7 @@ __global__ void pack_vt_kernel(const float* __restrict__ src, long long s0, long
   }
 }
 
-// triangle bias [1, H, N, N] -> [h][j][ldb]; mask bias [B, 1, 1, N] -> [b][ldb]
+// triangle bias [1, H, N, N] -> [j][h][ldb]; mask bias [B, 1, 1, N] -> [b][ldb]
 __global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, long long t2,
                                  long long t3, const float* __restrict__ mb, long long m0,
                                  long long m3, int batch, int n, int ldb, float* bias,
@@ -1150,7 +1237,7 @@ __global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, lon
       const long long hj = e / n;
       const int j = (int)(hj % n);
       const int h = (int)(hj / n);
-      bias[((size_t)h * n + j) * ldb + k] = tb[h * t1 + j * t2 + k * t3];
+      bias[((size_t)j * kHeads + h) * ldb + k] = tb[h * t1 + j * t2 + k * t3];
     } else {
       const long long f = e - nb;
       const int k = (int)(f % n);

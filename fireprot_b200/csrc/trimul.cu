@@ -21,10 +21,14 @@
 
 namespace fpb {
 
+// y coordinates: y is a yrows x ycols grid of pair rows; pair (r, s) of y
+// is z_loc[r][s] (outgoing) or z_loc[s][r] (incoming, z read transposed),
+// where z_loc is the [rows][zcols] block of z this call owns and r0 its first
+// global row (for the [N][N] mask).
 struct TriMulProjArgs {
   const float* z;
-  const float* mask;  // nullable
-  int n;
+  const float* mask;  // nullable, [N][N] global
+  int yrows, ycols, zcols, r0;
   float eps;
   const float* ln_w;
   const float* ln_b;
@@ -64,8 +68,7 @@ __global__ void __launch_bounds__(192, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = p.n;
-  const long long npairs = (long long)n * n;
+  const long long npairs = (long long)p.yrows * p.ycols;
   const long long p0 = (long long)blockIdx.x * 128;
 
   if (threadIdx.x == 0) {
@@ -105,8 +108,8 @@ __global__ void __launch_bounds__(192, 1)
         const long long pr = p0 + row;
         x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (pr < npairs) {
-          const long long r = pr / n, s = pr - r * n;
-          const long long src = kTrans ? (s * n + r) : pr;
+          const long long r = pr / p.ycols, s = pr - r * p.ycols;
+          const long long src = kTrans ? (s * p.zcols + r) : (r * p.zcols + s);
           x[u] = __ldg(z4 + src * 32 + lane);
         }
       }
@@ -127,9 +130,10 @@ __global__ void __launch_bounds__(192, 1)
     long long r = 0, s = 0;
     float m = 1.f;
     if (valid) {
-      r = pr / n;
-      s = pr - r * n;
-      if (p.mask) m = __ldg(p.mask + (kTrans ? (s * n + r) : pr));
+      r = pr / p.ycols;
+      s = pr - r * p.ycols;
+      if (p.mask)
+        m = __ldg(p.mask + (kTrans ? ((p.r0 + s) * p.zcols + r) : ((p.r0 + r) * p.zcols + s)));
     }
     const size_t pos = (size_t)r * p.ld + (size_t)s;
     if (mbar_wait(done, 0, g, 3)) {
@@ -480,6 +484,69 @@ bool make_weight_maps(const void* hi, const void* lo, int rows, bool strict, CUt
 }
 
 // workspace plan (shared by the size query and the call)
+// ----------------------------------------------------------------------------
+// phases (shared by the fused single-GPU call and the row-sharded calls)
+// ----------------------------------------------------------------------------
+int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols, int zcols,
+                    int r0, bool transposed, const float* ln_w, const float* ln_b,
+                    const float* w_a_p, const float* w_a_g, const float* w_b_p,
+                    const float* w_b_g, float eps, void* a_hi, void* a_lo, void* b_hi,
+                    void* b_lo, int ld, int plane_rows, bool strict, void* wp_hi, void* wp_lo,
+                    int* status, cudaStream_t stream) {
+  int st = pack_weights(PackSrc{{w_a_p, w_a_g, w_b_p, w_b_g}, 4, 128}, wp_hi, wp_lo, strict,
+                        stream);
+  if (st) return st;
+  CUtensorMap mph, mpl;
+  if (!make_weight_maps(wp_hi, wp_lo, 512, strict, &mph, &mpl)) return kErrArg;
+  const long long npairs = (long long)yrows * ycols;
+  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0, eps, ln_w, ln_b, a_hi, a_lo, b_hi,
+                    b_lo, ld, (size_t)plane_rows * ld, status};
+  const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
+  auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
+                  : (transposed ? trimul_proj_kernel<false, true>
+                                : trimul_proj_kernel<false, false>);
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  FPB_LAUNCH("trimul_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
+  return launch_status();
+}
+
+int trimul_finish_run(float* z_loc, int n, int rows, const void* x_blocked, const float* ln_in_w,
+                      const float* ln_in_b, const float* w_g, const float* ln_out_w,
+                      const float* ln_out_b, const float* w_z, float eps, bool add, bool strict,
+                      void* wo_hi, void* wo_lo, int* status, cudaStream_t stream) {
+  int st = pack_weights(PackSrc{{w_g, w_z, nullptr, nullptr}, 2, 128}, wo_hi, wo_lo, strict,
+                        stream);
+  if (st) return st;
+  CUtensorMap moh, mol;
+  if (!make_weight_maps(wo_hi, wo_lo, 256, strict, &moh, &mol)) return kErrArg;
+  const int njb = (n + 127) / 128;
+  TriMulOutArgs oa{z_loc, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, x_blocked, njb,
+                   add ? 1 : 0, status};
+  const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
+  auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const unsigned out_tiles = (unsigned)(rows * njb);
+  FPB_LAUNCH("trimul_out", stream, k<<<out_tiles, 192, smem, stream>>>(moh, mol, oa));
+  return launch_status();
+}
+
+int trimul_contract_run(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
+                        const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
+                        int b_chunks, size_t b_chunk_stride, int k, int ld, void* x_blocked,
+                        bool strict, int* status, cudaStream_t stream) {
+  ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, (size_t)a_plane_rows * ld,
+                      (size_t)b_chunk_rows * ld,
+                      m, nn, k, b_chunk_rows, b_chunks, b_chunk_stride, 128, strict};
+  ContractArgs ca{};
+  ca.out = x_blocked;
+  ca.out_bf16 = strict ? 0 : 1;
+  ca.status = status;
+  ca.blocked = 1;
+  ca.njb = (nn + 127) / 128;
+  return launch_contract(op, ca, stream);
+}
+
 template <class Alloc>
 struct TriMulPlan {
   void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
@@ -506,6 +573,16 @@ struct TriMulPlan {
     x = take((size_t)n * njb * 128 * 128);  // blocked [n][njb][128 c][128 j]
   }
 };
+
+// packed weights of one phase call (projection: 512 rows; finish: 256 rows)
+template <class Alloc>
+void plan_weights(Alloc& al, bool strict, int rows, void** hi, void** lo) {
+  auto take = [&](size_t c) -> void* {
+    return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
+  };
+  *hi = take((size_t)rows * 128);
+  *lo = strict ? take((size_t)rows * 128) : nullptr;
+}
 
 }  // namespace fpb
 
@@ -540,49 +617,101 @@ extern "C" int fpb_trimul(float* z, const float* mask, int n, int c_z, const flo
   if (!cur.ok) return kErrWorkspace;
   int* status = static_cast<int*>(workspace);
   if (reset_status(workspace, stream)) return kErrCuda;
+  int st = trimul_proj_run(z, mask, n, n, n, 0, !outgoing, ln_in_w, ln_in_b, w_a_p, w_a_g, w_b_p,
+                           w_b_g, eps, pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo, pl.ld, n, strict,
+                           pl.wp_hi, pl.wp_lo, status, stream);
+  if (st) return st;
+  st = trimul_contract_run(pl.a_hi, pl.a_lo, n, n, pl.b_hi, pl.b_lo, n, n, 1, 0, n, pl.ld, pl.x,
+                           strict, status, stream);
+  if (st) return st;
+  return trimul_finish_run(z, n, n, pl.x, ln_in_w, ln_in_b, w_g, ln_out_w, ln_out_b, w_z, eps,
+                           add != 0, strict, pl.wo_hi, pl.wo_lo, status, stream);
+}
 
-  int st = pack_weights(PackSrc{{w_a_p, w_a_g, w_b_p, w_b_g}, 4, 128}, pl.wp_hi, pl.wp_lo, strict,
-                        stream);
-  if (st) return st;
-  st = pack_weights(PackSrc{{w_g, w_z, nullptr, nullptr}, 2, 128}, pl.wo_hi, pl.wo_lo, strict,
-                    stream);
-  if (st) return st;
-  CUtensorMap mph, mpl, moh, mol;
-  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 512, strict, &mph, &mpl) ||
-      !make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol))
+// ---------------------------------------------------------------- row-sharded phases
+extern "C" size_t fpb_trimul_shard_workspace_size(int precision) {
+  if (precision != 0 && precision != 1) return 0;
+  WsCounter cnt;
+  void *h, *l;
+  plan_weights(cnt, precision == 0, 512, &h, &l);
+  return cnt.used;
+}
+
+extern "C" size_t fpb_trimul_plane_ld(int cols, int precision) {
+  return (size_t)padded_ld(cols, precision == 0 ? 4 : 2);
+}
+
+extern "C" int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int n, int rows,
+                                     int r0, int transposed, const float* ln_in_w,
+                                     const float* ln_in_b, const float* w_a_p, const float* w_a_g,
+                                     const float* w_b_p, const float* w_b_g, float eps, void* a_hi,
+                                     void* a_lo, void* b_hi, void* b_lo, int ld, int plane_rows,
+                                     int precision, void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream) {
+  if (!z_loc || !a_hi || !b_hi || !workspace || !ln_in_w || !ln_in_b || !w_a_p || !w_a_g ||
+      !w_b_p || !w_b_g)
     return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (strict && (!a_lo || !b_lo)) return kErrArg;
+  if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
+  const int yrows = transposed ? n : rows;
+  const int ycols = transposed ? rows : n;
+  if (plane_rows < yrows) return kErrShape;
+  if (ld < ycols || ld % (strict ? 32 : 64)) return kErrAlign;
+  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_in_w) || !aligned16(ln_in_b))
+    return kErrAlign;
+  if (workspace_bytes < fpb_trimul_shard_workspace_size(precision)) return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  void *wh, *wl;
+  plan_weights(cur, strict, 512, &wh, &wl);
+  if (reset_status(workspace, stream)) return kErrCuda;
+  // outgoing: y = z_loc (rows x n); incoming: y = z_loc^T (n x rows)
+  return trimul_proj_run(z_loc, mask, yrows, ycols, n, r0, transposed != 0, ln_in_w, ln_in_b,
+                         w_a_p, w_a_g, w_b_p, w_b_g, eps, a_hi, a_lo, b_hi, b_lo, ld, plane_rows,
+                         strict, wh, wl, static_cast<int*>(workspace), stream);
+}
 
-  const long long npairs = (long long)n * n;
-  const unsigned tiles = (unsigned)((npairs + 127) / 128);
-  TriMulProjArgs pa{z, mask, n, eps, ln_in_w, ln_in_b, pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo,
-                    pl.ld, pl.cs, status};
-  {
-    const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
-    auto k = strict ? (outgoing ? trimul_proj_kernel<true, false> : trimul_proj_kernel<true, true>)
-                    : (outgoing ? trimul_proj_kernel<false, false>
-                                : trimul_proj_kernel<false, true>);
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    FPB_LAUNCH("trimul_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
-    if ((st = launch_status())) return st;
-  }
-  ContractOperands op{pl.a_hi, pl.a_lo, pl.b_hi, pl.b_lo, pl.ld, pl.cs, 128, strict};
-  ContractArgs ca{};
-  ca.n = n;
-  ca.out = pl.x;
-  ca.out_bf16 = strict ? 0 : 1;
-  ca.status = status;
-  ca.blocked = 1;
-  ca.njb = pl.njb;
-  if ((st = launch_contract(op, ca, stream))) return st;
-  TriMulOutArgs oa{z, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, pl.x, pl.njb,
-                   add ? 1 : 0, status};
-  {
-    const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
-    auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    const unsigned out_tiles = (unsigned)(n * pl.njb);
-    FPB_LAUNCH("trimul_out", stream, k<<<out_tiles, 192, smem, stream>>>(moh, mol, oa));
-    if ((st = launch_status())) return st;
-  }
-  return kOk;
+extern "C" int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m,
+                                         int a_plane_rows, const void* b_hi, const void* b_lo,
+                                         int nn, int b_chunk_rows, int b_chunks,
+                                         size_t b_chunk_stride, int k, int ld, void* x_blocked,
+                                         int precision, void* workspace, size_t workspace_bytes,
+                                         cudaStream_t stream) {
+  if (!a_hi || !b_hi || !x_blocked || !workspace) return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (strict && (!a_lo || !b_lo)) return kErrArg;
+  if (m <= 0 || nn <= 0 || k <= 0 || b_chunk_rows <= 0 || b_chunks <= 0 || a_plane_rows < m ||
+      (long long)b_chunk_rows * b_chunks < nn)
+    return kErrShape;
+  if (workspace_bytes < kWsHeader || !aligned16(workspace)) return kErrWorkspace;
+  if (reset_status(workspace, stream)) return kErrCuda;
+  return trimul_contract_run(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows, b_chunks,
+                             b_chunk_stride, k, ld, x_blocked, strict,
+                             static_cast<int*>(workspace), stream);
+}
+
+extern "C" int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked,
+                                       const float* ln_in_w, const float* ln_in_b,
+                                       const float* w_g, const float* ln_out_w,
+                                       const float* ln_out_b, const float* w_z, float eps, int add,
+                                       int precision, void* workspace, size_t workspace_bytes,
+                                       cudaStream_t stream) {
+  if (!z_loc || !x_blocked || !workspace || !ln_in_w || !ln_in_b || !w_g || !ln_out_w ||
+      !ln_out_b || !w_z)
+    return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (n <= 0 || rows <= 0) return kErrShape;
+  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_in_w) || !aligned16(ln_in_b))
+    return kErrAlign;
+  const bool strict = precision == 0;
+  if (workspace_bytes < fpb_trimul_shard_workspace_size(precision)) return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  void *wh, *wl;
+  plan_weights(cur, strict, 256, &wh, &wl);
+  if (reset_status(workspace, stream)) return kErrCuda;
+  return trimul_finish_run(z_loc, n, rows, x_blocked, ln_in_w, ln_in_b, w_g, ln_out_w, ln_out_b,
+                           w_z, eps, add != 0, strict, wh, wl, static_cast<int*>(workspace),
+                           stream);
 }

@@ -1,0 +1,329 @@
+"""Row-sharded pair stack: one process per GPU, NCCL between the phases.
+
+Rank ``r`` of ``W`` owns rows ``[r0, r0 + rows)`` of the pair tensor
+``z [n, n, 128]``, held in a ``[chunk, n, 128]`` buffer. ``chunk`` is the
+common padded row count (``ceil(n / W)`` rounded up to 32 rows, so that a
+rank's rows are whole column tiles of the outgoing contraction); the last
+ranks may hold fewer valid rows, or none.
+
+Every operator of the block needs at most one exchange step (the reference
+runs each operator on one device; its only multi-device code is the outer
+batch split of ``python/fireprot/backends/amd/two_gcd_attention.py:53-101``):
+
+* TriMul outgoing ``x_ij = sum_k a_ik b_jk``: ``a`` rows are local, every
+  ``j`` needs all rows of ``b`` -> all-gather of the projected ``b`` planes,
+  then the local rows of ``x``.
+* TriMul incoming ``x_ij = sum_k a_ki b_kj``: the rank holds rows ``k`` of
+  ``a`` and ``b`` -> partial contraction over its ``k`` for all ``(i, j)``,
+  reduce-scatter of ``x`` by rows.
+* TriAttn starting node: q/k/v/gate of row ``i`` come from row ``i``; only
+  the pair bias ``b[h, j, k]`` spans all rows -> all-gather of the rank's
+  rows of the j-major bias.
+* TriAttn ending node: the starting form on ``z^T`` -> all-to-all transpose
+  of ``z``, starting form, all-to-all transpose back.
+* Transition: per position, local.
+
+The phase kernels are the single-GPU kernels run on row ranges
+(``fpb_trimul_shard_*``, ``fpb_triattn_shard_*``, ``fpb_transition``);
+``CudaPhases`` is the only compute provider in the package. ``Comm`` wraps
+the three collectives so the orchestration is independent of the transport.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops
+
+ROW_ALIGN = 32
+
+
+@dataclass(frozen=True)
+class RowShard:
+    """Rows of the pair tensor owned by one rank."""
+    n: int
+    world: int
+    rank: int
+
+    @property
+    def chunk(self) -> int:
+        per = -(-self.n // self.world)
+        return -(-per // ROW_ALIGN) * ROW_ALIGN
+
+    @property
+    def r0(self) -> int:
+        return min(self.rank * self.chunk, self.n)
+
+    @property
+    def rows(self) -> int:
+        return max(0, min(self.n, (self.rank + 1) * self.chunk) - self.r0)
+
+
+def shard_plan(n: int, world: int, rank: int) -> RowShard:
+    if n <= 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad shard plan n={n} world={world} rank={rank}")
+    return RowShard(n, world, rank)
+
+
+def local_rows(z: torch.Tensor, shard: RowShard) -> torch.Tensor:
+    """This rank's padded ``[chunk, n, c]`` slice of a full pair tensor."""
+    out = z.new_zeros((shard.chunk,) + tuple(z.shape[1:]))
+    out[:shard.rows] = z[shard.r0:shard.r0 + shard.rows]
+    return out
+
+
+class DistComm:
+    """Collectives of a ``torch.distributed`` process group (NCCL on GPUs).
+
+    Buffers are contiguous and rank-major along their first dimension; they
+    are passed flat, since only their sizes matter to the exchange."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self._dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        self._dist.all_gather_into_tensor(out.view(-1), inp.reshape(-1), group=self.group)
+
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        self._dist.reduce_scatter_tensor(out.view(-1), inp.reshape(-1),
+                                         op=self._dist.ReduceOp.SUM, group=self.group)
+
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        self._dist.all_to_all_single(out.view(-1), inp.reshape(-1), group=self.group)
+
+
+def gather_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
+    """Full ``[n, n, c]`` pair tensor on every rank (tests and checkpoints)."""
+    full = z_loc.new_empty((shard.world * shard.chunk,) + tuple(z_loc.shape[1:]))
+    comm.all_gather(full, z_loc.contiguous())
+    return full[:shard.n]
+
+
+def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
+    """Rows of ``z^T`` owned by this rank: ``zt[i, j] = z[j, i]`` for the
+    rank's ``i``. One all-to-all of ``[chunk, chunk, c]`` blocks; padded
+    columns travel as zeros and padded rows of the result are zero."""
+    w, c, n = shard.world, shard.chunk, shard.n
+    ch = z_loc.shape[-1]
+    zp = z_loc.new_zeros(c, w * c, ch)
+    zp[:, :n] = z_loc
+    send = zp.view(c, w, c, ch).permute(1, 0, 2, 3).contiguous()  # [dest][my i][dest j]
+    recv = torch.empty_like(send)
+    comm.all_to_all(recv, send)  # [src][src rows][my cols]
+    return recv.permute(2, 0, 1, 3).reshape(c, w * c, ch)[:, :n].contiguous()
+
+
+class CudaPhases:
+    """Phase kernels of the row-sharded operators (C-ABI entry points).
+
+    Buffers are allocated with torch on the current stream; every workspace
+    used is kept so ``check()`` can read the device status words.
+    """
+
+    def __init__(self, precision="strict", eps: float = 1e-5):
+        self.p = ops.precision_code(precision)
+        self.strict = self.p == ops.STRICT
+        self.eps = float(eps)
+        self.lib = _lib.load()
+        self._ws = []
+
+    # ---------------------------------------------------------------- helpers
+    def _dtype(self):
+        return torch.float32 if self.strict else torch.bfloat16
+
+    def _planes(self, rows, ld, device):
+        n_planes = 2 if self.strict else 1
+        return [torch.empty(128, rows, ld, dtype=self._dtype(), device=device)
+                for _ in range(n_planes)]
+
+    def _ws_take(self, nbytes, device):
+        ws = ops.workspace(nbytes, device)
+        self._ws.append(ws)
+        return ws
+
+    @staticmethod
+    def _ptr(t):
+        return 0 if t is None else t.data_ptr()
+
+    def _pair(self, planes):
+        return planes[0].data_ptr(), (planes[1].data_ptr() if self.strict else 0)
+
+    def check(self) -> None:
+        """Raise if any wait of any phase kernel gave up (reads status words)."""
+        for ws in self._ws:
+            st = ops.workspace_status(ws)
+            if st:
+                raise RuntimeError(f"phase kernel status {st}")
+        self._ws.clear()
+
+    # ---------------------------------------------------------------- TriMul
+    def trimul_proj(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
+        """Gated, masked a/b planes of the rank's rows: outgoing ``[128][chunk][ld(n)]``
+        (the b planes are the all-gather chunk), incoming ``[128][n][ld(rows)]``."""
+        n, rows = shard.n, shard.rows
+        dev = z_loc.device
+        if outgoing:
+            ld = int(self.lib.fpb_trimul_plane_ld(n, self.p))
+            plane_rows = shard.chunk
+        else:
+            if rows == 0:
+                return None, None, 0
+            ld = int(self.lib.fpb_trimul_plane_ld(rows, self.p))
+            plane_rows = n
+        a, b = self._planes(plane_rows, ld, dev), self._planes(plane_rows, ld, dev)
+        if rows == 0:
+            return a, b, ld
+        ws = self._ws_take(self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
+        keys = ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p", "w_b_g")
+        wt = [w[k].contiguous() for k in keys]
+        _lib.check(self.lib.fpb_trimul_shard_proj(
+            z_loc.data_ptr(), self._ptr(mask), n, rows, shard.r0, int(not outgoing),
+            *[t.data_ptr() for t in wt], self.eps, *self._pair(a), *self._pair(b), ld, plane_rows,
+            self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)), "fpb_trimul_shard_proj")
+        return a, b, ld
+
+    def new_x(self, rows: int, shard: RowShard, device):
+        njb = (shard.n + 127) // 128
+        return torch.empty(rows, njb, 128, 128, dtype=self._dtype(), device=device)
+
+    def _contract(self, a, m, a_plane_rows, b, nn, b_chunk_rows, b_chunks, b_chunk_stride, k,
+                  ld, x, device):
+        ws = self._ws_take(256, device)
+        _lib.check(self.lib.fpb_trimul_shard_contract(
+            *self._pair(a), m, a_plane_rows, *self._pair(b), nn, b_chunk_rows, b_chunks,
+            b_chunk_stride, k, ld, x.data_ptr(), self.p, ws.data_ptr(), ws.numel(),
+            ops._stream_ptr(device)), "fpb_trimul_shard_contract")
+
+    def trimul_contract_out(self, a, b_full, shard: RowShard, ld):
+        """Local rows of ``x = a b^T`` with ``b_full`` the gathered chunks."""
+        dev = b_full[0].device
+        x = self.new_x(shard.chunk, shard, dev)
+        if shard.rows:
+            self._contract(a, shard.rows, shard.chunk, b_full, shard.n, shard.chunk, shard.world,
+                           b_full[0][0].numel(), shard.n, ld, x, dev)
+        return x
+
+    def trimul_contract_in(self, a, b, shard: RowShard, ld, device):
+        """Partial ``x = a^T b`` over the rank's k rows, all ``world*chunk`` rows
+        (padding rows zero), ready for the reduce-scatter."""
+        x = self.new_x(shard.world * shard.chunk, shard, device)
+        if shard.rows:
+            self._contract(a, shard.n, shard.n, b, shard.n, shard.n, 1, 0, shard.rows, ld, x,
+                           device)
+            x[shard.n:].zero_()
+        else:
+            x.zero_()
+        return x
+
+    def trimul_finish(self, z_loc, shard: RowShard, x_loc, w: dict, add: bool):
+        if shard.rows == 0:
+            return
+        dev = z_loc.device
+        ws = self._ws_take(self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
+        keys = ("ln_in_w", "ln_in_b", "w_g", "ln_out_w", "ln_out_b", "w_z")
+        wt = [w[k].contiguous() for k in keys]
+        _lib.check(self.lib.fpb_trimul_shard_finish(
+            z_loc.data_ptr(), shard.n, shard.rows, x_loc.data_ptr(), *[t.data_ptr() for t in wt],
+            self.eps, int(bool(add)), self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)),
+            "fpb_trimul_shard_finish")
+
+    # ---------------------------------------------------------------- TriAttn
+    def triattn_bias_buffer(self, shard: RowShard, device):
+        ldb = int(self.lib.fpb_triattn_bias_ld(shard.n))
+        return torch.empty(shard.world * shard.chunk, 4, ldb, dtype=torch.float32, device=device)
+
+    def triattn_proj(self, z_loc, mask, shard: RowShard, w: dict, bias_full):
+        if shard.rows == 0:
+            return None
+        dev = z_loc.device
+        ws = self._ws_take(self.lib.fpb_triattn_shard_workspace_size(
+            shard.n, shard.rows, self.p, int(mask is not None)), dev)
+        wt = [w[k].contiguous() for k in ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias")]
+        _lib.check(self.lib.fpb_triattn_shard_proj(
+            z_loc.data_ptr(), self._ptr(mask), shard.n, shard.rows, shard.r0,
+            *[t.data_ptr() for t in wt], self.eps, bias_full.data_ptr(), self.p, ws.data_ptr(),
+            ws.numel(), ops._stream_ptr(dev)), "fpb_triattn_shard_proj")
+        return ws
+
+    def triattn_finish(self, z_loc, shard: RowShard, with_mask: bool, bias_full, w: dict, state):
+        if shard.rows == 0:
+            return
+        ws = state
+        keep = [None if w.get(k) is None else w[k].contiguous()
+                for k in ("ln_w", "ln_b", "w_g", "b_g", "w_o", "b_o")]
+        _lib.check(self.lib.fpb_triattn_shard_finish(
+            z_loc.data_ptr(), 0, shard.n, shard.rows, int(bool(with_mask)), bias_full.data_ptr(),
+            *[self._ptr(t) for t in keep], self.eps, self.p, ws.data_ptr(), ws.numel(),
+            ops._stream_ptr(z_loc.device)), "fpb_triattn_shard_finish")
+
+    # ---------------------------------------------------------------- transition
+    def transition(self, z_loc, shard: RowShard, w: dict):
+        if shard.rows == 0:
+            return
+        _, ws = ops.transition(z_loc[:shard.rows], w, precision=self.p, eps=self.eps,
+                               return_workspace=True)
+        self._ws.append(ws)
+
+
+# ---------------------------------------------------------------------------
+# rank-local orchestration (every rank runs the same collective sequence)
+# ---------------------------------------------------------------------------
+def sharded_trimul(z_loc, mask, w: dict, shard: RowShard, comm, phases, *, outgoing: bool,
+                   add: bool = True):
+    """Triangle multiplicative update of the rank's rows, in place on ``z_loc``."""
+    a, b, ld = phases.trimul_proj(z_loc, mask, shard, outgoing, w)
+    if outgoing:
+        b_full = []
+        for t in b:
+            full = t.new_empty((shard.world,) + tuple(t.shape))
+            comm.all_gather(full, t)
+            b_full.append(full)
+        x_loc = phases.trimul_contract_out(a, b_full, shard, ld)
+    else:
+        x_full = phases.trimul_contract_in(a, b, shard, ld, z_loc.device)
+        x_loc = phases.new_x(shard.chunk, shard, z_loc.device)
+        comm.reduce_scatter(x_loc, x_full)
+    phases.trimul_finish(z_loc, shard, x_loc, w, add)
+    return z_loc
+
+
+def sharded_triattn(z_loc, mask, w: dict, shard: RowShard, comm, phases, *,
+                    starting: bool = True):
+    """Triangle attention update added to the rank's rows of ``z_loc``."""
+    if not starting:
+        zt = transpose_rows(z_loc, shard, comm)
+        mt = None if mask is None else mask.transpose(0, 1).contiguous()
+        sharded_triattn(zt, mt, w, shard, comm, phases, starting=True)
+        z_loc.copy_(transpose_rows(zt, shard, comm))
+        return z_loc
+    bias_full = phases.triattn_bias_buffer(shard, z_loc.device)
+    state = phases.triattn_proj(z_loc, mask, shard, w, bias_full)
+    own = bias_full[shard.rank * shard.chunk:(shard.rank + 1) * shard.chunk]
+    comm.all_gather(bias_full, own.clone())
+    phases.triattn_finish(z_loc, shard, mask is not None, bias_full, w, state)
+    return z_loc
+
+
+def sharded_pair_block(z_loc, mask, weights: dict, shard: RowShard, comm, phases):
+    """Pair stack of one Pairformer block on the rank's rows (AF3 Algorithm 17
+    order): TriMul out, TriMul in, TriAttn start, TriAttn end, transition.
+    ``weights`` maps ``tri_mul_out, tri_mul_in, tri_att_start, tri_att_end,
+    pair_transition`` to the operators' weight dicts."""
+    sharded_trimul(z_loc, mask, weights["tri_mul_out"], shard, comm, phases, outgoing=True)
+    sharded_trimul(z_loc, mask, weights["tri_mul_in"], shard, comm, phases, outgoing=False)
+    sharded_triattn(z_loc, mask, weights["tri_att_start"], shard, comm, phases, starting=True)
+    sharded_triattn(z_loc, mask, weights["tri_att_end"], shard, comm, phases, starting=False)
+    phases.transition(z_loc, shard, weights["pair_transition"])
+    return z_loc
+
+
+def block_weight_dicts(block) -> dict:
+    """Weight dicts of a ``modules.PairformerPairBlock`` for ``sharded_pair_block``."""
+    return {name: getattr(block, name).weight_dict()
+            for name in ("tri_mul_out", "tri_mul_in", "tri_att_start", "tri_att_end",
+                         "pair_transition")}

@@ -141,6 +141,59 @@ int fpb_registry_resolve(void* registry, const char* signature_json, char* out, 
 int fpb_registry_manifest(void* registry, char* out, size_t cap);
 int fpb_registry_clear_runtime_state(void* registry);
 
+/* ---- Row-sharded phases (one rank owns rows [r0, r0 + rows) of z; the
+ * caller runs the NCCL collectives between phases). These split the fused
+ * operators above at their exchange points; the reference has no multi-GPU
+ * path for these operators (its only multi-device code is the two-GCD
+ * outer-batch split, python/fireprot/backends/amd/two_gcd_attention.py:53-101).
+ *
+ * TriMul planes are channel-first [128][plane_rows][ld] (ld =
+ * fpb_trimul_plane_ld of the column count), FP32 hi and lo in strict mode,
+ * BF16 in fast mode; the contraction output is tile-blocked
+ * [m][ceil(nn/128)][128][128] (FP32 strict, BF16 fast).
+ *   outgoing: proj(transposed=0, plane_rows=chunk) -> all-gather b ->
+ *             contract(m=rows, nn=n, B = the gathered chunks, k=n) -> finish.
+ *   incoming: proj(transposed=1, plane_rows=n) -> contract(m=n, nn=n, one B
+ *             chunk of n rows, k=rows) -> reduce-scatter x -> finish.
+ * In an all-gather buffer the chunk height must be a multiple of 32 rows;
+ * rows of the last chunk at or past nn are padding and are never stored. */
+size_t fpb_trimul_shard_workspace_size(int precision);
+size_t fpb_trimul_plane_ld(int cols, int precision);
+int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int n, int rows, int r0,
+                          int transposed, const float* ln_in_w, const float* ln_in_b,
+                          const float* w_a_p, const float* w_a_g, const float* w_b_p,
+                          const float* w_b_g, float eps, void* a_hi, void* a_lo, void* b_hi,
+                          void* b_lo, int ld, int plane_rows, int precision, void* workspace,
+                          size_t workspace_bytes, cudaStream_t stream);
+int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
+                              const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
+                              int b_chunks, size_t b_chunk_stride, int k, int ld,
+                              void* x_blocked, int precision, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
+int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked,
+                            const float* ln_in_w, const float* ln_in_b, const float* w_g,
+                            const float* ln_out_w, const float* ln_out_b, const float* w_z,
+                            float eps, int add, int precision, void* workspace,
+                            size_t workspace_bytes, cudaStream_t stream);
+/* Triangle attention, starting-node form on the rank's rows: proj writes the
+ * rank's rows of the j-major pair bias [n][4][fpb_triattn_bias_ld(n)]; the
+ * caller all-gathers it; finish runs attention + gate + output on the rows
+ * (z_loc += delta, or delta_out = delta). The ending node is this form on the
+ * transposed pair tensor (all-to-all transposes around it). proj and finish
+ * share the workspace. */
+size_t fpb_triattn_bias_ld(int n);
+size_t fpb_triattn_shard_workspace_size(int n, int rows, int precision, int with_mask);
+int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int n, int rows, int r0,
+                           const float* ln_w, const float* ln_b, const float* w_q,
+                           const float* w_k, const float* w_v, const float* w_bias, float eps,
+                           float* bias_full, int precision, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream);
+int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, int rows, int with_mask,
+                             const float* bias_full, const float* ln_w, const float* ln_b,
+                             const float* w_g, const float* b_g, const float* w_o,
+                             const float* b_o, float eps, int precision, void* workspace,
+                             size_t workspace_bytes, cudaStream_t stream);
+
 /* Weights of the five pair operators of one block (torch Linear layouts). */
 typedef struct {
   const float *ln_in_w, *ln_in_b, *w_a_p, *w_a_g, *w_b_p, *w_b_g, *w_g, *ln_out_w, *ln_out_b,

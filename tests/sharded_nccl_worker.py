@@ -1,0 +1,60 @@
+"""torchrun worker for ``test_gpu_sharded_nccl.py``: one process per GPU,
+NCCL process group, the sharded pair block on each rank's rows, then rank 0
+compares the all-gathered result with the CPU oracle and writes a JSON
+verdict to ``argv[1]``. Every rank runs the same collective sequence."""
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from fireprot_b200 import sharded as S  # noqa: E402
+from oracle import pairformer_oracle as O  # noqa: E402
+from sharded_util import oracle_weight_dicts  # noqa: E402
+
+
+def main(out_path: str) -> None:
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    comm = S.DistComm()
+    results = {}
+    try:
+        for n, mask_kind in ((150, "padding"), (96, "none")):
+            z = O.make_pair(n, seed=71 + n)
+            mask = O.make_padding_mask(n, n - 9) if mask_kind == "padding" else None
+            p = O.make_block_params(seed=17)
+            w = {k: {kk: (None if vv is None else vv.to(dev)) for kk, vv in d.items()}
+                 for k, d in oracle_weight_dicts(p).items()}
+            md = None if mask is None else mask.to(dev)
+            sh = S.shard_plan(n, comm.world, comm.rank)
+            ref = O.pair_block(z, mask, p) if comm.rank == 0 else None
+            for precision in ("strict", "fast"):
+                z_loc = S.local_rows(z.to(dev), sh)
+                ph = S.CudaPhases(precision)
+                S.sharded_pair_block(z_loc, md, w, sh, comm, ph)
+                torch.cuda.synchronize(dev)
+                ph.check()
+                full = S.gather_rows(z_loc, sh, comm).cpu()
+                if comm.rank == 0:
+                    tol = O.STRICT_TOL if precision == "strict" else O.FAST_TOL
+                    err = O.rel_max_err(full, ref)
+                    results[f"n{n}_{mask_kind}_{precision}"] = {"err": err, "tol": tol,
+                                                               "ok": err <= tol}
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    if comm.rank == 0:
+        Path(out_path).write_text(json.dumps({"world": comm.world, "cases": results}))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])

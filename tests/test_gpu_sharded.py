@@ -1,0 +1,112 @@
+"""GPU parity of the row-sharded phase kernels (``fpb_trimul_shard_*``,
+``fpb_triattn_shard_*``) against the single-device oracle.
+
+Ranks are emulated by threads on one GPU (``sharded_util.ThreadComm``: the
+collectives are tensor copies between the threads' buffers, every launch on
+one stream), so each rank's kernels run on its own row range, including
+ragged and empty ranks. The NCCL path itself is covered by
+``test_gpu_sharded_nccl.py``. Tolerances: strict 1e-4, fast 1e-2 of the
+fp32 output scale (single operators); the full block accumulates five
+updates, and is held to the same bounds.
+"""
+import pytest
+import torch
+
+from fireprot_b200 import sharded as S
+from oracle import pairformer_oracle as O
+
+from sharded_util import oracle_weight_dicts, run_threads
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(d, device):
+    return {k: (None if v is None else v.to(device)) for k, v in d.items()}
+
+
+def _tol(precision):
+    return O.STRICT_TOL if precision == "strict" else O.FAST_TOL
+
+
+def _mask(n, kind):
+    if kind == "none":
+        return None
+    if kind == "padding":
+        return O.make_padding_mask(n, n - 7)
+    g = torch.Generator().manual_seed(11)
+    return (torch.rand(n, n, generator=g) > 0.25).float()
+
+
+def _run(world, n, z, mask, device, body):
+    md = None if mask is None else mask.to(device)
+
+    def rank_fn(r, comm):
+        sh = S.shard_plan(n, world, r)
+        z_loc = S.local_rows(z.to(device), sh)
+        phases = body(z_loc, md, sh, comm)
+        torch.cuda.synchronize(device)
+        phases.check()
+        return S.gather_rows(z_loc, sh, comm).cpu()
+
+    return run_threads(world, rank_fn)
+
+
+@pytest.mark.parametrize("world,n", [(2, 100), (3, 70), (4, 40)])
+@pytest.mark.parametrize("outgoing", [True, False])
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+def test_sharded_trimul(cuda_device, world, n, outgoing, precision):
+    z = O.make_pair(n, seed=21 + n)
+    mask = _mask(n, "random")
+    p = O.make_trimul_params(seed=5, ln_affine_random=True)
+    ref = O.triangle_multiplication(z, mask, p, outgoing=outgoing, add=True)
+    w = _dev({k: getattr(p, k) for k in ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p",
+                                         "w_b_g", "w_g", "ln_out_w", "ln_out_b", "w_z")},
+             cuda_device)
+
+    def body(z_loc, md, sh, comm):
+        ph = S.CudaPhases(precision)
+        S.sharded_trimul(z_loc, md, w, sh, comm, ph, outgoing=outgoing)
+        return ph
+
+    for full in _run(world, n, z, mask, cuda_device, body):
+        assert O.rel_max_err(full, ref) <= _tol(precision)
+
+
+@pytest.mark.parametrize("world,n", [(2, 100), (3, 70)])
+@pytest.mark.parametrize("starting", [True, False])
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+@pytest.mark.parametrize("mask_kind", ["none", "padding"])
+def test_sharded_triattn(cuda_device, world, n, starting, precision, mask_kind):
+    z = O.make_pair(n, seed=31 + n)
+    mask = _mask(n, mask_kind)
+    p = O.make_triattn_params(seed=9)
+    ref = z + O.triangle_attention(z, mask, p, starting=starting)
+    w = _dev({k: getattr(p, k) for k in ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias", "w_g",
+                                         "b_g", "w_o", "b_o")}, cuda_device)
+
+    def body(z_loc, md, sh, comm):
+        ph = S.CudaPhases(precision)
+        S.sharded_triattn(z_loc, md, w, sh, comm, ph, starting=starting)
+        return ph
+
+    for full in _run(world, n, z, mask, cuda_device, body):
+        assert O.rel_max_err(full, ref) <= _tol(precision)
+
+
+@pytest.mark.parametrize("world,n,mask_kind", [(1, 96, "padding"), (2, 150, "padding"),
+                                               (3, 100, "none"), (5, 130, "random")])
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+def test_sharded_block(cuda_device, world, n, mask_kind, precision):
+    z = O.make_pair(n, seed=41 + n)
+    mask = _mask(n, mask_kind)
+    p = O.make_block_params(seed=13)
+    ref = O.pair_block(z, mask, p)
+    w = {k: _dev(v, cuda_device) for k, v in oracle_weight_dicts(p).items()}
+
+    def body(z_loc, md, sh, comm):
+        ph = S.CudaPhases(precision)
+        S.sharded_pair_block(z_loc, md, w, sh, comm, ph)
+        return ph
+
+    for full in _run(world, n, z, mask, cuda_device, body):
+        assert O.rel_max_err(full, ref) <= _tol(precision)

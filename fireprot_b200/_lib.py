@@ -43,6 +43,9 @@ SIGNATURES = {
     "fpb_transition": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_int]
                        + [c_void_p] * 5
                        + [c_float, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_transition_noalloc": (c_int, [c_void_p, c_void_p, ctypes.c_longlong, c_int, c_int]
+                               + [c_void_p] * 5
+                               + [c_float, c_int, ctypes.POINTER(c_int), c_void_p]),
     "fpb_pair_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "fpb_pair_block": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_float, c_int, c_void_p,
                                c_size_t, c_void_p]),

@@ -15,6 +15,7 @@ extern "C" const char* fpb_status_string(int status) {
     case kErrCuda: return "CUDA launch error";
     case kErrTimeout: return "device-side wait timed out";
     case kErrWorkspace: return "workspace too small";
+    case kErrScratch: return "request exceeds the static scratch capacity";
     default: return "unknown status";
   }
 }

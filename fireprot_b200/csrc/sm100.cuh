@@ -28,6 +28,7 @@ enum : int {
   kErrCuda = 5,
   kErrTimeout = 6,
   kErrWorkspace = 7,
+  kErrScratch = 8,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

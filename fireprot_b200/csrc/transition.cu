@@ -12,6 +12,7 @@
 // h_c = silu(a_c) * b_c and write it to shared memory as the A operand of
 // GEMM 2, which accumulates h_c Wout[:, c]^T into a 128-column TMEM
 // accumulator. The 4x-wide intermediate never reaches HBM.
+#include "../../include/fireprot_b200.h"
 #include "kernels.h"
 #include "rowgemm.cuh"
 
@@ -425,4 +426,115 @@ extern "C" int fpb_transition(float* z, float* delta_out, long long rows, int c_
                k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   }
   return launch_status();
+}
+
+// ============================================================================
+// Allocation-free variant: the scratch lives in a static device array
+// ============================================================================
+// Same kernels and results as fpb_transition; the packed weights and the
+// status word go to g_transition_scratch instead of a caller workspace, and
+// the launches bypass the timing hook (which creates events when enabled).
+namespace fpb {
+namespace {
+
+constexpr size_t kTransitionScratchBytes = FPB_TRANSITION_SCRATCH_BYTES;
+
+// One instance per device. Every call overwrites the packed weights in full;
+// only the 256-byte status header must start at zero, and each call zeroes
+// it on its own stream before its first kernel.
+static __device__ __align__(256) unsigned char g_transition_scratch[kTransitionScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxScratchDevices];  // device address of the array, per device
+
+// Device address of this device's scratch, looked up once per device with
+// that device current (the first call per device does the lookup).
+int transition_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  if (dev < 0 || dev >= kMaxScratchDevices) return kErrArg;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_transition_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return kErrCuda;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return kOk;
+}
+
+}  // namespace
+}  // namespace fpb
+
+extern "C" int fpb_transition_noalloc(float* z, float* delta_out, long long rows, int c_z,
+                                      int expansion, const float* ln_w, const float* ln_b,
+                                      const float* w_a, const float* w_b, const float* w_out,
+                                      float eps, int precision, int* status_out,
+                                      cudaStream_t stream) {
+  if (!z || !ln_w || !ln_b || !w_a || !w_b || !w_out) return kErrArg;
+  if (delta_out && !aligned16(delta_out)) return kErrAlign;
+  if (c_z != 128 || expansion != 4 || rows <= 0 || rows > 0x7fffffffll) return kErrShape;
+  if (precision != 0 && precision != 1) return kErrArg;
+  if (!aligned16(z) || !aligned16(ln_w) || !aligned16(ln_b)) return kErrAlign;
+  const size_t need = fpb_transition_workspace_size(c_z, expansion, precision);
+  if (need == 0) return kErrShape;
+  if (need > kTransitionScratchBytes) return kErrScratch;
+  void* scratch = nullptr;
+  int st = transition_scratch(&scratch);
+  if (st) return st;
+  const bool strict = precision == 0;
+  WsCursor cur(scratch, kTransitionScratchBytes);
+  TransPlan<WsCursor> pl;
+  pl.plan(cur, strict);
+  if (!cur.ok) return kErrScratch;
+  if (cudaMemsetAsync(scratch, 0, kWsHeader, stream) != cudaSuccess) return kErrCuda;
+  const int hc = strict ? TransCfg<true>::HC : TransCfg<false>::HC;
+  pack_transition_w1<<<128, 256, 0, stream>>>(w_a, w_b, hc, pl.w1_hi, pl.w1_lo, strict ? 1 : 0);
+  pack_plain<<<64, 256, 0, stream>>>(w_out, 128 * 512, pl.w2_hi, pl.w2_lo, strict ? 1 : 0);
+  if ((st = launch_status())) return st;
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap m1h, m1l, m2h, m2l;
+  bool ok = make_map_3d(&m1h, pl.w1_hi, dt, 128, 1024, 1, 128ull * esz, 128ull * esz * 1024,
+                        128 / esz, 2 * hc, 1) &&
+            make_map_3d(&m2h, pl.w2_hi, dt, 512, 128, 1, 512ull * esz, 512ull * esz * 128,
+                        128 / esz, 128, 1);
+  if (strict)
+    ok = ok &&
+         make_map_3d(&m1l, pl.w1_lo, dt, 128, 1024, 1, 128ull * esz, 128ull * esz * 1024,
+                     128 / esz, 2 * hc, 1) &&
+         make_map_3d(&m2l, pl.w2_lo, dt, 512, 128, 1, 512ull * esz, 512ull * esz * 128, 128 / esz,
+                     128, 1);
+  else {
+    m1l = m1h;
+    m2l = m2h;
+  }
+  if (!ok) return kErrArg;
+  TransArgs ta{z, delta_out, (int)rows, eps, ln_w, ln_b, static_cast<int*>(scratch)};
+  const unsigned tiles = (unsigned)((rows + 127) / 128);
+  if (strict) {
+    auto k = transition_kernel<true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
+    k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+  } else {
+    auto k = transition_kernel<false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
+    k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+  }
+  if ((st = launch_status())) return st;
+  if (status_out) {
+    // wait for this call, then report its device status word
+    int word = 0;
+    if (cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+      return kErrCuda;
+    *status_out = word;
+  }
+  return kOk;
 }

@@ -5,7 +5,8 @@
  * Conventions (mirroring the reference's C-ABI kernels):
  *  - every entry point returns an int status: 0 ok, 2 unsupported shape,
  *    3 misaligned pointer/stride, 4 invalid argument, 5 CUDA launch error,
- *    6 device-side wait timed out, 7 workspace too small
+ *    6 device-side wait timed out, 7 workspace too small, 8 request exceeds
+ *    the static scratch capacity (fpb_transition_noalloc only)
  *    (reference: kernels/amd/fireprot_ck_attention.cpp:35,68,106-108,
  *    kernels/amd/fireprot_lt_bmm.cpp:47-48,62);
  *  - pointers are raw device pointers, work is enqueued on `stream`, nothing
@@ -107,6 +108,35 @@ int fpb_transition(float* z, float* delta_out, long long rows, int c_z, int expa
                    const float* ln_w, const float* ln_b, const float* w_a, const float* w_b,
                    const float* w_out, float eps, int precision, void* workspace,
                    size_t workspace_bytes, cudaStream_t stream);
+
+/* Allocation-free pair transition. No counterpart in the reference: it is
+ * fpb_transition (same kernels, same results) for callers that must not
+ * allocate device memory, such as a serving process whose memory manager
+ * reserves the GPU's memory up front and owns every later allocation (a
+ * cudaMalloc from a library would then fail or break its accounting, and
+ * cudaFree synchronises the whole device), or a host behind an FFI with no
+ * device allocator of its own, which would need one only for this scratch.
+ *
+ * The scratch (packed weights plus the 256-byte status word) is a static
+ * device array of this library, FPB_TRANSITION_SCRATCH_BYTES per device; a
+ * request needing more is rejected with status 8. Nothing else is allocated.
+ *  - The first call on each device, with that device current, looks up the
+ *    array's device address; make that first call before any stream
+ *    capture that would include this function.
+ *  - Each call zeroes the status word on `stream` before its kernels (the
+ *    only part that must start at zero) and overwrites the packed weights.
+ *  - Calls on one device share the array: calls that can overlap (several
+ *    streams or threads on one device) race and must be serialised by the
+ *    caller, e.g. by issuing them on one stream.
+ *  - status_out (nullable host pointer): when given, the call waits for
+ *    `stream` and stores the device status word (0 = every wait completed).
+ * Arguments otherwise as fpb_transition; z, the weights and `stream` belong
+ * to the current device. */
+#define FPB_TRANSITION_SCRATCH_BYTES (2u << 20)
+int fpb_transition_noalloc(float* z, float* delta_out, long long rows, int c_z, int expansion,
+                           const float* ln_w, const float* ln_b, const float* w_a,
+                           const float* w_b, const float* w_out, float eps, int precision,
+                           int* status_out, cudaStream_t stream);
 
 /* Triangle attention core at the reference's q/k/v boundary
  * (dispatch_triangle_attention, python/fireprot/backends/amd/triangle_attention.py:199-256,

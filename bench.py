@@ -10,9 +10,11 @@ steps chain (step k+1 runs on step k's output), i.e. a K-block stack.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--precision strict|fast]
   python bench.py --impl reference ...   # the native math on host CPU cores
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own independent
-pair stack (data-parallel replicas, weak scaling); device time is the max over
-ranks and ``value`` is the total blocks/s of all ranks.
+Multi-GPU (torchrun, one rank per GPU): by default the rows of ONE pair
+tensor are sharded over the ranks (``fireprot_b200.sharded``, NCCL between
+the operator phases; strong scaling, ``value`` = blocks/s of the job);
+``--mode replicas`` runs an independent block per rank instead (weak
+scaling). Device time is the max over ranks.
 
 Printed on rank 0: one JSON line (see ``_result``) with device-timed
 ``value``, end-to-end ``e2e`` (host buffers, copies inside the timed region),
@@ -184,8 +186,9 @@ def run_reference(args, world, rank):
     return {
         "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
+        "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 and args.mode == "sharded" else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": _config(args),
         "cpu_baseline": {"value": value, "unit": "blocks/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -200,7 +203,10 @@ def _config(args):
                          f"precision, padding mask valid {args.valid}"),
             "n": args.n, "c_z": C, "precision": args.precision, "valid_length": args.valid,
             "l2": "inputs larger than L2 (z alone is %.2f GB)" % (args.n ** 2 * C * 4 / 1e9),
-            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+            "parallelism": ("single GPU" if args.gpus == 1 else
+                            f"rows of z sharded over {args.gpus} GPUs (NCCL all-gather, "
+                            f"reduce-scatter, all-to-all)" if args.mode == "sharded" else
+                            f"independent replicas x{args.gpus}")}
 
 
 # ---------------------------------------------------------------------------
@@ -213,27 +219,60 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     n = args.n
-    gen = torch.Generator().manual_seed(1000 + rank)
-    z_host = torch.randn(n, n, C, generator=gen).pin_memory()
+    sharded = world > 1 and args.mode == "sharded"
+    # sharded ranks hold rows of ONE problem: same data and weights everywhere
+    seed = 0 if sharded or world == 1 else rank
+    gen = torch.Generator().manual_seed(1000 + seed)
+    z_full = torch.randn(n, n, C, generator=gen)
     valid = torch.arange(n) < args.valid
     mask_host = (valid[:, None] & valid[None, :]).float().pin_memory()
-    block = PairformerPairBlock().init_random_(seed=1 + rank).to(dev)
-    cw = block.c_weights()
-    z = z_host.to(dev)
+    block = PairformerPairBlock().init_random_(seed=1 + seed).to(dev)
     mask = mask_host.to(dev)
-    ws = ops.pair_block_workspace(n, args.precision, True, dev)
+
+    if sharded:
+        from fireprot_b200 import sharded as S
+        shard = S.shard_plan(n, world, rank)
+        comm = S.DistComm()
+        weights = S.block_weight_dicts(block)
+        z_host = S.local_rows(z_full, shard).pin_memory()
+        rows_frac = shard.rows / n
+
+        def make_step(precision):
+            phases = S.CudaPhases(precision)
+
+            def step(zz, mm):
+                S.sharded_pair_block(zz, mm, weights, shard, comm, phases)
+            return step, phases.check
+    else:
+        z_host = z_full.pin_memory()
+        cw = block.c_weights()
+        rows_frac = 1.0
+
+        def make_step(precision):
+            ws = ops.pair_block_workspace(n, precision, True, dev)
+
+            def step(zz, mm):
+                ops.pair_block(zz, mm, cw, precision=precision, workspace=ws)
+
+            def check():
+                st = ops.workspace_status(ws)
+                if st != 0:
+                    raise RuntimeError(f"device status {st}")
+            return step, check
+    del z_full
+    blocks_per_step = 1 if sharded else world
+    z = z_host.to(dev)
     stream = torch.cuda.current_stream(dev)
+    step_fn, check = make_step(args.precision)
 
     def step(zz):
-        ops.pair_block(zz, mask, cw, precision=args.precision, workspace=ws)
+        step_fn(zz, mask)
 
     # ---- warm-up
     for _ in range(args.warmup):
         step(z)
     torch.cuda.synchronize(dev)
-    st = ops.workspace_status(ws)
-    if st != 0:
-        raise RuntimeError(f"device status {st} after warm-up")
+    check()
 
     # ---- timed region: K chained blocks, inputs resident in HBM
     bus = None
@@ -262,7 +301,8 @@ def run_ours(args, world, rank, local):
     ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(ms, world, dev)
     ms_per_step = ms_max / args.steps
-    value = world * args.steps / (ms_max / 1e3)
+    value = blocks_per_step * args.steps / (ms_max / 1e3)
+    check()
     if not torch.isfinite(z).all():
         raise RuntimeError("non-finite pair tensor after the timed steps")
 
@@ -278,36 +318,40 @@ def run_ours(args, world, rank, local):
     for _ in range(e2e_steps):
         zz.copy_(z_host, non_blocking=True)
         mm.copy_(mask_host, non_blocking=True)
-        step(zz)
+        step_fn(zz, mm)
         out_host.copy_(zz, non_blocking=True)
     f1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world, dev)
-    e2e_value = world * e2e_steps / (e2e_ms / 1e3)
-    h2d = z_host.numel() * 4 + mask_host.numel() * 4
-    d2h = out_host.numel() * 4
+    e2e_value = blocks_per_step * e2e_steps / (e2e_ms / 1e3)
+    # whole-job bytes: every rank copies its z rows (or replica) and the mask
+    h2d = world * (z_host.numel() * 4 + mask_host.numel() * 4)
+    d2h = world * out_host.numel() * 4
 
     # ---- fast-mode side measurement (strict is the headline)
     side = None
     if args.precision == "strict" and not args.no_side:
-        ws_f = ops.pair_block_workspace(n, "fast", True, dev)
+        fast_step, fast_check = make_step("fast")
         zf = z_host.to(dev)
         for _ in range(2):
-            ops.pair_block(zf, mask, cw, precision="fast", workspace=ws_f)
+            fast_step(zf, mask)
         torch.cuda.synchronize(dev)
+        fast_check()
+        barrier(world)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         for _ in range(args.steps):
-            ops.pair_block(zf, mask, cw, precision="fast", workspace=ws_f)
+            fast_step(zf, mask)
         g1.record(stream)
         torch.cuda.synchronize(dev)
         fms = max_over_ranks(g0.elapsed_time(g1), world, dev) / args.steps
         pf, _, _ = peaks("fast")
-        side = {"precision": "fast", "value": world * 1e3 / fms, "unit": "blocks/s",
+        side = {"precision": "fast", "value": blocks_per_step * 1e3 / fms, "unit": "blocks/s",
                 "ms_per_step": fms,
-                "tc_frac_block": block_flops(n) / (fms / 1e3) / 1e12 / pf}
-        del ws_f, zf
+                "tc_frac_block": blocks_per_step * block_flops(n) / (fms / 1e3) / 1e12
+                / (pf * world)}
+        del zf
 
     if rank != 0:
         return None
@@ -317,14 +361,14 @@ def run_ours(args, world, rank, local):
     per_kernel = {}
     for name, rec in kernels.items():
         avg = rec["total_ms"] / rec["launches"]
-        fl = kernel_flops(name, n)
+        fl = kernel_flops(name, n) * rows_frac
         per_kernel[name] = {"launches": rec["launches"], "avg_ms": round(avg, 4),
                             "share": round(rec["total_ms"] / max(1e-9, sum(
                                 r["total_ms"] for r in kernels.values())), 4),
                             "tflops": round(fl / (avg / 1e3) / 1e12, 2) if fl else None}
     dom = max(kernels, key=lambda k: kernels[k]["total_ms"])
     dom_avg_s = kernels[dom]["total_ms"] / kernels[dom]["launches"] / 1e3
-    achieved = kernel_flops(dom, n) / dom_avg_s / 1e12
+    achieved = kernel_flops(dom, n) * rows_frac / dom_avg_s / 1e12
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
@@ -347,11 +391,13 @@ def run_ours(args, world, rank, local):
     return {
         "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None,
         "dtype": "f32 (3xTF32 tensor cores)" if args.precision == "strict" else "bf16 (f32 acc)",
         "data": "synthetic (seeded N(0,1) pair tensor, random-init weights)",
         "config": _config(args),
-        "tc_frac_block": block_flops(n) / (ms_per_step / 1e3) / 1e12 / peak_tc,
+        "tc_frac_block": blocks_per_step * block_flops(n) / (ms_per_step / 1e3) / 1e12
+        / (peak_tc * world),
         "e2e": {"value": e2e_value, "unit": "blocks/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": launches,
@@ -375,6 +421,8 @@ def main():
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--valid", type=int, default=1480)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--mode", choices=["sharded", "replicas"], default="sharded",
+                    help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
     args = ap.parse_args()

@@ -121,8 +121,10 @@ def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
 class CudaPhases:
     """Phase kernels of the row-sharded operators (C-ABI entry points).
 
-    Buffers are allocated with torch on the current stream; every workspace
-    used is kept so ``check()`` can read the device status words.
+    Buffers are allocated with torch on the current stream. Each phase keeps
+    one workspace, reused by its later calls on the same stream (each call
+    restarts its status word), so ``check()`` reports the latest call of
+    every phase.
     """
 
     def __init__(self, precision="strict", eps: float = 1e-5):
@@ -130,7 +132,7 @@ class CudaPhases:
         self.strict = self.p == ops.STRICT
         self.eps = float(eps)
         self.lib = _lib.load()
-        self._ws = []
+        self._ws = {}
 
     # ---------------------------------------------------------------- helpers
     def _dtype(self):
@@ -141,9 +143,11 @@ class CudaPhases:
         return [torch.empty(128, rows, ld, dtype=self._dtype(), device=device)
                 for _ in range(n_planes)]
 
-    def _ws_take(self, nbytes, device):
-        ws = ops.workspace(nbytes, device)
-        self._ws.append(ws)
+    def _ws_take(self, name, nbytes, device):
+        ws = self._ws.get(name)
+        if ws is None or ws.numel() < nbytes or ws.device != device:
+            ws = ops.workspace(nbytes, device)
+            self._ws[name] = ws
         return ws
 
     @staticmethod
@@ -155,11 +159,10 @@ class CudaPhases:
 
     def check(self) -> None:
         """Raise if any wait of any phase kernel gave up (reads status words)."""
-        for ws in self._ws:
+        for name, ws in self._ws.items():
             st = ops.workspace_status(ws)
             if st:
-                raise RuntimeError(f"phase kernel status {st}")
-        self._ws.clear()
+                raise RuntimeError(f"{name} phase kernel status {st}")
 
     # ---------------------------------------------------------------- TriMul
     def trimul_proj(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
@@ -178,7 +181,7 @@ class CudaPhases:
         a, b = self._planes(plane_rows, ld, dev), self._planes(plane_rows, ld, dev)
         if rows == 0:
             return a, b, ld
-        ws = self._ws_take(self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
+        ws = self._ws_take("trimul_proj", self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
         keys = ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p", "w_b_g")
         wt = [w[k].contiguous() for k in keys]
         _lib.check(self.lib.fpb_trimul_shard_proj(
@@ -193,7 +196,7 @@ class CudaPhases:
 
     def _contract(self, a, m, a_plane_rows, b, nn, b_chunk_rows, b_chunks, b_chunk_stride, k,
                   ld, x, device):
-        ws = self._ws_take(256, device)
+        ws = self._ws_take("trimul_contract", 256, device)
         _lib.check(self.lib.fpb_trimul_shard_contract(
             *self._pair(a), m, a_plane_rows, *self._pair(b), nn, b_chunk_rows, b_chunks,
             b_chunk_stride, k, ld, x.data_ptr(), self.p, ws.data_ptr(), ws.numel(),
@@ -224,7 +227,7 @@ class CudaPhases:
         if shard.rows == 0:
             return
         dev = z_loc.device
-        ws = self._ws_take(self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
+        ws = self._ws_take("trimul_finish", self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
         keys = ("ln_in_w", "ln_in_b", "w_g", "ln_out_w", "ln_out_b", "w_z")
         wt = [w[k].contiguous() for k in keys]
         _lib.check(self.lib.fpb_trimul_shard_finish(
@@ -241,7 +244,7 @@ class CudaPhases:
         if shard.rows == 0:
             return None
         dev = z_loc.device
-        ws = self._ws_take(self.lib.fpb_triattn_shard_workspace_size(
+        ws = self._ws_take("triattn", self.lib.fpb_triattn_shard_workspace_size(
             shard.n, shard.rows, self.p, int(mask is not None)), dev)
         wt = [w[k].contiguous() for k in ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias")]
         _lib.check(self.lib.fpb_triattn_shard_proj(
@@ -265,9 +268,14 @@ class CudaPhases:
     def transition(self, z_loc, shard: RowShard, w: dict):
         if shard.rows == 0:
             return
-        _, ws = ops.transition(z_loc[:shard.rows], w, precision=self.p, eps=self.eps,
-                               return_workspace=True)
-        self._ws.append(ws)
+        ws = self._ws_take("transition", self.lib.fpb_transition_workspace_size(128, 4, self.p),
+                           z_loc.device)
+        keys = ("ln_w", "ln_b", "w_a", "w_b", "w_out")
+        wt = [w[k].contiguous() for k in keys]
+        _lib.check(self.lib.fpb_transition(
+            z_loc.data_ptr(), 0, shard.rows * shard.n, 128, 4, *[t.data_ptr() for t in wt],
+            self.eps, self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(z_loc.device)),
+            "fpb_transition")
 
 
 # ---------------------------------------------------------------------------

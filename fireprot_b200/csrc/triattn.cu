@@ -28,6 +28,19 @@ constexpr int kHeads = 4;
 constexpr int kHeadDim = 32;
 constexpr float kMaskInf = 1e9f;
 
+// Pair bias layout, j-blocked: [ceil(n/32)][head][ldb/4][32 rows j][4 keys k]
+// (ldb = keys padded to 32). A warp's 32 query rows read 4 keys each as one
+// contiguous 512-byte access, and rows [32q, 32q + 32m) form one contiguous
+// block (the all-gather unit of the row-sharded path).
+__host__ __device__ __forceinline__ size_t bias_index(int j, int h, int k, int ldb) {
+  return ((((size_t)(j >> 5) * kHeads + h) * (size_t)(ldb >> 2) + (size_t)(k >> 2)) * 32 +
+          (size_t)(j & 31)) * 4 + (size_t)(k & 3);
+}
+// floats of a pair bias buffer for n rows
+__host__ __device__ __forceinline__ size_t bias_elems(int n, int ldb) {
+  return (size_t)((n + 31) / 32) * 32 * kHeads * ldb;
+}
+
 // ============================================================================
 // 1. projection
 // ============================================================================
@@ -51,7 +64,7 @@ struct AttnProjArgs {
   void* v_hi;
   void* v_lo;
   int ldv;          // keys pitch of v^T
-  float* bias;      // [n][4][ldb] (row j outermost), global rows
+  float* bias;      // j-blocked pair bias (bias_index), global rows
   int ldb;
   float* mbias;     // [yrows][ldb] or null
   int* status;
@@ -160,7 +173,7 @@ __global__ void __launch_bounds__(192, 1)
       s = pr - r * n;
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        p.bias[(((size_t)(p.r0 + r)) * kHeads + h) * p.ldb + s] = bias_tile[h * 128 + t];
+        p.bias[bias_index((int)(p.r0 + r), h, (int)s, p.ldb)] = bias_tile[h * 128 + t];
       if (p.mbias) {
         const float m =
             __ldg(p.mask + (kTrans ? ((size_t)s * n + r) : ((size_t)(p.r0 + r) * n + s)));
@@ -276,7 +289,7 @@ __global__ void __launch_bounds__(192, 1)
 // ============================================================================
 struct AttnCoreArgs {
   int n;
-  const float* bias;   // [n][4][ldb] (row j outermost)
+  const float* bias;   // j-blocked pair bias (bias_index)
   const float* mbias;  // [rows][ldb] or null
   int ldb;
   void* o;             // [rows*n][128] fp32 (strict or o_f32) / bf16 (fast)
@@ -386,9 +399,12 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 4) {
     // ------------------------------------------------------------ TMA
     if (lane == 0) {
+      // the Q tile is read by this CTA only; keep L2 for the pair bias
+      const uint64_t pol_q = policy_evict_first();
       mbar_arrive_expect_tx(q_full, C::NSPLIT * C::Q_BYTES);
-      tma_load_3d(Q, &mq_hi, q_full, 0, jt * C::BQ, ih);
-      if constexpr (kStrict) tma_load_3d(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih);
+      tma_load_3d_hint(Q, &mq_hi, q_full, 0, jt * C::BQ, ih, pol_q);
+      if constexpr (kStrict)
+        tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int s = t % C::KV_STAGES;
@@ -493,38 +509,61 @@ __global__ void __launch_bounds__(192, 2)
     const int t_row = warp * 32 + lane;  // TMEM lane / query row in tile
     const int j = jt * C::BQ + t_row;
     const bool jvalid = j < n;
-    const float* brow = p.bias + ((size_t)(jvalid ? j : 0) * kHeads + h) * p.ldb;
+    // this thread's row of the j-blocked bias: key k at brow[(k >> 2) * 128 + (k & 3)]
+    const float* brow = p.bias + bias_index(jvalid ? j : 0, h, 0, p.ldb);
     const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
+    // the pair bias (every row i reads all of it) and the mask bias row stay in L2
+    const uint64_t pol_bias = policy_evict_last();
     float m_run = -INFINITY, l_run = 0.f;
     float a1 = 0.f, a2 = 0.f;  // alpha of the previous / second previous tile
     float o[32];
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] = 0.f;
-    // additive term of key tile t: mask bias + triangle bias, -inf past n.
-    // Adding (mask + bias) to q.k equals the reference's (q.k + mask) + bias
-    // for 0/1 masks: -1e9 absorbs any |x| < 32 in FP32 either way.
-    auto load_add = [&](int t, float (&cv)[C::BKV]) {
+    // Additive terms of key tile t: the pair bias (a different row per
+    // thread) is loaded in one batch a tile ahead and added to q.k first;
+    // the mask bias row (the same for every thread, an L1 hit) and -inf past
+    // n are applied when the tile is consumed. (q.k + bias) + mask equals the
+    // reference's (q.k + mask) + bias: unmasked keys add 0, and for masked
+    // keys -1e9 absorbs any |x| < 32 in FP32 either way.
+    auto load_bias = [&](int t, float (&cb)[C::BKV]) {
       const int k0 = t * C::BKV;
+      if (jvalid && k0 + C::BKV <= n) {
 #pragma unroll
-      for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
-        const int k = k0 + 4 * e4;
-        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), mb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k + 4 <= n) {
-          if (jvalid) bb = __ldg(reinterpret_cast<const float4*>(brow + k));
-          if (mrow) mb = __ldg(reinterpret_cast<const float4*>(mrow + k));
-          cv[4 * e4] = mb.x + bb.x;
-          cv[4 * e4 + 1] = mb.y + bb.y;
-          cv[4 * e4 + 2] = mb.z + bb.z;
-          cv[4 * e4 + 3] = mb.w + bb.w;
-        } else {
+        for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
+          const float4 b = ldg_f4_hint(brow + ((k0 >> 2) + e4) * 128, pol_bias);
+          cb[4 * e4] = b.x;
+          cb[4 * e4 + 1] = b.y;
+          cb[4 * e4 + 2] = b.z;
+          cb[4 * e4 + 3] = b.w;
+        }
+      } else {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float v = -INFINITY;
-            if (k + u < n) v = (mrow ? mrow[k + u] : 0.f) + (jvalid ? brow[k + u] : 0.f);
-            cv[4 * e4 + u] = v;
+        for (int e = 0; e < C::BKV; ++e) {
+          const int k = k0 + e;
+          cb[e] = (jvalid && k < n) ? brow[(k >> 2) * 128 + (k & 3)] : 0.f;
+        }
+      }
+    };
+    auto add_mask = [&](int t, float (&sv)[C::BKV]) {
+      const int k0 = t * C::BKV;
+      if (k0 + C::BKV <= n) {
+        if (mrow) {
+#pragma unroll
+          for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
+            const float4 m = ldg_f4_hint(mrow + k0 + 4 * e4, pol_bias);
+            sv[4 * e4] += m.x;
+            sv[4 * e4 + 1] += m.y;
+            sv[4 * e4 + 2] += m.z;
+            sv[4 * e4 + 3] += m.w;
           }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < C::BKV; ++e) {
+          const int k = k0 + e;
+          sv[e] = k < n ? sv[e] + (mrow ? mrow[k] : 0.f) : -INFINITY;
         }
       }
     };
@@ -541,16 +580,16 @@ __global__ void __launch_bounds__(192, 2)
       for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
       return true;
     };
-    // strict (32-key tiles): the next tile's additive terms are prefetched
-    // into registers while the current tile is processed; fast (64-key
-    // tiles) loads them in place to stay within 168 registers.
+    // strict (32-key tiles): the next tile's pair bias is prefetched into
+    // registers while the current tile is processed; fast (64-key tiles)
+    // issues the tile's loads before waiting for S, within 168 registers.
     constexpr bool kPrefetch = kStrict;
     float cadd[kPrefetch ? C::BKV : 1];
-    if constexpr (kPrefetch) load_add(0, cadd);
+    if constexpr (kPrefetch) load_bias(0, cadd);
     bool ok = true;
     for (int t = 0; t < nt && ok; ++t) {
       float sv[C::BKV];
-      if constexpr (!kPrefetch) load_add(t, sv);
+      if constexpr (!kPrefetch) load_bias(t, sv);
       if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, g, 26)) {
         ok = false;
         break;
@@ -571,20 +610,22 @@ __global__ void __launch_bounds__(192, 2)
       tc_fence_before();
       mbar_arrive(&s_free[t & 1]);
       if constexpr (kPrefetch) {
-        if (t + 1 < nt) load_add(t + 1, cadd);
+        if (t + 1 < nt) load_bias(t + 1, cadd);
       }
-      float mx = -INFINITY;
+      add_mask(t, sv);
+      // four independent partial maxima / sums (short dependency chains)
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < C::BKV; ++e) mx = fmaxf(mx, sv[e]);
-      const float m_new = fmaxf(m_run, mx);
+      for (int e = 0; e < C::BKV; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], sv[e]);
+      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
       const float alpha = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first tile
-      float lsum = 0.f;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < C::BKV; ++e) {
         sv[e] = ex2_approx((sv[e] - m_new) * kLog2e);
-        lsum += sv[e];
+        ls4[e & 3] += sv[e];
       }
-      l_run = l_run * alpha + lsum;
+      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
       m_run = m_new;
       // P V of tile t-2 is done: fold it and release its buffers (its P
       // buffer is the one P(t) overwrites)
@@ -959,7 +1000,7 @@ struct TriAttnPlan {
     v_hi = take(vc);
     if (strict) v_lo = take(vc);
     ldb = padded_ld(n, 4);
-    if (own_bias) bias = al.template take<float>((size_t)n * kHeads * ldb);
+    if (own_bias) bias = al.template take<float>(bias_elems(n, ldb));
     if (with_mask) mbias = al.template take<float>((size_t)rows * ldb);
     o = take((size_t)rows * n * 128);
   }
@@ -1223,7 +1264,7 @@ __global__ void pack_vt_kernel(const float* __restrict__ src, long long s0, long
   }
 }
 
-// triangle bias [1, H, N, N] -> [j][h][ldb]; mask bias [B, 1, 1, N] -> [b][ldb]
+// triangle bias [1, H, N, N] -> j-blocked (bias_index); mask bias [B, 1, 1, N] -> [b][ldb]
 __global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, long long t2,
                                  long long t3, const float* __restrict__ mb, long long m0,
                                  long long m3, int batch, int n, int ldb, float* bias,
@@ -1237,7 +1278,7 @@ __global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, lon
       const long long hj = e / n;
       const int j = (int)(hj % n);
       const int h = (int)(hj / n);
-      bias[((size_t)j * kHeads + h) * ldb + k] = tb[h * t1 + j * t2 + k * t3];
+      bias[bias_index(j, h, k, ldb)] = tb[h * t1 + j * t2 + k * t3];
     } else {
       const long long f = e - nb;
       const int k = (int)(f % n);
@@ -1269,7 +1310,7 @@ struct CorePlan {
     v_hi = take(vc);
     if (strict) v_lo = take(vc);
     ldb = padded_ld(n, 4);
-    bias = al.template take<float>((size_t)kHeads * n * ldb);
+    bias = al.template take<float>(bias_elems(n, ldb));
     if (with_mask) mbias = al.template take<float>((size_t)batch * ldb);
   }
 };

@@ -18,7 +18,7 @@ batch split of ``python/fireprot/backends/amd/two_gcd_attention.py:53-101``):
   reduce-scatter of ``x`` by rows.
 * TriAttn starting node: q/k/v/gate of row ``i`` come from row ``i``; only
   the pair bias ``b[h, j, k]`` spans all rows -> all-gather of the rank's
-  rows of the j-major bias.
+  rows of the row-blocked bias.
 * TriAttn ending node: the starting form on ``z^T`` -> all-to-all transpose
   of ``z``, starting form, all-to-all transpose back.
 * Transition: per position, local.
@@ -237,8 +237,11 @@ class CudaPhases:
 
     # ---------------------------------------------------------------- TriAttn
     def triattn_bias_buffer(self, shard: RowShard, device):
+        """Row-blocked pair bias for ``world*chunk`` rows, viewed ``[rows, 4*ldb]``:
+        a rank's ``chunk`` rows (a multiple of 32) are one contiguous range."""
         ldb = int(self.lib.fpb_triattn_bias_ld(shard.n))
-        return torch.empty(shard.world * shard.chunk, 4, ldb, dtype=torch.float32, device=device)
+        return torch.empty(shard.world * shard.chunk, 4 * ldb, dtype=torch.float32,
+                           device=device)
 
     def triattn_proj(self, z_loc, mask, shard: RowShard, w: dict, bias_full):
         if shard.rows == 0:

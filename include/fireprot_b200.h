@@ -206,11 +206,15 @@ int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked
                             float eps, int add, int precision, void* workspace,
                             size_t workspace_bytes, cudaStream_t stream);
 /* Triangle attention, starting-node form on the rank's rows: proj writes the
- * rank's rows of the j-major pair bias [n][4][fpb_triattn_bias_ld(n)]; the
- * caller all-gathers it; finish runs attention + gate + output on the rows
+ * rank's rows of the pair bias; the caller all-gathers it; finish runs
+ * attention + gate + output on the rows
  * (z_loc += delta, or delta_out = delta). The ending node is this form on the
  * transposed pair tensor (all-to-all transposes around it). proj and finish
- * share the workspace. */
+ * share the workspace. The bias buffer is row-blocked: for ldb =
+ * fpb_triattn_bias_ld(n), rows are grouped by 32, and rows [32q, 32q + 32m)
+ * occupy the m*32*4*ldb floats starting at float q*32*4*ldb (so a rank whose
+ * r0 and row chunk are multiples of 32 owns one contiguous range); the
+ * buffer holds ceil(n/32)*32*4*ldb floats. */
 size_t fpb_triattn_bias_ld(int n);
 size_t fpb_triattn_shard_workspace_size(int n, int rows, int precision, int with_mask);
 int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int n, int rows, int r0,

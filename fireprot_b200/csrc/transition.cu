@@ -111,20 +111,11 @@ __global__ void __launch_bounds__(192, 1)
       const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
       const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
       const float4* z4 = reinterpret_cast<const float4*>(p.z);
-#pragma unroll 1
-      for (int rr = 0; rr < 32; rr += 4) {
-        float4 x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const long long pr = p0 + warp * 32 + rr + u;
-          x[u] = pr < rows ? __ldg(z4 + pr * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
-          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
-        }
-      }
+      auto src = [&](int row) -> const float4* {
+        const long long pr = p0 + row;
+        return pr < rows ? z4 + pr * 32 : nullptr;
+      };
+      ln_rows_to_a<kStrict, 32, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }

@@ -134,31 +134,22 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
     for (int h = 0; h < 4; ++h) wbh[h] = reinterpret_cast<const float4*>(wb + h * 128)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
-#pragma unroll 1
-    for (int rr = 0; rr < 32; rr += 4) {
-      float4 x[4];
+    auto src = [&](int row) -> const float4* {
+      const long long pr = p0 + row;
+      if (pr >= npairs) return nullptr;
+      const long long r = pr / n, s = pr - r * n;
+      return z4 + (kTrans ? (s * n + r) : (r * n + s)) * 32;
+    };
+    // the 4-head pair bias of each row, on the CUDA cores
+    auto head_bias = [&](int row, float4 y) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const long long pr = p0 + warp * 32 + rr + u;
-        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (pr < npairs) {
-          const long long r = pr / n, s = pr - r * n;
-          x[u] = __ldg(z4 + (kTrans ? (s * n + r) : (r * n + s)) * 32 + lane);
-        }
+      for (int h = 0; h < 4; ++h) {
+        const float b = warp_sum(y.x * wbh[h].x + y.y * wbh[h].y + y.z * wbh[h].z +
+                                 y.w * wbh[h].w);
+        if (lane == h) bias_tile[h * 128 + row] = b;
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = warp * 32 + rr + u;
-        const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
-        a_store4<kStrict>(A, row, lane * 4, y.x, y.y, y.z, y.w);
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float b = warp_sum(y.x * wbh[h].x + y.y * wbh[h].y + y.z * wbh[h].z +
-                                   y.w * wbh[h].w);
-          if (lane == h) bias_tile[h * 128 + row] = b;
-        }
-      }
-    }
+    };
+    ln_rows_to_a<kStrict, 16, true>(A, warp * 32, src, lw, lb, p.eps, head_bias);
     fence_proxy_async_smem();
     mbar_arrive(a_full);
     // named barrier over the 128 row threads: bias_tile complete
@@ -788,24 +779,13 @@ __global__ void __launch_bounds__(192, 1)
       const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
       const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
       const float4* z4 = reinterpret_cast<const float4*>(p.z);
-#pragma unroll 1
-      for (int rr = 0; rr < 32; rr += 4) {
-        float4 x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const long long pr = p0 + warp * 32 + rr + u;
-          x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (pr < npairs) {
-            const long long r = pr / n, s = pr - r * n;
-            x[u] = z4[(kTrans ? (s * n + r) : pr) * 32 + lane];
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
-          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
-        }
-      }
+      auto src = [&](int row) -> const float4* {
+        const long long pr = p0 + row;
+        if (pr >= npairs) return nullptr;
+        const long long r = pr / n, s = pr - r * n;
+        return z4 + (kTrans ? (s * n + r) : pr) * 32;
+      };
+      ln_rows_to_a<kStrict, 32, false>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }

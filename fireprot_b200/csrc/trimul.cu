@@ -99,27 +99,13 @@ __global__ void __launch_bounds__(192, 1)
     const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
     const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
-#pragma unroll 1
-    for (int rr = 0; rr < 32; rr += 4) {
-      float4 x[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = warp * 32 + rr + u;
-        const long long pr = p0 + row;
-        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (pr < npairs) {
-          const long long r = pr / p.ycols, s = pr - r * p.ycols;
-          const long long src = kTrans ? (s * p.zcols + r) : (r * p.zcols + s);
-          x[u] = __ldg(z4 + src * 32 + lane);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = warp * 32 + rr + u;
-        const float4 y = ln_row_warp(x[u], lw, lb, p.eps);
-        a_store4<kStrict>(A, row, lane * 4, y.x, y.y, y.z, y.w);
-      }
-    }
+    auto src = [&](int row) -> const float4* {
+      const long long pr = p0 + row;
+      if (pr >= npairs) return nullptr;
+      const long long r = pr / p.ycols, s = pr - r * p.ycols;
+      return z4 + (kTrans ? (s * p.zcols + r) : (r * p.zcols + s)) * 32;
+    };
+    ln_rows_to_a<kStrict, 32, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
     fence_proxy_async_smem();
     mbar_arrive(a_full);
 
@@ -302,57 +288,47 @@ __global__ void __launch_bounds__(192, 1)
       const float4 lw = reinterpret_cast<const float4*>(p.ln_in_w)[lane];
       const float4 lb = reinterpret_cast<const float4*>(p.ln_in_b)[lane];
       const float4* z4 = reinterpret_cast<const float4*>(p.z);
-#pragma unroll 1
-      for (int rr = 0; rr < 32; rr += 4) {
-        float4 x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int row = warp * 32 + rr + u;
-          x[u] = row < jvalid ? z4[(p0 + row) * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 y = ln_row_warp(x[u], lw, lb, p.eps_in);
-          a_store4<kStrict>(A, warp * 32 + rr + u, lane * 4, y.x, y.y, y.z, y.w);
-        }
-      }
+      auto src = [&](int row) -> const float4* {
+        return row < jvalid ? z4 + (p0 + row) * 32 : nullptr;
+      };
+      ln_rows_to_a<kStrict, 32, false>(A, warp * 32, src, lw, lb, p.eps_in, NoRowHook{});
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }
     // ---- A2 = LN_out(x). The x tile is one contiguous [128 c][128 rows]
-    // block; thread t owns row t. Pass 1 streams it for shifted sums (a
-    // stable variance with no row kept in registers), pass 2 re-reads it
-    // (L1/L2 resident) to normalise into the A tile.
+    // block; thread t owns row t and loads its 128 channels in one batch
+    // (coalesced across the warp), then normalises them from registers
+    // (two-pass mean / variance) once GEMM 1 has released A.
     const int t = warp * 32 + lane;
     const bool valid = t < jvalid;
     {
       const size_t tile_elems = (size_t)blockIdx.x * 128 * 128;
       const void* xt = kStrict ? (const void*)(static_cast<const float*>(p.x) + tile_elems)
                                : (const void*)(static_cast<const __nv_bfloat16*>(p.x) + tile_elems);
-      const float shift = x_at<kStrict>(xt, 0, t);
-      float s1 = 0.f, s2 = 0.f;
-#pragma unroll 16
+      float xv[128];
+#pragma unroll
+      for (int c = 0; c < 128; ++c) xv[c] = x_at<kStrict>(xt, c, t);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) s4[c & 3] += xv[c];
+      const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 128.0f);
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
       for (int c = 0; c < 128; ++c) {
-        const float d = x_at<kStrict>(xt, c, t) - shift;
-        s1 += d;
-        s2 += d * d;
+        const float d = xv[c] - mean;
+        q4[c & 3] += d * d;
       }
-      const float m1 = s1 * (1.0f / 128.0f);
-      const float mean = shift + m1;
-      const float var = fmaxf(s2 * (1.0f / 128.0f) - m1 * m1, 0.f);
+      const float var = ((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.0f / 128.0f);
       const float rs = rsqrtf(var + p.eps_out);
       // the MMAs of GEMM 1 must have finished reading A before it is reused
       const bool ok = mbar_wait(a_free, 0, g, 5);
       if (ok) {
-#pragma unroll 4
-        for (int c = 0; c < 128; c += 4) {
-          const float v0 = x_at<kStrict>(xt, c, t), v1 = x_at<kStrict>(xt, c + 1, t);
-          const float v2 = x_at<kStrict>(xt, c + 2, t), v3 = x_at<kStrict>(xt, c + 3, t);
-          a_store4<kStrict>(A, t, c, (v0 - mean) * rs * lnp[c] + lnp[128 + c],
-                            (v1 - mean) * rs * lnp[c + 1] + lnp[129 + c],
-                            (v2 - mean) * rs * lnp[c + 2] + lnp[130 + c],
-                            (v3 - mean) * rs * lnp[c + 3] + lnp[131 + c]);
-        }
+#pragma unroll
+        for (int c = 0; c < 128; c += 4)
+          a_store4<kStrict>(A, t, c, (xv[c] - mean) * rs * lnp[c] + lnp[128 + c],
+                            (xv[c + 1] - mean) * rs * lnp[c + 1] + lnp[129 + c],
+                            (xv[c + 2] - mean) * rs * lnp[c + 2] + lnp[130 + c],
+                            (xv[c + 3] - mean) * rs * lnp[c + 3] + lnp[131 + c]);
       }
       fence_proxy_async_smem();
       mbar_arrive(a_full);

@@ -290,25 +290,34 @@ struct AttnCoreArgs {
 
 template <bool kStrict>
 struct AttnCfg {
-  static constexpr int BQ = 128;
-  // key tile: one 128-byte row of V^T (32 fp32 keys strict / 64 bf16 fast)
-  static constexpr int BKV = kStrict ? 32 : 64;
+  static constexpr int BQ = 128;                       // queries per CTA
+  static constexpr int BKV = 48;                       // keys per tile
   static constexpr int ESZ = kStrict ? 4 : 2;
   static constexpr int NSPLIT = kStrict ? 2 : 1;
-  static constexpr int QK_ROW = 32 * ESZ;                 // bytes per q/k row (128 / 64)
-  static constexpr int Q_BYTES = BQ * QK_ROW;             // per split
-  static constexpr int K_BYTES = BKV * QK_ROW;            // per split
-  static constexpr int V_ATOM_KEYS = 128 / ESZ;           // keys per 128-byte row
-  static constexpr int V_ATOMS = BKV / V_ATOM_KEYS;       // 1
-  static constexpr int V_BYTES = V_ATOMS * 32 * 128;      // per split
+  static constexpr int QK_ROW = 32 * ESZ;              // bytes per q/k row (128 / 64)
+  static constexpr int Q_BYTES = BQ * QK_ROW;          // per split
+  static constexpr int K_BYTES = BKV * QK_ROW;         // per split
+  // V^T atoms: 64-byte rows of 16 fp32 keys (strict, 3 per tile) or
+  // 128-byte rows of 64 bf16 keys (fast, 1 per tile), 32 rows (d) each
+  static constexpr int V_ROW = kStrict ? 64 : 128;
+  static constexpr int V_ATOM_KEYS = V_ROW / ESZ;
+  static constexpr int V_ATOMS = (BKV + V_ATOM_KEYS - 1) / V_ATOM_KEYS;
+  static constexpr int V_ATOM_BYTES = 32 * V_ROW;
+  static constexpr int V_BYTES = V_ATOMS * V_ATOM_BYTES;  // per split
   static constexpr int KV_STAGE = NSPLIT * (K_BYTES + V_BYTES);
-  static constexpr int KV_STAGES = kStrict ? 4 : 6;
-  // TMEM columns: S[2] (BKV each), P V[2] (32 each), P[2] (P_COLS each:
-  // tf32 hi | lo in strict mode, bf16 pairs in fast mode)
-  static constexpr int P_COLS = kStrict ? 2 * BKV : BKV / 2;
-  static constexpr uint32_t kS = 0, kPV = 2 * BKV, kP = 2 * BKV + 64;
+  static constexpr int KV_STAGES = kStrict ? 3 : 8;
+  static constexpr int QK_STEPS = QK_ROW / 32;         // 32-byte K steps over d
+  static constexpr int KSTEP_KEYS = kStrict ? 8 : 16;  // keys per P V K step
+  static constexpr int PV_STEPS = BKV / KSTEP_KEYS;
+  // TMEM: two S/P buffers (S(t) is read, then P(t) overwrites it: tf32
+  // hi | lo = 2 BKV columns, bf16 pairs = BKV / 2) and O (32 columns)
+  static constexpr int BUF_COLS = kStrict ? 2 * BKV : BKV;
+  static constexpr uint32_t kO = 2 * BUF_COLS;
   static constexpr int TMEM_COLS = 256;
-  static_assert(2 * BKV + 64 + 2 * P_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(2 * BUF_COLS + 32 <= TMEM_COLS, "TMEM budget");
+  static_assert(BKV % KSTEP_KEYS == 0 && BKV % 16 == 0, "key tile shape");
+  static_assert(KV_STAGE % 1024 == 0 && (NSPLIT * K_BYTES) % 1024 == 0, "stage alignment");
+  static constexpr int THREADS = 192;  // 4 softmax warps, TMA warp, MMA warp
   static constexpr int SMEM =
       tmem_safe_smem(NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + 1024 + 256, TMEM_COLS);
 };
@@ -321,12 +330,21 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
     return umma_desc_sw64(addr);
 }
 
-// Pipeline per CTA (one MMA thread, one TMA thread, 128 softmax threads):
-//   MMA:     S(t) = Q K_t^T -> S[t%2];  P V(t-1) = P[(t-1)%2] (TMEM) x V_{t-1}
-//   softmax: read S(t), online max/exp/sum, fold P V(t-2) into registers,
-//            write P(t) to TMEM P[t%2]
-// P and P V are double-buffered, so the softmax of tile t never waits for
-// the P V product of tile t-1; it folds the one of tile t-2.
+// One CTA = 128 queries j of one (pair row i, head h), two CTAs per SM (a
+// tcgen05.mma is issued every ~50 cycles by one thread whatever its N below
+// 128, so two issuing threads per SM double the small-MMA rate).
+//   MMA warp:     S(t) = Q K_t^T -> TMEM buffer t%2;
+//                 O += P(t) V_t (P(t) read from the same buffer)
+//   softmax warps (thread = query row = TMEM lane):
+//                 read S(t), add the pair bias (prefetched a tile ahead)
+//                 and the mask bias, exponentiate against a running
+//                 reference max, write P(t) over S(t).
+// O stays in TMEM for the whole key loop. The reference max of a row only
+// moves when the tile max exceeds it by more than 8 in log2 units (P <=
+// 2^8), and O and the row sum are then rescaled; numerator and denominator
+// always use the same reference, so the result is the exact softmax.
+// S(t+2) reuses buffer t%2 once P V(t) has retired, so the softmax of
+// tile t+1 never waits on the tensor pipe.
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 2)
     attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
@@ -345,12 +363,10 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + C::KV_STAGES;
-  uint64_t* s_full = kv_empty + C::KV_STAGES;   // [2]
-  uint64_t* s_free = s_full + 2;                // [2]
-  uint64_t* p_full = s_free + 2;                // [2]
-  uint64_t* pv_full = p_full + 2;               // [2]
-  uint64_t* pv_free = pv_full + 2;              // [2]
-  uint64_t* drain = pv_free + 2;
+  uint64_t* s_full = kv_empty + C::KV_STAGES;   // [2 buffers]
+  uint64_t* p_full = s_full + 2;                // [2 buffers]
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* drain = pv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -368,11 +384,9 @@ __global__ void __launch_bounds__(192, 2)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
       mbar_init(&p_full[b], 128);
-      mbar_init(&pv_full[b], 1);
-      mbar_init(&pv_free[b], 128);
     }
+    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -394,21 +408,23 @@ __global__ void __launch_bounds__(192, 2)
       const uint64_t pol_q = policy_evict_first();
       mbar_arrive_expect_tx(q_full, C::NSPLIT * C::Q_BYTES);
       tma_load_3d_hint(Q, &mq_hi, q_full, 0, jt * C::BQ, ih, pol_q);
-      if constexpr (kStrict)
-        tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
+      if constexpr (kStrict) tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int s = t % C::KV_STAGES;
         const uint32_t ph = (t / C::KV_STAGES) & 1;
         if (t >= C::KV_STAGES && !mbar_wait(&kv_empty[s], ph ^ 1, g, 21)) break;
         uint8_t* st = KV + s * C::KV_STAGE;
+        uint8_t* vst = st + C::NSPLIT * C::K_BYTES;
         mbar_arrive_expect_tx(&kv_full[s], C::KV_STAGE);
         tma_load_3d(st, &mk_hi, &kv_full[s], 0, t * C::BKV, ih);
-        uint8_t* vst = st + C::NSPLIT * C::K_BYTES;
-        tma_load_3d(vst, &mv_hi, &kv_full[s], t * C::BKV, 0, ih);
-        if constexpr (kStrict) {
-          tma_load_3d(st + C::K_BYTES, &mk_lo, &kv_full[s], 0, t * C::BKV, ih);
-          tma_load_3d(vst + C::V_BYTES, &mv_lo, &kv_full[s], t * C::BKV, 0, ih);
+        if constexpr (kStrict) tma_load_3d(st + C::K_BYTES, &mk_lo, &kv_full[s], 0, t * C::BKV, ih);
+#pragma unroll
+        for (int a = 0; a < C::V_ATOMS; ++a) {
+          const int key = t * C::BKV + a * C::V_ATOM_KEYS;
+          tma_load_3d(vst + a * C::V_ATOM_BYTES, &mv_hi, &kv_full[s], key, 0, ih);
+          if constexpr (kStrict)
+            tma_load_3d(vst + C::V_BYTES + a * C::V_ATOM_BYTES, &mv_lo, &kv_full[s], key, 0, ih);
         }
         ++issued;
       }
@@ -424,51 +440,12 @@ __global__ void __launch_bounds__(192, 2)
     if (lane == 0) {
       const uint32_t id_s = kStrict ? idesc_tf32(128, C::BKV) : idesc_bf16(128, C::BKV);
       const uint32_t id_o = kStrict ? idesc_tf32(128, 32) : idesc_bf16(128, 32);
-      const uint32_t q_hi = smem_u32(Q), q_lo = smem_u32(Q + C::Q_BYTES);
-      constexpr int QK_STEPS = C::QK_ROW / 32;  // 32-byte K steps over d
-      bool ok = mbar_wait(q_full, 0, g, 22);
-      auto issue_pv = [&](int u) -> bool {
-        const int b = u & 1;
-        if (!mbar_wait(&p_full[b], (u >> 1) & 1, g, 23)) return false;
-        if (u >= 2 && !mbar_wait(&pv_free[b], ((u - 2) >> 1) & 1, g, 29)) return false;
-        tc_fence_after();
-        const uint32_t vst =
-            smem_u32(KV + (u % C::KV_STAGES) * C::KV_STAGE + C::NSPLIT * C::K_BYTES);
-        const uint32_t pa = tmem + C::kP + b * C::P_COLS;
-        const uint32_t dpv = tmem + C::kPV + b * 32;
+      const uint32_t q_hi = smem_u32(Q), q_lo = q_hi + C::Q_BYTES;
+      auto issue_s = [&](int t) {
+        const uint32_t kst = smem_u32(KV + (t % C::KV_STAGES) * C::KV_STAGE);
+        const uint32_t sbuf = tmem + (t & 1) * C::BUF_COLS;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {  // 4 x 32-byte K steps over the tile's keys
-          const uint32_t acc = kk == 0 ? 0u : 1u;
-          const uint64_t dvh = umma_desc_sw128(vst + kk * 32);
-          if constexpr (kStrict) {
-            const uint64_t dvl = umma_desc_sw128(vst + C::V_BYTES + kk * 32);
-            umma_tf32_ts(dpv, pa + kk * 8, dvh, id_o, acc);             // P_hi V_hi
-            umma_tf32_ts(dpv, pa + kk * 8, dvl, id_o, 1u);              // P_hi V_lo
-            umma_tf32_ts(dpv, pa + C::BKV + kk * 8, dvh, id_o, 1u);     // P_lo V_hi
-          } else {
-            umma_bf16_ts(dpv, pa + kk * 8, dvh, id_o, acc);
-          }
-        }
-        umma_commit(&pv_full[b]);
-        umma_commit(&kv_empty[u % C::KV_STAGES]);
-        return true;
-      };
-      if (ok) tc_fence_after();
-      for (int t = 0; t < nt && ok; ++t) {
-        const int s = t % C::KV_STAGES;
-        if (!mbar_wait(&kv_full[s], (t / C::KV_STAGES) & 1, g, 24)) {
-          ok = false;
-          break;
-        }
-        if (t >= 2 && !mbar_wait(&s_free[t & 1], ((t - 2) >> 1) & 1, g, 25)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kst = smem_u32(KV + s * C::KV_STAGE);
-        const uint32_t sbuf = tmem + C::kS + (t & 1) * C::BKV;
-#pragma unroll
-        for (int kk = 0; kk < QK_STEPS; ++kk) {
+        for (int kk = 0; kk < C::QK_STEPS; ++kk) {
           const uint32_t off = kk * 32;
           const uint64_t dqh = qk_desc<kStrict>(q_hi + off);
           const uint64_t dkh = qk_desc<kStrict>(kst + off);
@@ -484,12 +461,62 @@ __global__ void __launch_bounds__(192, 2)
           }
         }
         umma_commit(&s_full[t & 1]);
-        if (t >= 1 && !issue_pv(t - 1)) {
+      };
+      auto issue_pv = [&](int t) {
+        const uint32_t vst =
+            smem_u32(KV + (t % C::KV_STAGES) * C::KV_STAGE + C::NSPLIT * C::K_BYTES);
+        const uint32_t pa = tmem + (t & 1) * C::BUF_COLS;
+        const uint32_t d_o = tmem + C::kO;
+#pragma unroll
+        for (int kk = 0; kk < C::PV_STEPS; ++kk) {
+          const uint32_t acc = (t == 0 && kk == 0) ? 0u : 1u;
+          // K step kk: V^T atom key / V_ATOM_KEYS, 32-byte offset in its row
+          const int key = kk * C::KSTEP_KEYS;
+          const uint32_t vo =
+              (key / C::V_ATOM_KEYS) * C::V_ATOM_BYTES + (key % C::V_ATOM_KEYS) * C::ESZ;
+          if constexpr (kStrict) {
+            const uint64_t dvh = umma_desc_sw64(vst + vo);
+            const uint64_t dvl = umma_desc_sw64(vst + C::V_BYTES + vo);
+            umma_tf32_ts(d_o, pa + kk * 8, dvh, id_o, acc);             // P_hi V_hi
+            umma_tf32_ts(d_o, pa + kk * 8, dvl, id_o, 1u);              // P_hi V_lo
+            umma_tf32_ts(d_o, pa + C::BKV + kk * 8, dvh, id_o, 1u);     // P_lo V_hi
+          } else {
+            umma_bf16_ts(d_o, pa + kk * 8, umma_desc_sw128(vst + vo), id_o, acc);
+          }
+        }
+        umma_commit(pv_done);
+      };
+      bool ok = mbar_wait(q_full, 0, g, 22);
+      if (ok) tc_fence_after();
+      // S of the first two tiles fill both buffers
+      for (int t = 0; t < 2 && t < nt && ok; ++t) {
+        if (!mbar_wait(&kv_full[t], 0, g, 24)) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        issue_s(t);
       }
-      if (ok && nt >= 1) ok = issue_pv(nt - 1);
+      for (int t = 0; t < nt && ok; ++t) {
+        if (!mbar_wait(&p_full[t & 1], (t >> 1) & 1, g, 23)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(t);
+        umma_commit(&kv_empty[t % C::KV_STAGES]);
+        if (t + 2 < nt) {
+          const int t2 = t + 2;
+          // buffer t%2 holds P(t): S(t+2) overwrites it once P V(t) retired
+          if (!mbar_wait(&kv_full[t2 % C::KV_STAGES], (t2 / C::KV_STAGES) & 1, g, 24) ||
+              !mbar_wait(pv_done, t & 1, g, 25)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(t2);
+        }
+      }
       if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
@@ -497,21 +524,17 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int t_row = warp * 32 + lane;  // TMEM lane / query row in tile
+    const int quad = warp;
+    const int t_row = quad * 32 + lane;  // TMEM lane / query row in the tile
     const int j = jt * C::BQ + t_row;
     const bool jvalid = j < n;
+    const uint32_t tb = tmem + ((uint32_t)(quad * 32) << 16);
     // this thread's row of the j-blocked bias: key k at brow[(k >> 2) * 128 + (k & 3)]
     const float* brow = p.bias + bias_index(jvalid ? j : 0, h, 0, p.ldb);
     const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
-    // the pair bias (every row i reads all of it) and the mask bias row stay in L2
+    constexpr float kRescale = 8.0f / kLog2e;  // move the reference max past 2^8
     const uint64_t pol_bias = policy_evict_last();
-    float m_run = -INFINITY, l_run = 0.f;
-    float a1 = 0.f, a2 = 0.f;  // alpha of the previous / second previous tile
-    float o[32];
-#pragma unroll
-    for (int d = 0; d < 32; ++d) o[d] = 0.f;
     // Additive terms of key tile t: the pair bias (a different row per
     // thread) is loaded in one batch a tile ahead and added to q.k first;
     // the mask bias row (the same for every thread, an L1 hit) and -inf past
@@ -558,111 +581,107 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
     };
-    // fold P V(u) (scale factor alpha_u) into the register accumulator
-    auto fold = [&](int u, float alpha) -> bool {
-      const int b = u & 1;
-      if (!mbar_wait(&pv_full[b], (u >> 1) & 1, g, 27)) return false;
-      tc_fence_after();
-      float pv[32];
-      tmem_row32(tmem + C::kPV + b * 32, warp, 0, pv);
-      tc_fence_before();
-      mbar_arrive(&pv_free[b]);
-#pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha + pv[d];
-      return true;
-    };
-    // strict (32-key tiles): the next tile's pair bias is prefetched into
-    // registers while the current tile is processed; fast (64-key tiles)
-    // issues the tile's loads before waiting for S, within 168 registers.
-    constexpr bool kPrefetch = kStrict;
-    float cadd[kPrefetch ? C::BKV : 1];
-    if constexpr (kPrefetch) load_bias(0, cadd);
+    float m_ref = -INFINITY, l_run = 0.f;
+    float cb[C::BKV];
+    load_bias(0, cb);
     bool ok = true;
     for (int t = 0; t < nt && ok; ++t) {
+      const uint32_t buf = tb + (t & 1) * C::BUF_COLS;
       float sv[C::BKV];
-      if constexpr (!kPrefetch) load_bias(t, sv);
       if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, g, 26)) {
         ok = false;
         break;
       }
       tc_fence_after();
 #pragma unroll
-      for (int q = 0; q < C::BKV / 32; ++q) {
-        float tmp[32];
-        tmem_row32(tmem + C::kS + (t & 1) * C::BKV, warp, q * 32, tmp);
+      for (int c = 0; c < C::BKV / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(buf + c * 16, r);
+        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if constexpr (kPrefetch)
-            sv[q * 32 + e] = tmp[e] + cadd[q * 32 + e];
-          else
-            sv[q * 32 + e] = tmp[e] + sv[q * 32 + e];
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[t & 1]);
-      if constexpr (kPrefetch) {
-        if (t + 1 < nt) load_bias(t + 1, cadd);
+        for (int e = 0; e < 16; ++e) sv[c * 16 + e] = __uint_as_float(r[e]) + cb[c * 16 + e];
       }
       add_mask(t, sv);
+      if (t + 1 < nt) load_bias(t + 1, cb);
       // four independent partial maxima / sums (short dependency chains)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int e = 0; e < C::BKV; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], sv[e]);
-      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
-      const float alpha = ex2_approx((m_run - m_new) * kLog2e);  // 0 on the first tile
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const bool move = mx > m_ref + kRescale;  // always on the first tile
+      const float m_new = move ? mx : m_ref;
+      const float alpha = move ? ex2_approx((m_ref - m_new) * kLog2e) : 1.0f;
+      m_ref = m_new;
+      // P(t) over S(t) (A operand of P V), 16 keys at a time
       float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < C::BKV; ++e) {
-        sv[e] = ex2_approx((sv[e] - m_new) * kLog2e);
-        ls4[e & 3] += sv[e];
-      }
-      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
-      m_run = m_new;
-      // P V of tile t-2 is done: fold it and release its buffers (its P
-      // buffer is the one P(t) overwrites)
-      if (t >= 2 && !fold(t - 2, a2)) {
-        ok = false;
-        break;
-      }
-      a2 = a1;
-      a1 = alpha;
-      // P(t) -> TMEM (A operand of P V)
-      const uint32_t pdst = tmem + lane_off + C::kP + (t & 1) * C::P_COLS;
-      if constexpr (kStrict) {
-        // hi at columns [0, 32), lo = x - hi (exact) at [32, 64), 16 at a time
+      for (int c = 0; c < C::BKV / 16; ++c) {
+        float pv[16];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int e = 0; e < 16; ++e) {
+          pv[e] = ex2_approx((sv[c * 16 + e] - m_ref) * kLog2e);
+          ls4[e & 3] += pv[e];
+        }
+        if constexpr (kStrict) {
+          // hi at columns [0, BKV), lo = x - hi (exact) at [BKV, 2 BKV)
           uint32_t part[16];
 #pragma unroll
+          for (int e = 0; e < 16; ++e) part[e] = __float_as_uint(pv[e]) & 0xFFFFE000u;
+          tmem_st16(buf + c * 16, part);
+#pragma unroll
           for (int e = 0; e < 16; ++e)
-            part[e] = __float_as_uint(sv[half * 16 + e]) & 0xFFFFE000u;
-          tmem_st16(pdst + half * 16, part);
+            part[e] = __float_as_uint(pv[e] - __uint_as_float(__float_as_uint(pv[e]) & 0xFFFFE000u));
+          tmem_st16(buf + C::BKV + c * 16, part);
+        } else {
+          // bf16 pairs: 16 keys -> 8 columns
+          uint32_t pk[8];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float x = sv[half * 16 + e];
-            part[e] = __float_as_uint(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+          for (int e = 0; e < 8; ++e) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[2 * e], pv[2 * e + 1]);
+            pk[e] = *reinterpret_cast<uint32_t*>(&b2);
           }
-          tmem_st16(pdst + C::BKV + half * 16, part);
+          tmem_st8(buf + c * 8, pk);
         }
-      } else {
-        uint32_t pk[32];
+      }
+      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+      // Observe every completion of pv_done in order (a parity wait cannot
+      // tell phase k from phase k - 2): P V(t-1) was issued when this tile
+      // started, so it has normally retired by now. Then a moved reference
+      // rescales O (all P V up to t-1) before P V(t) accumulates into it.
+      if (t > 0) {
+        if (!mbar_wait(pv_done, (t - 1) & 1, g, 27)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (t > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          __nv_bfloat162 b2 = __floats2bfloat162_rn(sv[2 * e], sv[2 * e + 1]);
-          pk[e] = *reinterpret_cast<uint32_t*>(&b2);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t ov[16];
+          tmem_ld16(tb + C::kO + c * 16, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int d = 0; d < 16; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+          tmem_st16(tb + C::kO + c * 16, ov);
         }
-        tmem_st32(pdst, pk);
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t & 1]);
     }
-    if (ok && nt >= 2) ok = fold(nt - 2, a2);
-    if (ok && nt >= 1) ok = fold(nt - 1, a1);
-    if (ok) {
+    if (ok && mbar_wait(pv_done, (nt - 1) & 1, g, 28)) {
+      tc_fence_after();
       const float inv = 1.0f / l_run;
+      float o[32];
 #pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] *= inv;
+      for (int c = 0; c < 2; ++c) {
+        uint32_t ov[16];
+        tmem_ld16(tb + C::kO + c * 16, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int d = 0; d < 16; ++d) o[c * 16 + d] = __uint_as_float(ov[d]) * inv;
+      }
       if (jvalid) {
         const size_t orow = (size_t)i * n + j;
         if (kStrict || p.o_f32) {
@@ -677,9 +696,9 @@ __global__ void __launch_bounds__(192, 2)
           for (int e = 0; e < 4; ++e) {
             uint32_t w4[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * e + 2 * u], o[8 * e + 2 * u + 1]);
-              w4[u] = *reinterpret_cast<uint32_t*>(&b2);
+            for (int q = 0; q < 4; ++q) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * e + 2 * q], o[8 * e + 2 * q + 1]);
+              w4[q] = *reinterpret_cast<uint32_t*>(&b2);
             }
             dst[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
@@ -694,6 +713,53 @@ __global__ void __launch_bounds__(192, 2)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// Tensor maps and launch of the attention core over nh = rows x 4 (row,
+// head) pairs: q, k [nh][n][32] (hi/lo or bf16), v^T [nh][32][ldv].
+int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const void* k_lo,
+                     const void* v_hi, const void* v_lo, int n, int rows, int ldv,
+                     const AttnCoreArgs& ca, bool strict, cudaStream_t stream) {
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const uint64_t rowb = 32ull * esz;
+  const uint64_t nh = (uint64_t)rows * kHeads;
+  const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
+  const uint32_t vkeys = strict ? AttnCfg<true>::V_ATOM_KEYS : AttnCfg<false>::V_ATOM_KEYS;
+  const CUtensorMapSwizzle vsw = strict ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+  bool ok = make_map_3d(&mqh, q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+            make_map_3d(&mkh, k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
+            make_map_3d(&mvh, v_hi, dt, n, 32, nh, (uint64_t)ldv * esz,
+                        (uint64_t)ldv * esz * 32, vkeys, 32, 1, vsw);
+  if (strict)
+    ok = ok && make_map_3d(&mql, q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+         make_map_3d(&mkl, k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
+         make_map_3d(&mvl, v_lo, dt, n, 32, nh, (uint64_t)ldv * esz, (uint64_t)ldv * esz * 32,
+                     vkeys, 32, 1, vsw);
+  else {
+    mql = mqh;
+    mkl = mkh;
+    mvl = mvh;
+  }
+  if (!ok) return kErrArg;
+  dim3 grid((n + 127) / 128, kHeads, rows);
+  if (strict) {
+    auto k = attn_core_kernel<true>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
+    FPB_LAUNCH("triattn_core", stream,
+               k<<<grid, AttnCfg<true>::THREADS, AttnCfg<true>::SMEM, stream>>>(
+                   mqh, mql, mkh, mkl, mvh, mvl, ca));
+  } else {
+    auto k = attn_core_kernel<false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
+    FPB_LAUNCH("triattn_core", stream,
+               k<<<grid, AttnCfg<false>::THREADS, AttnCfg<false>::SMEM, stream>>>(
+                   mqh, mql, mkh, mkl, mvh, mvl, ca));
+  }
+  return launch_status();
 }
 
 // ============================================================================
@@ -1026,43 +1092,10 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
   CUtensorMap moh, mol;
   if (!make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol)) return kErrArg;
   {
-    const int esz = strict ? 4 : 2;
-    const CUtensorMapDataType dt =
-        strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    const uint64_t rowb = 32ull * esz;
-    CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
-    const uint64_t nh = (uint64_t)rows * kHeads;
-    const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
-    bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-              make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
-              make_map_3d(&mvh, pl.v_hi, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
-                          (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
-    if (strict)
-      ok = ok && make_map_3d(&mql, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-           make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
-           make_map_3d(&mvl, pl.v_lo, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
-                       (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
-    else {
-      mql = mqh;
-      mkl = mkh;
-      mvl = mvh;
-    }
-    if (!ok) return kErrArg;
     AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0};
-    dim3 grid((n + 127) / 128, kHeads, rows);
-    if (strict) {
-      auto k = attn_core_kernel<true>;
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
-      FPB_LAUNCH("triattn_core", stream,
-                 k<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
-    } else {
-      auto k = attn_core_kernel<false>;
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
-      FPB_LAUNCH("triattn_core", stream,
-                 k<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
-    }
-    if ((st = launch_status())) return st;
+    if ((st = launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, rows,
+                               pl.ldv, ca, strict, stream)))
+      return st;
   }
   AttnOutArgs oa{z_loc, delta_out, n, rows, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
   const long long npairs = (long long)rows * n;
@@ -1365,42 +1398,8 @@ extern "C" int fpb_attention_core(const float* q, const long long* q_strides, co
                                                         with_mask ? mbs[3] : 0, batch, n, pl.ldb,
                                                         pl.bias, pl.mbias));
   if ((st = launch_status())) return st;
-  const int esz = strict ? 4 : 2;
-  const CUtensorMapDataType dt =
-      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  const uint64_t rowb = 32ull * esz;
-  const uint64_t nh = (uint64_t)batch * kHeads;
-  const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
-  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
-  bool ok = make_map_3d(&mqh, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-            make_map_3d(&mkh, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
-            make_map_3d(&mvh, pl.v_hi, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
-                        (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
-  if (strict)
-    ok = ok && make_map_3d(&mql, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-         make_map_3d(&mkl, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
-         make_map_3d(&mvl, pl.v_lo, dt, n, 32, nh, (uint64_t)pl.ldv * esz,
-                     (uint64_t)pl.ldv * esz * 32, 128 / esz, 32, 1);
-  else {
-    mql = mqh;
-    mkl = mkh;
-    mvl = mvh;
-  }
-  if (!ok) return kErrArg;
   // this boundary returns FP32 [B, N, H, D] in both precision modes
   AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1};
-  dim3 grid((n + 127) / 128, kHeads, batch);
-  if (strict) {
-    auto kk = attn_core_kernel<true>;
-    cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
-    FPB_LAUNCH("triattn_core", stream,
-               kk<<<grid, 192, AttnCfg<true>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
-  } else {
-    auto kk = attn_core_kernel<false>;
-    cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
-    FPB_LAUNCH("triattn_core", stream,
-               kk<<<grid, 192, AttnCfg<false>::SMEM, stream>>>(mqh, mql, mkh, mkl, mvh, mvl, ca));
-  }
-  return launch_status();
+  return launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, batch, pl.ldv,
+                          ca, strict, stream);
 }

@@ -35,7 +35,7 @@ def _mask(kind, n):
     return m
 
 
-@pytest.mark.parametrize("n", [7, 33, 124, 200])
+@pytest.mark.parametrize("n", [7, 33, 96, 124, 144, 200, 257])
 @pytest.mark.parametrize("starting", [True, False])
 @pytest.mark.parametrize("precision", ["strict", "fast"])
 @pytest.mark.parametrize("mask_kind", ["none", "random", "padding"])
@@ -73,3 +73,29 @@ def test_triattn_c1_known_answer(cuda_device):
     out = ops.triattn(z.to(cuda_device), mask.to(cuda_device), _weights(p, cuda_device),
                       starting=True, precision="strict")
     assert O.rel_max_err(out, ref) <= O.STRICT_TOL
+
+
+@pytest.mark.parametrize("n", [48, 96, 100, 144, 300])
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+def test_attention_core_key_tile_weights(cuda_device, n, precision):
+    """Uniform softmax (q = 0, zero bias) over V that one-hot encodes each
+    key's 48-key tile and carries the key index: every output row must give
+    each key tile its share of the weight and the mean key index, whatever
+    the number of key tiles and whether the last one is full."""
+    from fireprot_b200 import ops
+    q = torch.zeros(1, 4, n, 32, device=cuda_device)
+    k = torch.randn(1, 4, n, 32, generator=torch.Generator().manual_seed(n)).to(cuda_device)
+    v = torch.zeros(1, 4, n, 32)
+    keys = torch.arange(n)
+    v[0, :, keys, torch.clamp(keys // 48, max=30)] = 1.0
+    v[0, :, :, 31] = keys.float()
+    tb = torch.zeros(1, 4, n, n, device=cuda_device)
+    o = ops.attention_core(q, k, v.to(cuda_device), [tb], precision=precision).cpu()
+    expect = torch.zeros(32)
+    for t in range((n + 47) // 48):
+        expect[min(t, 30)] += min(48, n - 48 * t) / n
+    expect[31] = (n - 1) / 2
+    tol = 1e-5 if precision == "strict" else 1e-2
+    for h in range(4):
+        err = (o[0, :, h] - expect).abs() / expect.abs().clamp(min=1.0)
+        assert err.max().item() <= tol, (h, o[0, 0, h, :8], expect[:8])

@@ -16,6 +16,19 @@ thread_local int g_composite_depth = 0;
 CompositeCall::CompositeCall() { ++g_composite_depth; }
 CompositeCall::~CompositeCall() { --g_composite_depth; }
 
+int sm_count() {
+  static int cached[64] = {0};  // benign race: every writer stores the same value
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int c = 0;
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0)
+      c = 148;
+    cached[dev] = c;
+  }
+  return cached[dev];
+}
+
 int reset_status(void* workspace, cudaStream_t stream) {
   if (g_composite_depth > 0) return kOk;
   return cudaMemsetAsync(workspace, 0, kWsHeader, stream) == cudaSuccess ? kOk : kErrCuda;

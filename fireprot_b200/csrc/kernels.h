@@ -78,6 +78,10 @@ int pack_weights(const PackSrc& src, void* hi, void* lo, bool strict, cudaStream
 bool make_weight_maps(const void* hi, const void* lo, int rows, bool strict, CUtensorMap* mh,
                       CUtensorMap* ml);
 
+// Number of SMs of the current device (cached per device): the grid of a
+// persistent kernel (one CTA per SM walking tiles).
+int sm_count();
+
 // Dynamic shared memory to request so that the number of co-resident CTAs
 // never exceeds what TMEM can hold (512 columns per SM): a CTA never waits
 // inside tcgen05.alloc.

@@ -208,6 +208,7 @@ struct TriMulOutArgs {
   int njb;
   int add;
   int* status;
+  int ntiles;  // rows x njb tiles, walked by a persistent grid
 };
 
 // Element (channel c, tile row t) of a blocked x tile.
@@ -222,9 +223,18 @@ __device__ __forceinline__ float x_at(const void* tile, int c, int t) {
 template <bool kStrict>
 constexpr int out_smem_bytes() {
   using C = RowCfg<kStrict>;
-  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
+  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 512);
 }
 
+// Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ... Per
+// tile, GEMM 1 (gate G = LN_in(z) Wg^T) and GEMM 2 (Y = LN_out(x) Wz^T)
+// share the A tile and write one of two TMEM buffers (256 columns each), so
+// the epilogue of the previous tile runs while GEMM 1 of this one executes,
+// the x row loads overlap GEMM 1 and the next tile's z rows are prefetched
+// into registers during GEMM 2. The weight ring runs on across tiles.
+// Row warps, per tile i:
+//   wait GEMM 2(i-1) -> LN_in(z_i) into A -> epilogue(i-1) -> load x_i ->
+//   wait GEMM 1(i) -> LN_out(x_i) into A -> prefetch z_{i+1}
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 1)
     trimul_out_kernel(const __grid_constant__ CUtensorMap w_hi,
@@ -240,19 +250,17 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(lnp + 256);
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
-  uint64_t* a_full = bars + 2 * WSTAGES;
-  uint64_t* a_free = a_full + 1;
-  uint64_t* done = a_free + 1;
-  uint64_t* drain = done + 1;
+  uint64_t* a_full = bars + 2 * WSTAGES;  // LN_in / LN_out of a tile written to A
+  uint64_t* gdone = a_full + 1;           // GEMM 1 / GEMM 2 of a tile retired
+  uint64_t* tfree = gdone + 1;            // [2] epilogue done reading a TMEM buffer
+  uint64_t* drain = tfree + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  // tile = (pair row i, 128-column block jb): rows never straddle i
-  const int ti = blockIdx.x / p.njb, jb = blockIdx.x % p.njb;
-  const int jvalid = min(128, n - jb * 128);             // valid rows of this tile
-  const long long p0 = (long long)ti * n + jb * 128;     // pair index of tile row 0
+  const int ntiles = p.ntiles;
+  const int nmine = blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -260,8 +268,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&wempty[s], 1);
     }
     mbar_init(a_full, 128);
-    mbar_init(a_free, 1);
-    mbar_init(done, 1);
+    mbar_init(gdone, 1);
+    mbar_init(&tfree[0], 128);
+    mbar_init(&tfree[1], 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -271,7 +280,7 @@ __global__ void __launch_bounds__(192, 1)
     lnp[128 + threadIdx.x] = p.ln_out_b[threadIdx.x];
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -280,63 +289,32 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
   const Guard g{p.status, abort_flag};
   const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
-  constexpr int NLOADS = 2 * C::NKA;
+  constexpr int NLOADS = 2 * C::NKA;  // per tile: GEMM 1 then GEMM 2, K atoms each
 
   if (warp < 4) {
-    // ---- A1 = LN_in(z) (lane-cooperative rows)
-    {
-      const float4 lw = reinterpret_cast<const float4*>(p.ln_in_w)[lane];
-      const float4 lb = reinterpret_cast<const float4*>(p.ln_in_b)[lane];
-      const float4* z4 = reinterpret_cast<const float4*>(p.z);
-      auto src = [&](int row) -> const float4* {
-        return row < jvalid ? z4 + (p0 + row) * 32 : nullptr;
-      };
-      ln_rows_to_a<kStrict, 32, false>(A, warp * 32, src, lw, lb, p.eps_in, NoRowHook{});
-      fence_proxy_async_smem();
-      mbar_arrive(a_full);
-    }
-    // ---- A2 = LN_out(x). The x tile is one contiguous [128 c][128 rows]
-    // block; thread t owns row t and loads its 128 channels in one batch
-    // (coalesced across the warp), then normalises them from registers
-    // (two-pass mean / variance) once GEMM 1 has released A.
-    const int t = warp * 32 + lane;
-    const bool valid = t < jvalid;
-    {
-      const size_t tile_elems = (size_t)blockIdx.x * 128 * 128;
-      const void* xt = kStrict ? (const void*)(static_cast<const float*>(p.x) + tile_elems)
-                               : (const void*)(static_cast<const __nv_bfloat16*>(p.x) + tile_elems);
-      float xv[128];
+    const int t = warp * 32 + lane;  // tile row (TMEM lane)
+    const float4 lw = reinterpret_cast<const float4*>(p.ln_in_w)[lane];
+    const float4 lb = reinterpret_cast<const float4*>(p.ln_in_b)[lane];
+    const float4* z4 = reinterpret_cast<const float4*>(p.z);
+    // tile -> (pair row i, 128-column block jb); rows never straddle i
+    auto tile_p0 = [&](int tile) { return (long long)(tile / p.njb) * n + (tile % p.njb) * 128; };
+    auto tile_rows = [&](int tile) { return min(128, n - (tile % p.njb) * 128); };
+    // z rows of this warp's 32 tile rows, lane-cooperative (lane = 4 channels)
+    float4 zr[32];
+    auto load_z = [&](int tile) {
+      const long long p0 = tile_p0(tile);
+      const int valid = tile_rows(tile);
 #pragma unroll
-      for (int c = 0; c < 128; ++c) xv[c] = x_at<kStrict>(xt, c, t);
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 128; ++c) s4[c & 3] += xv[c];
-      const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 128.0f);
-      float q4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float d = xv[c] - mean;
-        q4[c & 3] += d * d;
+      for (int u = 0; u < 32; ++u) {
+        const int row = warp * 32 + u;
+        zr[u] = row < valid ? z4[(p0 + row) * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      const float var = ((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.0f / 128.0f);
-      const float rs = rsqrtf(var + p.eps_out);
-      // the MMAs of GEMM 1 must have finished reading A before it is reused
-      const bool ok = mbar_wait(a_free, 0, g, 5);
-      if (ok) {
-#pragma unroll
-        for (int c = 0; c < 128; c += 4)
-          a_store4<kStrict>(A, t, c, (xv[c] - mean) * rs * lnp[c] + lnp[128 + c],
-                            (xv[c + 1] - mean) * rs * lnp[c + 1] + lnp[129 + c],
-                            (xv[c + 2] - mean) * rs * lnp[c + 2] + lnp[130 + c],
-                            (xv[c + 3] - mean) * rs * lnp[c + 3] + lnp[131 + c]);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(a_full);
-    }
-    // ---- epilogue: delta = sigmoid(G) * Y, z <- [z +] delta; the z chunk
-    // of the next step is loaded before the current one is processed
-    if (mbar_wait(done, 0, g, 3)) {
-      tc_fence_after();
+    };
+    auto epilogue = [&](int tile, int b) {
+      // delta = sigmoid(G) * Y, z <- [z +] delta; thread t owns row t
+      const long long p0 = tile_p0(tile);
+      const bool valid = t < tile_rows(tile);
+      const uint32_t tb = tmem + b * 256;
       float4* zrow = reinterpret_cast<float4*>(p.z) + (p0 + (valid ? t : 0)) * 32;
       float4 zc[8];
 #pragma unroll
@@ -350,8 +328,8 @@ __global__ void __launch_bounds__(192, 1)
           zn[v4] = (cc < 3 && valid && p.add) ? zrow[(cc + 1) * 8 + v4]
                                               : make_float4(0.f, 0.f, 0.f, 0.f);
         float gv[32], yv[32];
-        tmem_row32(tmem, warp, cc * 32, gv);
-        tmem_row32(tmem, warp, 128 + cc * 32, yv);
+        tmem_row32(tb, warp, cc * 32, gv);
+        tmem_row32(tb, warp, 128 + cc * 32, yv);
         if (valid) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
@@ -366,14 +344,94 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int v4 = 0; v4 < 8; ++v4) zc[v4] = zn[v4];
       }
+    };
+    bool ok = true;
+    if (nmine > 0) load_z(blockIdx.x);
+    for (int it = 0; it < nmine && ok; ++it) {
+      const int tile = blockIdx.x + it * gridDim.x;
+      // A is free once GEMM 2 of the previous tile retired
+      if (it > 0) {
+        if (!mbar_wait(gdone, 1, g, 5)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // ---- A1 = LN_in(z) from the prefetched rows
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float4 y = ln_row_warp(zr[u], lw, lb, p.eps_in);
+        a_store4<kStrict>(A, warp * 32 + u, lane * 4, y.x, y.y, y.z, y.w);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+      // ---- epilogue of the previous tile (overlaps GEMM 1 of this one)
+      if (it > 0) {
+        const int pb = (it - 1) & 1;
+        epilogue(tile - (int)gridDim.x, pb);
+        tc_fence_before();
+        mbar_arrive(&tfree[pb]);
+      }
+      // ---- A2 = LN_out(x): thread t loads its row's 128 channels in one batch
+      {
+        const size_t tile_elems = (size_t)tile * 128 * 128;
+        const void* xt = kStrict ? (const void*)(static_cast<const float*>(p.x) + tile_elems)
+                                 : (const void*)(static_cast<const __nv_bfloat16*>(p.x) + tile_elems);
+        float xv[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) xv[c] = x_at<kStrict>(xt, c, t);
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s4[c & 3] += xv[c];
+        const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 128.0f);
+        float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float d = xv[c] - mean;
+          q4[c & 3] += d * d;
+        }
+        const float var = ((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.0f / 128.0f);
+        const float rs = rsqrtf(var + p.eps_out);
+        // GEMM 1 must have finished reading A before it is reused
+        if (!mbar_wait(gdone, 0, g, 6)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 128; c += 4)
+          a_store4<kStrict>(A, t, c, (xv[c] - mean) * rs * lnp[c] + lnp[128 + c],
+                            (xv[c + 1] - mean) * rs * lnp[c + 1] + lnp[129 + c],
+                            (xv[c + 2] - mean) * rs * lnp[c + 2] + lnp[130 + c],
+                            (xv[c + 3] - mean) * rs * lnp[c + 3] + lnp[131 + c]);
+        fence_proxy_async_smem();
+        mbar_arrive(a_full);
+      }
+      // ---- next tile's z rows (overlap GEMM 2); the last iteration reloads
+      // its own tile so that zr is always redefined here (never live across
+      // the epilogue and LN_out)
+      load_z(it + 1 < nmine ? tile + (int)gridDim.x : tile);
+    }
+    // ---- last tile's epilogue
+    if (ok && nmine > 0 && mbar_wait(gdone, 1, g, 7)) {
+      tc_fence_after();
+      epilogue(blockIdx.x + (nmine - 1) * gridDim.x, (nmine - 1) & 1);
     }
   } else if (warp == 4) {
     if (lane == 0) {
       int issued = 0;
-      for (int q = 0; q < NLOADS; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
-        ++issued;
+      for (int it = 0; it < nmine; ++it) {
+        bool pushed = true;
+        for (int q = 0; q < NLOADS; ++q) {
+          const int nc = q / C::NKA, ka = q % C::NKA;
+          if (!wring_push<kStrict>(ring, it * NLOADS + q, &w_hi, &w_lo, ka * C::KATOM, nc * 128,
+                                   g)) {
+            pushed = false;
+            break;
+          }
+          ++issued;
+        }
+        if (!pushed) break;
       }
       if (g.aborted()) wring_drain(ring, issued, abort_flag);
     }
@@ -382,28 +440,34 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
       const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
       bool ok = true;
-      for (int q = 0; q < NLOADS && ok; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (ka == 0) {
-          if (nc == 1) umma_commit(a_free);  // GEMM 1 done reading A once it retires
-          if (!mbar_wait(a_full, nc & 1, g, 4)) {
+      for (int it = 0; it < nmine && ok; ++it) {
+        const int b = it & 1;
+        // TMEM buffer b was read by the epilogue of tile it-2
+        if (it >= 2 && !mbar_wait(&tfree[b], ((it - 2) >> 1) & 1, g, 8)) {
+          ok = false;
+          break;
+        }
+        for (int nc = 0; nc < 2 && ok; ++nc) {
+          if (!mbar_wait(a_full, nc, g, 4)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          for (int ka = 0; ka < C::NKA; ++ka) {
+            const int q = it * NLOADS + nc * C::NKA + ka;
+            const uint32_t w = wring_wait(ring, q, g);
+            if (!w) {
+              ok = false;
+              break;
+            }
+            mma_k_atom<kStrict>(tmem + b * 256 + nc * 128, a_hi + ka * C::ATOM_BYTES,
+                                a_lo + ka * C::ATOM_BYTES, w, w + C::ATOM_BYTES, idesc, ka == 0);
+            wring_release(ring, q);
+          }
+          if (ok) umma_commit(gdone);
         }
-        const uint32_t w = wring_wait(ring, q, g);
-        if (!w) {
-          ok = false;
-          break;
-        }
-        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
-                            w, w + C::ATOM_BYTES, idesc, ka == 0);
-        wring_release(ring, q);
       }
-      if (ok) {
-        umma_commit(done);
-      } else {
+      if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
       }
@@ -414,7 +478,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -497,13 +561,14 @@ int trimul_finish_run(float* z_loc, int n, int rows, const void* x_blocked, cons
   CUtensorMap moh, mol;
   if (!make_weight_maps(wo_hi, wo_lo, 256, strict, &moh, &mol)) return kErrArg;
   const int njb = (n + 127) / 128;
+  const int out_tiles = rows * njb;
   TriMulOutArgs oa{z_loc, n, eps, eps, ln_in_w, ln_in_b, ln_out_w, ln_out_b, x_blocked, njb,
-                   add ? 1 : 0, status};
+                   add ? 1 : 0, status, out_tiles};
   const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
   auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const unsigned out_tiles = (unsigned)(rows * njb);
-  FPB_LAUNCH("trimul_out", stream, k<<<out_tiles, 192, smem, stream>>>(moh, mol, oa));
+  const unsigned grid = (unsigned)min(out_tiles, sm_count());
+  FPB_LAUNCH("trimul_out", stream, k<<<grid, 192, smem, stream>>>(moh, mol, oa));
   return launch_status();
 }
 

@@ -181,6 +181,29 @@ __device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// TMA tensor store of a shared-memory box (elements past the tensor's
+// extent are not written). The source must stay untouched until the bulk
+// group has been read (tma_store_wait_read).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x,
+                                             int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// every committed store has finished reading its shared-memory source
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// every committed store has completed
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMEM
 // Allocation is warp-collective; the allocated base column is written to smem.
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -369,7 +392,9 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
   lo = x - hi;
 }
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Logistic sigmoid with the approximate divide (2 ulp): 1 / (1 + e^-x);
+// saturates to 0 / 1 for large |x|.
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // 2^x on the SFU (PTX ex2.approx.ftz.f32).
 __device__ __forceinline__ float ex2_approx(float x) {

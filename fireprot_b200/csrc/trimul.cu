@@ -50,7 +50,11 @@ constexpr int proj_smem_bytes() {
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(192, 1)
     trimul_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
-                       const __grid_constant__ CUtensorMap w_lo, TriMulProjArgs p) {
+                       const __grid_constant__ CUtensorMap w_lo,
+                       const __grid_constant__ CUtensorMap st_a_hi,
+                       const __grid_constant__ CUtensorMap st_a_lo,
+                       const __grid_constant__ CUtensorMap st_b_hi,
+                       const __grid_constant__ CUtensorMap st_b_lo, TriMulProjArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = 2;
   extern __shared__ uint8_t smem_raw[];
@@ -68,8 +72,10 @@ __global__ void __launch_bounds__(192, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long npairs = (long long)p.yrows * p.ycols;
-  const long long p0 = (long long)blockIdx.x * 128;
+  // tile = (y row r, 128-column block jb): a tile never straddles two y rows,
+  // so each output plane receives one [128 channels][128 columns] box
+  const int njb = (p.ycols + 127) / 128;
+  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -100,56 +106,60 @@ __global__ void __launch_bounds__(192, 1)
     const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
     auto src = [&](int row) -> const float4* {
-      const long long pr = p0 + row;
-      if (pr >= npairs) return nullptr;
-      const long long r = pr / p.ycols, s = pr - r * p.ycols;
-      return z4 + (kTrans ? (s * p.zcols + r) : (r * p.zcols + s)) * 32;
+      const int s = s0 + row;
+      if (s >= p.ycols) return nullptr;
+      return z4 + (kTrans ? ((long long)s * p.zcols + r) : ((long long)r * p.zcols + s)) * 32;
     };
     ln_rows_to_a<kStrict, 32, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
     fence_proxy_async_smem();
     mbar_arrive(a_full);
 
-    // ---- epilogue: thread t owns tile row t (TMEM lane t)
+    // ---- epilogue: thread t owns tile row t (TMEM lane t). Each part (a,
+    // then b) is staged in the A buffer as [channel][128 columns] planes and
+    // written by one TMA store per plane (columns past ycols are clipped).
     const int t = warp * 32 + lane;
-    const long long pr = p0 + t;
-    const bool valid = pr < npairs;
-    long long r = 0, s = 0;
+    const int s = s0 + t;
     float m = 1.f;
-    if (valid) {
-      r = pr / p.ycols;
-      s = pr - r * p.ycols;
-      if (p.mask)
-        m = __ldg(p.mask + (kTrans ? ((p.r0 + s) * p.zcols + r) : ((p.r0 + r) * p.zcols + s)));
-    }
-    const size_t pos = (size_t)r * p.ld + (size_t)s;
+    if (p.mask && s < p.ycols)
+      m = __ldg(p.mask + (kTrans ? ((size_t)(p.r0 + s) * p.zcols + r)
+                                 : ((size_t)(p.r0 + r) * p.zcols + s)));
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
 #pragma unroll 1
       for (int part = 0; part < 2; ++part) {
-        void* dst_hi = part ? p.b_hi : p.a_hi;
-        void* dst_lo = part ? p.b_lo : p.a_lo;
+        if (part == 1) {
+          // the stores of part a must have read the staging buffer
+          if (t == 0) tma_store_wait_read();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
           float pv[32], gv[32];
           tmem_row32(tmem, warp, part * 256 + cc * 32, pv);
           tmem_row32(tmem, warp, part * 256 + 128 + cc * 32, gv);
-          if (valid) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float v = sigmoidf_(gv[e]) * pv[e] * m;
-              const size_t idx = (size_t)(cc * 32 + e) * p.cs + pos;
-              if constexpr (kStrict) {
-                float h, l;
-                split_tf32(v, h, l);
-                static_cast<float*>(dst_hi)[idx] = h;
-                static_cast<float*>(dst_lo)[idx] = l;
-              } else {
-                static_cast<__nv_bfloat16*>(dst_hi)[idx] = __float2bfloat16_rn(v);
-              }
+          for (int e = 0; e < 32; ++e) {
+            const float v = sigmoidf_(gv[e]) * pv[e] * m;
+            const int c = cc * 32 + e;
+            if constexpr (kStrict) {
+              float h, l;
+              split_tf32(v, h, l);
+              reinterpret_cast<float*>(A)[c * 128 + t] = h;
+              reinterpret_cast<float*>(A)[128 * 128 + c * 128 + t] = l;
+            } else {
+              reinterpret_cast<__nv_bfloat16*>(A)[c * 128 + t] = __float2bfloat16_rn(v);
             }
           }
         }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t == 0) {
+          tma_store_3d(part ? &st_b_hi : &st_a_hi, A, s0, r, 0);
+          if constexpr (kStrict) tma_store_3d(part ? &st_b_lo : &st_a_lo, A + 65536, s0, r, 0);
+          tma_store_commit();
+        }
       }
+      if (t == 0) tma_store_wait_all();
     }
   } else if (warp == 4) {
     if (lane == 0) {
@@ -538,16 +548,37 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   if (st) return st;
   CUtensorMap mph, mpl;
   if (!make_weight_maps(wp_hi, wp_lo, 512, strict, &mph, &mpl)) return kErrArg;
-  const long long npairs = (long long)yrows * ycols;
-  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  // output planes [128 channels][plane rows][ld]: one store map per plane
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t esz = strict ? 4 : 2;
+  const size_t cs = (size_t)plane_rows * ld;
+  CUtensorMap sah, sal, sbh, sbl;
+  bool ok = make_map_3d(&sah, a_hi, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_3d(&sbh, b_hi, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (strict)
+    ok = ok &&
+         make_map_3d(&sal, a_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         make_map_3d(&sbl, b_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  else {
+    sal = sah;
+    sbl = sbh;
+  }
+  if (!ok) return kErrArg;
+  const unsigned tiles = (unsigned)(yrows * ((ycols + 127) / 128));
   TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0, eps, ln_w, ln_b, a_hi, a_lo, b_hi,
-                    b_lo, ld, (size_t)plane_rows * ld, status};
+                    b_lo, ld, cs, status};
   const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
                   : (transposed ? trimul_proj_kernel<false, true>
                                 : trimul_proj_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  FPB_LAUNCH("trimul_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
+  FPB_LAUNCH("trimul_proj", stream,
+             k<<<tiles, 192, smem, stream>>>(mph, mpl, sah, sal, sbh, sbl, pa));
   return launch_status();
 }
 

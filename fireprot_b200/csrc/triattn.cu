@@ -76,10 +76,18 @@ constexpr int attn_proj_smem_bytes() {
   return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 2 * 4 * 128 * 4, 512);
 }
 
+// Maps of the outputs written by TMA stores from the freed A buffer: q / k
+// [row*4 + h][j][32] (boxes of 128 j x 32, swizzled like the core's loads),
+// v^T [(row*4 + h)*32 + d][key] (boxes of 32 d x 128 keys).
+struct AttnProjStoreMaps {
+  CUtensorMap q_hi, q_lo, k_hi, k_lo, v_hi, v_lo;
+};
+
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(192, 1)
     attn_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
-                     const __grid_constant__ CUtensorMap w_lo, AttnProjArgs p) {
+                     const __grid_constant__ CUtensorMap w_lo,
+                     const __grid_constant__ AttnProjStoreMaps sm, AttnProjArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = 2;
   extern __shared__ uint8_t smem_raw[];
@@ -100,8 +108,9 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  const long long npairs = (long long)p.yrows * n;
-  const long long p0 = (long long)blockIdx.x * 128;
+  // tile = (y row r, 128-column block): a tile never straddles two rows
+  const int njb = (n + 127) / 128;
+  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -135,10 +144,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int h = 0; h < 4; ++h) wbh[h] = reinterpret_cast<const float4*>(wb + h * 128)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
     auto src = [&](int row) -> const float4* {
-      const long long pr = p0 + row;
-      if (pr >= npairs) return nullptr;
-      const long long r = pr / n, s = pr - r * n;
-      return z4 + (kTrans ? (s * n + r) : (r * n + s)) * 32;
+      const int s = s0 + row;
+      if (s >= n) return nullptr;
+      return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
     };
     // the 4-head pair bias of each row, on the CUDA cores
     auto head_bias = [&](int row, float4 y) {
@@ -156,39 +164,38 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("bar.sync 1, 128;" ::: "memory");
 
     const int t = warp * 32 + lane;
-    const long long pr = p0 + t;
-    const bool valid = pr < npairs;
-    long long r = 0, s = 0;
-    if (valid) {
-      r = pr / n;
-      s = pr - r * n;
+    const int s = s0 + t;
+    if (s < n) {
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        p.bias[bias_index((int)(p.r0 + r), h, (int)s, p.ldb)] = bias_tile[h * 128 + t];
+        p.bias[bias_index(p.r0 + r, h, s, p.ldb)] = bias_tile[h * 128 + t];
       if (p.mbias) {
         const float m =
             __ldg(p.mask + (kTrans ? ((size_t)s * n + r) : ((size_t)(p.r0 + r) * n + s)));
         p.mbias[(size_t)r * p.ldb + s] = kMaskInf * (m - 1.0f);
       }
     }
+    // q, k, v^T of the tile, one part at a time, staged in the freed A buffer
+    // (per head: 16 KB fp32 / 8 KB bf16; strict lo planes 64 KB further)
+    // and written by TMA stores; rows / keys past n are clipped.
+    constexpr int HS = kStrict ? 16384 : 8192;
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
 #pragma unroll 1
       for (int part = 0; part < 3; ++part) {
+        if (part > 0) {
+          if (t == 0) tma_store_wait_read();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
 #pragma unroll 1
         for (int h = 0; h < 4; ++h) {
           float v[32];
           tmem_row32(tmem, warp, part * 128 + h * 32, v);
-          if (!valid) continue;
-          const size_t ih = (size_t)r * kHeads + h;
+          uint8_t* sh = A + h * HS;
           if (part < 2) {
+            // [128 rows j][32] in the swizzled layout of the store map
             const float sc = part == 0 ? p.q_scale : 1.0f;
-            const size_t row = ih * n + s;  // [i][h][j] row of 32
-            void* dh = part == 0 ? p.q_hi : p.k_hi;
-            void* dl = part == 0 ? p.q_lo : p.k_lo;
             if constexpr (kStrict) {
-              float4* oh = reinterpret_cast<float4*>(static_cast<float*>(dh) + row * 32);
-              float4* ol = reinterpret_cast<float4*>(static_cast<float*>(dl) + row * 32);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 float h0, l0, h1, l1, h2, l2, h3, l3;
@@ -196,11 +203,11 @@ __global__ void __launch_bounds__(192, 1)
                 split_tf32(v[4 * e + 1] * sc, h1, l1);
                 split_tf32(v[4 * e + 2] * sc, h2, l2);
                 split_tf32(v[4 * e + 3] * sc, h3, l3);
-                oh[e] = make_float4(h0, h1, h2, h3);
-                ol[e] = make_float4(l0, l1, l2, l3);
+                const uint32_t off = sw128_offset(t, e * 16);
+                *reinterpret_cast<float4*>(sh + off) = make_float4(h0, h1, h2, h3);
+                *reinterpret_cast<float4*>(sh + 65536 + off) = make_float4(l0, l1, l2, l3);
               }
             } else {
-              uint4* oh = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dh) + row * 32);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 uint32_t w4[4];
@@ -210,26 +217,47 @@ __global__ void __launch_bounds__(192, 1)
                                                             v[8 * e + 2 * u + 1] * sc);
                   w4[u] = *reinterpret_cast<uint32_t*>(&b2);
                 }
-                oh[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                *reinterpret_cast<uint4*>(sh + sw64_offset(t, e * 16)) =
+                    make_uint4(w4[0], w4[1], w4[2], w4[3]);
               }
             }
           } else {
-            // v^T: [i][h][d][k]
+            // v^T: [32 d][128 keys]
 #pragma unroll
             for (int d = 0; d < 32; ++d) {
-              const size_t idx = (ih * 32 + d) * p.ldv + s;
               if constexpr (kStrict) {
                 float hh, ll;
                 split_tf32(v[d], hh, ll);
-                static_cast<float*>(p.v_hi)[idx] = hh;
-                static_cast<float*>(p.v_lo)[idx] = ll;
+                reinterpret_cast<float*>(sh)[d * 128 + t] = hh;
+                reinterpret_cast<float*>(sh + 65536)[d * 128 + t] = ll;
               } else {
-                static_cast<__nv_bfloat16*>(p.v_hi)[idx] = __float2bfloat16_rn(v[d]);
+                reinterpret_cast<__nv_bfloat16*>(sh)[d * 128 + t] = __float2bfloat16_rn(v[d]);
               }
             }
           }
         }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t == 0) {
+#pragma unroll 1
+          for (int h = 0; h < 4; ++h) {
+            const int ih = r * kHeads + h;
+            uint8_t* sh = A + h * HS;
+            if (part == 0) {
+              tma_store_3d(&sm.q_hi, sh, 0, s0, ih);
+              if constexpr (kStrict) tma_store_3d(&sm.q_lo, sh + 65536, 0, s0, ih);
+            } else if (part == 1) {
+              tma_store_3d(&sm.k_hi, sh, 0, s0, ih);
+              if constexpr (kStrict) tma_store_3d(&sm.k_lo, sh + 65536, 0, s0, ih);
+            } else {
+              tma_store_3d(&sm.v_hi, sh, s0, ih * 32, 0);
+              if constexpr (kStrict) tma_store_3d(&sm.v_lo, sh + 65536, s0, ih * 32, 0);
+            }
+          }
+          tma_store_commit();
+        }
       }
+      if (t == 0) tma_store_wait_all();
     }
   } else if (warp == 4) {
     if (lane == 0) {
@@ -1065,8 +1093,29 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
     return st;
   CUtensorMap mph, mpl;
   if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl)) return kErrArg;
-  const long long npairs = (long long)rows * n;
-  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  const int esz = strict ? 4 : 2;
+  const CUtensorMapDataType dt =
+      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const uint64_t rowb = 32ull * esz, nh = (uint64_t)rows * kHeads;
+  const uint64_t vrow = (uint64_t)pl.ldv * esz;
+  AttnProjStoreMaps sm{};
+  bool ok = make_map_3d(&sm.q_hi, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+            make_map_3d(&sm.k_hi, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+            make_map_3d(&sm.v_hi, pl.v_hi, dt, n, nh * 32, 1, vrow, vrow * nh * 32, 128, 32, 1,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (strict)
+    ok = ok && make_map_3d(&sm.q_lo, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+         make_map_3d(&sm.k_lo, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+         make_map_3d(&sm.v_lo, pl.v_lo, dt, n, nh * 32, 1, vrow, vrow * nh * 32, 128, 32, 1,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  else {
+    sm.q_lo = sm.q_hi;
+    sm.k_lo = sm.k_hi;
+    sm.v_lo = sm.v_hi;
+  }
+  if (!ok) return kErrArg;
+  const unsigned tiles = (unsigned)(rows * ((n + 127) / 128));
   AttnProjArgs pa{z_loc, mask, n, rows, r0, eps, ln_w, ln_b, w_bias,
                   1.0f / sqrtf((float)kHeadDim), pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi,
                   pl.v_lo, pl.ldv, bias, pl.ldb, pl.mbias, status};
@@ -1074,7 +1123,7 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
   auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
                   : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, pa));
+  FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, sm, pa));
   return launch_status();
 }
 

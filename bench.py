@@ -306,28 +306,51 @@ def run_ours(args, world, rank, local):
     if not torch.isfinite(z).all():
         raise RuntimeError("non-finite pair tensor after the timed steps")
 
-    # ---- end to end: pinned host z in, result out, through the public API
+    # ---- end to end: pinned host z in, result out, through the public API.
+    # The e2e steps are independent blocks, pipelined as a serving loop
+    # would: the input copy of step k+1 (host->device stream) and the result
+    # copy of step k-1 (device->host stream) overlap the compute of step k,
+    # on two device buffers. Every step still moves its own bytes.
     e2e_steps = max(1, args.e2e_steps)
-    out_host = torch.empty_like(z_host).pin_memory()
-    zz = torch.empty_like(z)
-    mm = torch.empty_like(mask)
+    out_host = [torch.empty_like(z_host).pin_memory() for _ in range(2)]
+    zbuf = [torch.empty_like(z) for _ in range(2)]
+    mbuf = [torch.empty_like(mask) for _ in range(2)]
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    drained = [torch.cuda.Event() for _ in range(2)]
     barrier(world)
     torch.cuda.synchronize(dev)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
-    for _ in range(e2e_steps):
-        zz.copy_(z_host, non_blocking=True)
-        mm.copy_(mask_host, non_blocking=True)
-        step_fn(zz, mm)
-        out_host.copy_(zz, non_blocking=True)
+    h2d_s.wait_event(f0)
+    for k in range(e2e_steps):
+        b = k % 2
+        with torch.cuda.stream(h2d_s):
+            if k >= 2:
+                h2d_s.wait_event(drained[b])
+            zbuf[b].copy_(z_host, non_blocking=True)
+            mbuf[b].copy_(mask_host, non_blocking=True)
+            loaded[b].record(h2d_s)
+        stream.wait_event(loaded[b])
+        step_fn(zbuf[b], mbuf[b])
+        computed[b].record(stream)
+        with torch.cuda.stream(d2h_s):
+            d2h_s.wait_event(computed[b])
+            out_host[b].copy_(zbuf[b], non_blocking=True)
+            drained[b].record(d2h_s)
+    stream.wait_stream(d2h_s)
     f1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world, dev)
     e2e_value = blocks_per_step * e2e_steps / (e2e_ms / 1e3)
-    # whole-job bytes: every rank copies its z rows (or replica) and the mask
+    if not torch.isfinite(out_host[(e2e_steps - 1) % 2]).all():
+        raise RuntimeError("non-finite end-to-end result")
+    # whole-job bytes per step: every rank copies its z rows (or replica) and
+    # the mask in, and its z rows out
     h2d = world * (z_host.numel() * 4 + mask_host.numel() * 4)
-    d2h = world * out_host.numel() * 4
+    d2h = world * z_host.numel() * 4
 
     # ---- fast-mode side measurement (strict is the headline)
     side = None
@@ -399,7 +422,8 @@ def run_ours(args, world, rank, local):
         "tc_frac_block": blocks_per_step * block_flops(n) / (ms_per_step / 1e3) / 1e12
         / (peak_tc * world),
         "e2e": {"value": e2e_value, "unit": "blocks/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "schedule": "independent blocks; copies of neighbouring steps overlap compute"},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak_tc,
                      "unit": "TFLOP/s", "frac": achieved / peak_tc, "traffic": traffic,
@@ -420,7 +444,7 @@ def main():
     ap.add_argument("--precision", choices=["strict", "fast"], default="strict")
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--valid", type=int, default=1480)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--mode", choices=["sharded", "replicas"], default="sharded",
                     help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")

@@ -396,7 +396,8 @@ def run_ours(args, world, rank, local):
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
         try:
-            traffic = json.loads(tfile.read_text()).get(f"{dom}:{args.precision}:{n}")
+            entry = json.loads(tfile.read_text()).get(f"{dom}:{args.precision}:{n}")
+            traffic = None if entry is None else float(entry["bytes_per_launch"])
         except Exception:
             traffic = None
     launches = sum(r["launches"] for r in kernels.values())

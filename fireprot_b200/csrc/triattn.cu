@@ -338,11 +338,15 @@ struct AttnCfg {
   static constexpr int KSTEP_KEYS = kStrict ? 8 : 16;  // keys per P V K step
   static constexpr int PV_STEPS = BKV / KSTEP_KEYS;
   // TMEM: two S/P buffers (S(t) is read, then P(t) overwrites it: tf32
-  // hi | lo = 2 BKV columns, bf16 pairs = BKV / 2) and O (32 columns)
+  // hi | lo = 2 BKV columns, bf16 pairs = BKV / 2), O (32 columns) and the
+  // query tile's A operand for the S MMAs (Q_hi, tf32: 32 columns; Q, bf16
+  // pairs: 16 columns), so those MMAs read only K from shared memory
   static constexpr int BUF_COLS = kStrict ? 2 * BKV : BKV;
   static constexpr uint32_t kO = 2 * BUF_COLS;
+  static constexpr uint32_t kQ = kO + 32;
+  static constexpr int Q_COLS = kStrict ? 32 : 16;
   static constexpr int TMEM_COLS = 256;
-  static_assert(2 * BUF_COLS + 32 <= TMEM_COLS, "TMEM budget");
+  static_assert(kQ + Q_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(BKV % KSTEP_KEYS == 0 && BKV % 16 == 0, "key tile shape");
   static_assert(KV_STAGE % 1024 == 0 && (NSPLIT * K_BYTES) % 1024 == 0, "stage alignment");
   static constexpr int THREADS = 192;  // 4 softmax warps, TMA warp, MMA warp
@@ -394,7 +398,8 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* s_full = kv_empty + C::KV_STAGES;   // [2 buffers]
   uint64_t* p_full = s_full + 2;                // [2 buffers]
   uint64_t* pv_done = p_full + 2;
-  uint64_t* drain = pv_done + 1;
+  uint64_t* q_tmem = pv_done + 1;               // Q (hi) copied into TMEM
+  uint64_t* drain = q_tmem + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -415,6 +420,7 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&p_full[b], 128);
     }
     mbar_init(pv_done, 1);
+    mbar_init(q_tmem, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -468,24 +474,24 @@ __global__ void __launch_bounds__(192, 2)
     if (lane == 0) {
       const uint32_t id_s = kStrict ? idesc_tf32(128, C::BKV) : idesc_bf16(128, C::BKV);
       const uint32_t id_o = kStrict ? idesc_tf32(128, 32) : idesc_bf16(128, 32);
-      const uint32_t q_hi = smem_u32(Q), q_lo = q_hi + C::Q_BYTES;
+      const uint32_t q_lo = smem_u32(Q) + C::Q_BYTES;
       auto issue_s = [&](int t) {
         const uint32_t kst = smem_u32(KV + (t % C::KV_STAGES) * C::KV_STAGE);
         const uint32_t sbuf = tmem + (t & 1) * C::BUF_COLS;
 #pragma unroll
         for (int kk = 0; kk < C::QK_STEPS; ++kk) {
           const uint32_t off = kk * 32;
-          const uint64_t dqh = qk_desc<kStrict>(q_hi + off);
+          const uint32_t qa = tmem + C::kQ + kk * 8;  // 8 tf32 / 16 bf16 of d per step
           const uint64_t dkh = qk_desc<kStrict>(kst + off);
           const uint32_t acc = kk == 0 ? 0u : 1u;
           if constexpr (kStrict) {
             const uint64_t dql = qk_desc<kStrict>(q_lo + off);
             const uint64_t dkl = qk_desc<kStrict>(kst + C::K_BYTES + off);
-            umma_tf32(sbuf, dqh, dkh, id_s, acc);
-            umma_tf32(sbuf, dqh, dkl, id_s, 1u);
-            umma_tf32(sbuf, dql, dkh, id_s, 1u);
+            umma_tf32_ts(sbuf, qa, dkh, id_s, acc);  // Q_hi K_hi
+            umma_tf32_ts(sbuf, qa, dkl, id_s, 1u);   // Q_hi K_lo
+            umma_tf32(sbuf, dql, dkh, id_s, 1u);     // Q_lo K_hi
           } else {
-            umma_bf16(sbuf, dqh, dkh, id_s, acc);
+            umma_bf16_ts(sbuf, qa, dkh, id_s, acc);
           }
         }
         umma_commit(&s_full[t & 1]);
@@ -514,7 +520,8 @@ __global__ void __launch_bounds__(192, 2)
         }
         umma_commit(pv_done);
       };
-      bool ok = mbar_wait(q_full, 0, g, 22);
+      // the softmax warps have copied Q (hi) into TMEM (after q_full)
+      bool ok = mbar_wait(q_full, 0, g, 22) && mbar_wait(q_tmem, 0, g, 29);
       if (ok) tc_fence_after();
       // S of the first two tiles fill both buffers
       for (int t = 0; t < 2 && t < nt && ok; ++t) {
@@ -612,7 +619,36 @@ __global__ void __launch_bounds__(192, 2)
     float m_ref = -INFINITY, l_run = 0.f;
     float cb[C::BKV];
     load_bias(0, cb);
-    bool ok = true;
+    // this thread's query row of Q (hi) -> TMEM, the A operand of the S MMAs
+    bool ok = mbar_wait(q_full, 0, g, 20);
+    if (ok) {
+      if constexpr (kStrict) {
+        uint32_t qr[32];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint4 v = *reinterpret_cast<const uint4*>(Q + sw128_offset(t_row, e * 16));
+          qr[4 * e] = v.x;
+          qr[4 * e + 1] = v.y;
+          qr[4 * e + 2] = v.z;
+          qr[4 * e + 3] = v.w;
+        }
+        tmem_st32(tb + C::kQ, qr);
+      } else {
+        uint32_t qr[16];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint4 v = *reinterpret_cast<const uint4*>(Q + sw64_offset(t_row, e * 16));
+          qr[4 * e] = v.x;
+          qr[4 * e + 1] = v.y;
+          qr[4 * e + 2] = v.z;
+          qr[4 * e + 3] = v.w;
+        }
+        tmem_st16(tb + C::kQ, qr);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(q_tmem);
+    }
     for (int t = 0; t < nt && ok; ++t) {
       const uint32_t buf = tb + (t & 1) * C::BUF_COLS;
       float sv[C::BKV];

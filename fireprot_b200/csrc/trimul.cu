@@ -39,6 +39,7 @@ struct TriMulProjArgs {
   int ld;
   size_t cs;
   int* status;
+  int b_plain;  // strict: write b unsplit (FP32) into the b_hi planes
 };
 
 template <bool kStrict>
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(192, 1)
           if (t == 0) tma_store_wait_read();
           asm volatile("bar.sync 1, 128;" ::: "memory");
         }
+        const bool plain = kStrict && part == 1 && p.b_plain;
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
           float pv[32], gv[32];
@@ -144,7 +146,7 @@ __global__ void __launch_bounds__(192, 1)
             if constexpr (kStrict) {
               float h, l;
               split_tf32(v, h, l);
-              reinterpret_cast<float*>(A)[c * 128 + t] = h;
+              reinterpret_cast<float*>(A)[c * 128 + t] = plain ? v : h;
               reinterpret_cast<float*>(A)[128 * 128 + c * 128 + t] = l;
             } else {
               reinterpret_cast<__nv_bfloat16*>(A)[c * 128 + t] = __float2bfloat16_rn(v);
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(192, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (t == 0) {
           tma_store_3d(part ? &st_b_hi : &st_a_hi, A, s0, r, 0);
-          if constexpr (kStrict) tma_store_3d(part ? &st_b_lo : &st_a_lo, A + 65536, s0, r, 0);
+          if (kStrict && !plain) tma_store_3d(part ? &st_b_lo : &st_a_lo, A + 65536, s0, r, 0);
           tma_store_commit();
         }
       }
@@ -558,12 +560,15 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
                         CU_TENSOR_MAP_SWIZZLE_NONE) &&
             make_map_3d(&sbh, b_hi, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
+  // strict with no b_lo: b is written unsplit into the b_hi planes
+  const int b_plain = (strict && b_lo == nullptr) ? 1 : 0;
   if (strict)
     ok = ok &&
          make_map_3d(&sal, a_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
                      CU_TENSOR_MAP_SWIZZLE_NONE) &&
-         make_map_3d(&sbl, b_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+         (b_plain ? (sbl = sbh, true)
+                  : make_map_3d(&sbl, b_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1,
+                                128, CU_TENSOR_MAP_SWIZZLE_NONE));
   else {
     sal = sah;
     sbl = sbh;
@@ -571,7 +576,7 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   if (!ok) return kErrArg;
   const unsigned tiles = (unsigned)(yrows * ((ycols + 127) / 128));
   TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0, eps, ln_w, ln_b, a_hi, a_lo, b_hi,
-                    b_lo, ld, cs, status};
+                    b_lo, ld, cs, status, b_plain};
   const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
                   : (transposed ? trimul_proj_kernel<false, true>
@@ -725,7 +730,7 @@ extern "C" int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int 
     return kErrArg;
   if (precision != 0 && precision != 1) return kErrArg;
   const bool strict = precision == 0;
-  if (strict && (!a_lo || !b_lo)) return kErrArg;
+  if (strict && !a_lo) return kErrArg;  // b_lo null: b unsplit (FP32)
   if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
   const int yrows = transposed ? n : rows;
   const int ycols = transposed ? rows : n;
@@ -786,4 +791,42 @@ extern "C" int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void
   return trimul_finish_run(z_loc, n, rows, x_blocked, ln_in_w, ln_in_b, w_g, ln_out_w, ln_out_b,
                            w_z, eps, add != 0, strict, wh, wl, static_cast<int*>(workspace),
                            stream);
+}
+
+// Exact tf32 split of FP32 values: hi = x with the low 13 mantissa bits
+// cleared, lo = x - hi. hi may alias src (in-place split).
+namespace fpb {
+__global__ void split_tf32_kernel(const float* src, float* hi, float* lo, size_t count) {
+  const size_t n4 = count / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float4 x = reinterpret_cast<const float4*>(src)[i];
+    float4 h, l;
+    split_tf32(x.x, h.x, l.x);
+    split_tf32(x.y, h.y, l.y);
+    split_tf32(x.z, h.z, l.z);
+    split_tf32(x.w, h.w, l.w);
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+  for (size_t i = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float h, l;
+    split_tf32(src[i], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+}  // namespace fpb
+
+extern "C" int fpb_split_tf32(const float* src, void* hi, void* lo, size_t count,
+                              cudaStream_t stream) {
+  if (!src || !hi || !lo) return kErrArg;
+  if (!aligned16(src) || !aligned16(hi) || !aligned16(lo)) return kErrAlign;
+  if (count == 0) return kOk;
+  const unsigned blocks = (unsigned)min((size_t)sm_count() * 8, (count / 4 + 255) / 256 + 1);
+  FPB_LAUNCH("split_tf32", stream,
+             split_tf32_kernel<<<blocks, 256, 0, stream>>>(src, static_cast<float*>(hi),
+                                                           static_cast<float*>(lo), count));
+  return launch_status();
 }

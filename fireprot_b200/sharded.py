@@ -167,7 +167,9 @@ class CudaPhases:
     # ---------------------------------------------------------------- TriMul
     def trimul_proj(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
         """Gated, masked a/b planes of the rank's rows: outgoing ``[128][chunk][ld(n)]``
-        (the b planes are the all-gather chunk), incoming ``[128][n][ld(rows)]``."""
+        (the b planes are the all-gather chunk; in strict mode one unsplit FP32
+        plane, split after the gather: half the bytes), incoming
+        ``[128][n][ld(rows)]``."""
         n, rows = shard.n, shard.rows
         dev = z_loc.device
         if outgoing:
@@ -178,7 +180,11 @@ class CudaPhases:
                 return None, None, 0
             ld = int(self.lib.fpb_trimul_plane_ld(rows, self.p))
             plane_rows = n
-        a, b = self._planes(plane_rows, ld, dev), self._planes(plane_rows, ld, dev)
+        a = self._planes(plane_rows, ld, dev)
+        if outgoing and self.strict:
+            b = [torch.empty(128, plane_rows, ld, dtype=torch.float32, device=dev)]
+        else:
+            b = self._planes(plane_rows, ld, dev)
         if rows == 0:
             return a, b, ld
         ws = self._ws_take("trimul_proj", self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
@@ -186,7 +192,8 @@ class CudaPhases:
         wt = [w[k].contiguous() for k in keys]
         _lib.check(self.lib.fpb_trimul_shard_proj(
             z_loc.data_ptr(), self._ptr(mask), n, rows, shard.r0, int(not outgoing),
-            *[t.data_ptr() for t in wt], self.eps, *self._pair(a), *self._pair(b), ld, plane_rows,
+            *[t.data_ptr() for t in wt], self.eps, *self._pair(a), b[0].data_ptr(),
+            (b[1].data_ptr() if len(b) > 1 else 0), ld, plane_rows,
             self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)), "fpb_trimul_shard_proj")
         return a, b, ld
 
@@ -203,8 +210,16 @@ class CudaPhases:
             ops._stream_ptr(device)), "fpb_trimul_shard_contract")
 
     def trimul_contract_out(self, a, b_full, shard: RowShard, ld):
-        """Local rows of ``x = a b^T`` with ``b_full`` the gathered chunks."""
+        """Local rows of ``x = a b^T`` with ``b_full`` the gathered chunks
+        (strict: unsplit FP32, split in place into hi + a new lo here)."""
         dev = b_full[0].device
+        if self.strict and len(b_full) == 1:
+            hi = b_full[0]
+            lo = torch.empty_like(hi)
+            _lib.check(self.lib.fpb_split_tf32(hi.data_ptr(), hi.data_ptr(), lo.data_ptr(),
+                                               hi.numel(), ops._stream_ptr(dev)),
+                       "fpb_split_tf32")
+            b_full = [hi, lo]
         x = self.new_x(shard.chunk, shard, dev)
         if shard.rows:
             self._contract(a, shard.rows, shard.chunk, b_full, shard.n, shard.chunk, shard.world,

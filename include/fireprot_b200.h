@@ -195,6 +195,12 @@ int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int n, int rows
                           const float* w_b_g, float eps, void* a_hi, void* a_lo, void* b_hi,
                           void* b_lo, int ld, int plane_rows, int precision, void* workspace,
                           size_t workspace_bytes, cudaStream_t stream);
+/* Strict mode may pass b_lo = NULL to fpb_trimul_shard_proj: b is then
+ * written unsplit (FP32) into the b_hi planes, half the bytes of the
+ * outgoing all-gather; after it, fpb_split_tf32 splits the gathered planes
+ * exactly (hi = x with the low 13 mantissa bits cleared, lo = x - hi; hi may
+ * alias src). No reference counterpart (the reference has no sharded path). */
+int fpb_split_tf32(const float* src, void* hi, void* lo, size_t count, cudaStream_t stream);
 int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
                               const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
                               int b_chunks, size_t b_chunk_stride, int k, int ld,

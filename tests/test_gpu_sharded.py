@@ -110,3 +110,23 @@ def test_sharded_block(cuda_device, world, n, mask_kind, precision):
 
     for full in _run(world, n, z, mask, cuda_device, body):
         assert O.rel_max_err(full, ref) <= _tol(precision)
+
+
+@pytest.mark.parametrize("count", [1, 7, 4096, 100003])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_split_tf32_exact(cuda_device, count, in_place):
+    """``fpb_split_tf32``: hi has the low 13 mantissa bits clear and
+    hi + lo reproduces every FP32 input exactly (also in place)."""
+    from fireprot_b200 import _lib
+    g = torch.Generator().manual_seed(count)
+    x = (torch.randn(count, generator=g) * torch.exp(torch.randn(count, generator=g) * 4)).to(
+        cuda_device)
+    src = x.clone()
+    hi = src if in_place else torch.empty_like(x)
+    lo = torch.empty_like(x)
+    lib = _lib.load()
+    assert lib.fpb_split_tf32(src.data_ptr(), hi.data_ptr(), lo.data_ptr(), count,
+                              torch.cuda.current_stream(cuda_device).cuda_stream) == 0
+    torch.cuda.synchronize(cuda_device)
+    assert torch.equal(hi.view(torch.int32) & 0x1FFF, torch.zeros_like(hi, dtype=torch.int32))
+    assert torch.equal((hi.double() + lo.double()), x.double())

@@ -27,11 +27,17 @@ struct TransCfg {
   static constexpr int G1_STAGE = G1N * 128 * R::NSPLIT;   // bytes of one GEMM-1 W stage
   static constexpr int G2_STAGE = 128 * 128 * R::NSPLIT;   // bytes of one GEMM-2 W stage
   static constexpr int STAGE = G1_STAGE > G2_STAGE ? G1_STAGE : G2_STAGE;
-  static constexpr int STAGES = kStrict ? 2 : 3;
-  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows
-  static constexpr int TMEM_COLS = kStrict ? 256 : 512;    // 2*G1N + 128 rounded up
-  static constexpr int SMEM = tmem_safe_smem(R::A_BYTES + H_BYTES + STAGES * STAGE + 1024 + 256,
-                                             TMEM_COLS);
+  static constexpr int STAGES = 5;
+  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows (x2 buffers)
+  // TMEM: A = LN(z) (tf32 hi | lo: 256 columns; bf16 pairs: 64), two
+  // GEMM-1 buffers, the GEMM-2 accumulator (128)
+  static constexpr uint32_t kA_LO = 128;
+  static constexpr uint32_t kG1 = kStrict ? 256 : 64;
+  static constexpr uint32_t kAcc = kG1 + 2 * G1N;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(kAcc + 128 <= TMEM_COLS, "TMEM budget");
+  static constexpr int SMEM =
+      tmem_safe_smem(2 * H_BYTES + STAGES * STAGE + 1024 + 256 + 1024, TMEM_COLS);
 };
 
 struct TransArgs {
@@ -44,6 +50,14 @@ struct TransArgs {
   int* status;
 };
 
+// One CTA per 128-row tile. The LayerNorm'd tile lives in TMEM (thread t =
+// row t normalises its own row and stores it as the A operand of GEMM 1), so
+// shared memory holds only two SwiGLU tiles H and a 5-stage weight ring:
+//   GEMM 1 (chunk c): [a_c | b_c] = A [Wa_c; Wb_c]^T     (A from TMEM)
+//   row threads:      H = silu(a_c) * b_c -> shared memory (A operand)
+//   GEMM 2:           acc += H Wout_c^T
+// with GEMM 1 double-buffered in TMEM so that it runs one chunk ahead, and H
+// double-buffered so that the SwiGLU of chunk c+1 never waits for GEMM 2(c).
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 1)
     transition_kernel(const __grid_constant__ CUtensorMap w1_hi,
@@ -55,18 +69,18 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* A = smem;
-  uint8_t* H = A + R::A_BYTES;
-  uint8_t* W = H + C::H_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(W + C::STAGES * C::STAGE);
+  uint8_t* H = smem;                 // [2][H_BYTES]
+  uint8_t* W = H + 2 * C::H_BYTES;
+  float* lnp = reinterpret_cast<float*>(W + C::STAGES * C::STAGE);  // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lnp + 256);
   uint64_t* wfull = bars;
   uint64_t* wempty = wfull + C::STAGES;
   uint64_t* a_full = wempty + C::STAGES;
   uint64_t* g1_full = a_full + 1;   // [2]
   uint64_t* g1_free = g1_full + 2;  // [2]
-  uint64_t* h_full = g1_free + 2;
-  uint64_t* h_free = h_full + 1;
-  uint64_t* done = h_free + 1;
+  uint64_t* h_full = g1_free + 2;  // [2]
+  uint64_t* h_free = h_full + 2;   // [2]
+  uint64_t* done = h_free + 2;
   uint64_t* drain = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
@@ -74,7 +88,6 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long rows = p.n_rows;
   const long long p0 = (long long)blockIdx.x * 128;
-  constexpr uint32_t kAcc = 2 * C::G1N;  // accumulator columns [kAcc, kAcc + 128)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -86,12 +99,18 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&g1_full[b], 1);
       mbar_init(&g1_free[b], 128);
     }
-    mbar_init(h_full, 128);
-    mbar_init(h_free, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&h_full[b], 128);
+      mbar_init(&h_free[b], 1);
+    }
     mbar_init(done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if (threadIdx.x < 128) {
+    lnp[threadIdx.x] = p.ln_w[threadIdx.x];
+    lnp[128 + threadIdx.x] = p.ln_b[threadIdx.x];
   }
   if (warp == 5) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -105,21 +124,66 @@ __global__ void __launch_bounds__(192, 1)
 
   // Weight-load sequence shared by the TMA and MMA threads:
   // G1(0), then for c = 0..NCH-1: [G1(c+1)], G2(c). G1 chunk = R::NKA loads.
-  // seq index -> (is_g2, chunk, atom)
   if (warp < 4) {
+    const int t = warp * 32 + lane;
+    const uint32_t lrow = tmem + ((uint32_t)(warp * 32) << 16);  // this thread's TMEM lane
+    const long long pr = p0 + t;
     {
-      const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
-      const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
-      const float4* z4 = reinterpret_cast<const float4*>(p.z);
-      auto src = [&](int row) -> const float4* {
-        const long long pr = p0 + row;
-        return pr < rows ? z4 + pr * 32 : nullptr;
-      };
-      ln_rows_to_a<kStrict, 32, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
-      fence_proxy_async_smem();
+      // ---- A = LN(z row t) into TMEM: one row per thread, all loads first
+      float x[128];
+      const float4* zr = reinterpret_cast<const float4*>(p.z) + (pr < rows ? pr : 0) * 32;
+#pragma unroll
+      for (int v4 = 0; v4 < 32; ++v4) {
+        const float4 v = pr < rows ? __ldg(zr + v4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[4 * v4] = v.x;
+        x[4 * v4 + 1] = v.y;
+        x[4 * v4 + 2] = v.z;
+        x[4 * v4 + 3] = v.w;
+      }
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) s4[c & 3] += x[c];
+      const float mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 128.0f);
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float d = x[c] - mean;
+        q4[c & 3] += d * d;
+      }
+      const float rs =
+          rsqrtf(((q4[0] + q4[1]) + (q4[2] + q4[3])) * (1.0f / 128.0f) + p.eps);
+#pragma unroll
+      for (int c = 0; c < 128; ++c) x[c] = (x[c] - mean) * rs * lnp[c] + lnp[128 + c];
+      if constexpr (kStrict) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t hv[32], lv[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float h, l;
+            split_tf32(x[q * 32 + e], h, l);
+            hv[e] = __float_as_uint(h);
+            lv[e] = __float_as_uint(l);
+          }
+          tmem_st32(lrow + q * 32, hv);
+          tmem_st32(lrow + C::kA_LO + q * 32, lv);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(x[q * 64 + 2 * e], x[q * 64 + 2 * e + 1]);
+            pk[e] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          tmem_st32(lrow + q * 32, pk);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(a_full);
     }
-    const int t = warp * 32 + lane;
     bool ok = true;
 #pragma unroll 1
     for (int c = 0; c < C::NCH && ok; ++c) {
@@ -133,21 +197,22 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int q = 0; q < C::HC / 32; ++q) {
         float av[32], bv[32];
-        tmem_row32(tmem + b * C::G1N, warp, q * 32, av);
-        tmem_row32(tmem + b * C::G1N, warp, C::HC + q * 32, bv);
+        tmem_row32(tmem + C::kG1 + b * C::G1N, warp, q * 32, av);
+        tmem_row32(tmem + C::kG1 + b * C::G1N, warp, C::HC + q * 32, bv);
 #pragma unroll
         for (int e = 0; e < 32; ++e) hv[q * 32 + e] = av[e] * sigmoidf_(av[e]) * bv[e];
       }
       tc_fence_before();
       mbar_arrive(&g1_free[b]);
-      if (c >= 1 && !mbar_wait(h_free, (c - 1) & 1, g, 32)) {
+      // H buffer b was read by GEMM 2 of chunk c-2
+      if (c >= 2 && !mbar_wait(&h_free[b], ((c - 2) >> 1) & 1, g, 32)) {
         ok = false;
         break;
       }
       // H row t: one K atom (HC elements)
 #pragma unroll
       for (int e = 0; e < C::HC; e += 4) {
-        uint8_t* dst = H + sw128_offset(t, e * R::ESZ);
+        uint8_t* dst = H + b * C::H_BYTES + sw128_offset(t, e * R::ESZ);
         if constexpr (kStrict) {
           float h0, l0, h1, l1, h2, l2, h3, l3;
           split_tf32(hv[e], h0, l0);
@@ -167,11 +232,10 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(h_full);
+      mbar_arrive(&h_full[b]);
     }
     if (ok && mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
-      const long long pr = p0 + t;
       const long long rsafe = pr < rows ? pr : 0;
       float4* zrow = reinterpret_cast<float4*>(p.z) + rsafe * 32;
       float4* drow = p.delta ? reinterpret_cast<float4*>(p.delta) + rsafe * 32 : zrow;
@@ -183,7 +247,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int v4 = 0; v4 < 8; ++v4)
           zc[v4] = (residual && pr < rows) ? zrow[cc * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
         float yv[32];
-        tmem_row32(tmem + kAcc, warp, cc * 32, yv);
+        tmem_row32(tmem + C::kAcc, warp, cc * 32, yv);
         if (pr < rows) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
@@ -234,8 +298,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       const uint32_t id1 = kStrict ? idesc_tf32(128, C::G1N) : idesc_bf16(128, C::G1N);
       const uint32_t id2 = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
-      const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + R::A_SPLIT_BYTES);
-      const uint32_t h_hi = smem_u32(H), h_lo = smem_u32(H + R::ATOM_BYTES);
+      const uint32_t h0 = smem_u32(H);
       int seq = 0;
       auto take = [&]() -> uint32_t {
         const int s = seq % C::STAGES;
@@ -251,11 +314,25 @@ __global__ void __launch_bounds__(192, 1)
         const int b = c & 1;
         if (c >= 2 && !mbar_wait(&g1_free[b], ((c - 2) >> 1) & 1, g, 35)) return false;
         tc_fence_after();
+        const uint32_t d = tmem + C::kG1 + b * C::G1N;
         for (int a = 0; a < R::NKA; ++a) {
           const uint32_t w = take();
           if (!w) return false;
-          mma_k_atom<kStrict>(tmem + b * C::G1N, a_hi + a * R::ATOM_BYTES,
-                              a_lo + a * R::ATOM_BYTES, w, w + C::G1N * 128, id1, a == 0);
+          // A atom a from TMEM: 4 K steps of 8 tf32 / 16 bf16 (8 columns each)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acol = a * (R::KATOM * R::ESZ / 4) + kk * 8;
+            const uint64_t dwh = umma_desc_sw128(w + kk * 32);
+            const uint32_t acc = (a == 0 && kk == 0) ? 0u : 1u;
+            if constexpr (kStrict) {
+              const uint64_t dwl = umma_desc_sw128(w + C::G1N * 128 + kk * 32);
+              umma_tf32_ts(d, tmem + acol, dwh, id1, acc);             // A_hi W_hi
+              umma_tf32_ts(d, tmem + acol, dwl, id1, 1u);              // A_hi W_lo
+              umma_tf32_ts(d, tmem + C::kA_LO + acol, dwh, id1, 1u);   // A_lo W_hi
+            } else {
+              umma_bf16_ts(d, tmem + acol, dwh, id1, acc);
+            }
+          }
           release();
         }
         umma_commit(&g1_full[b]);
@@ -266,7 +343,8 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = gemm1(0);
       for (int c = 0; c < C::NCH && ok; ++c) {
         if (c + 1 < C::NCH && !(ok = gemm1(c + 1))) break;
-        if (!mbar_wait(h_full, c & 1, g, 37)) {
+        const int hb = c & 1;
+        if (!mbar_wait(&h_full[hb], (c >> 1) & 1, g, 37)) {
           ok = false;
           break;
         }
@@ -276,9 +354,11 @@ __global__ void __launch_bounds__(192, 1)
           ok = false;
           break;
         }
-        mma_k_atom<kStrict>(tmem + kAcc, h_hi, h_lo, w, w + R::ATOM_BYTES, id2, c == 0);
+        const uint32_t h_hi = h0 + hb * C::H_BYTES;
+        mma_k_atom<kStrict>(tmem + C::kAcc, h_hi, h_hi + R::ATOM_BYTES, w, w + R::ATOM_BYTES, id2,
+                            c == 0);
         release();
-        umma_commit(h_free);
+        umma_commit(&h_free[hb]);
       }
       if (ok) {
         umma_commit(done);

@@ -849,10 +849,14 @@ constexpr int attn_out_smem_bytes() {
   return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
 }
 
+// out_map: z (or delta) viewed as [a][b][128 channels] with z row a*n + b;
+// the tile's 128 rows are b = s0.. (box {32, 128, 1}) or, transposed,
+// a = s0.. (box {32, 1, 128}); rows past n are clipped by the store.
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(192, 1)
     attn_out_kernel(const __grid_constant__ CUtensorMap w_hi,
-                    const __grid_constant__ CUtensorMap w_lo, AttnOutArgs p) {
+                    const __grid_constant__ CUtensorMap w_lo,
+                    const __grid_constant__ CUtensorMap out_map, AttnOutArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = 2;
   extern __shared__ uint8_t smem_raw[];
@@ -873,8 +877,9 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  const long long npairs = (long long)p.rows * n;
-  const long long p0 = (long long)blockIdx.x * 128;
+  // tile = (y row r, 128-column block): a tile never straddles two rows
+  const int njb = (n + 127) / 128;
+  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -910,23 +915,18 @@ __global__ void __launch_bounds__(192, 1)
       const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
       const float4* z4 = reinterpret_cast<const float4*>(p.z);
       auto src = [&](int row) -> const float4* {
-        const long long pr = p0 + row;
-        if (pr >= npairs) return nullptr;
-        const long long r = pr / n, s = pr - r * n;
-        return z4 + (kTrans ? (s * n + r) : pr) * 32;
+        const int s = s0 + row;
+        if (s >= n) return nullptr;
+        return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
       };
       ln_rows_to_a<kStrict, 32, false>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }
     const int t = warp * 32 + lane;
-    const long long pr = p0 + t;
-    const bool valid = pr < npairs;
-    long long zrow_idx = 0;
-    if (valid) {
-      const long long r = pr / n, s = pr - r * n;
-      zrow_idx = kTrans ? (s * n + r) : pr;
-    }
+    const bool valid = s0 + t < n;
+    const long long pr = (long long)r * n + (valid ? s0 + t : 0);  // y pair (o row)
+    const long long zrow_idx = kTrans ? (long long)(valid ? s0 + t : 0) * n + r : pr;
     // attention output chunk cc (32 channels) of this thread's row
     auto load_o = [&](int cc, float (&ov)[32]) {
       if (!valid) {
@@ -1001,6 +1001,9 @@ __global__ void __launch_bounds__(192, 1)
       zc[v4] = (valid && residual) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
     if (mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
+      // the finished rows are staged in the freed A buffer (and, in fast
+      // mode, the weight ring right behind it) as 4 boxes [128 rows][32
+      // channels] in the 128-byte swizzled layout, then written by TMA stores
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         float4 zn[8];
@@ -1010,20 +1013,32 @@ __global__ void __launch_bounds__(192, 1)
                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
         float yv[32];
         tmem_row32(tmem, warp, 128 + cc * 32, yv);
-        if (valid) {
+        uint8_t* box = A + cc * 16384;
 #pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4) {
-            float4 o = zc[v4];
-            const int c = cc * 32 + 4 * v4;
-            o.x += yv[4 * v4] + bvec[128 + c];
-            o.y += yv[4 * v4 + 1] + bvec[129 + c];
-            o.z += yv[4 * v4 + 2] + bvec[130 + c];
-            o.w += yv[4 * v4 + 3] + bvec[131 + c];
-            drow[cc * 8 + v4] = o;
-          }
+        for (int v4 = 0; v4 < 8; ++v4) {
+          float4 o = zc[v4];
+          const int c = cc * 32 + 4 * v4;
+          o.x += yv[4 * v4] + bvec[128 + c];
+          o.y += yv[4 * v4 + 1] + bvec[129 + c];
+          o.z += yv[4 * v4 + 2] + bvec[130 + c];
+          o.w += yv[4 * v4 + 3] + bvec[131 + c];
+          *reinterpret_cast<float4*>(box + sw128_offset(t, v4 * 16)) = o;
         }
 #pragma unroll
         for (int v4 = 0; v4 < 8; ++v4) zc[v4] = zn[v4];
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) {
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          if constexpr (kTrans)
+            tma_store_3d(&out_map, A + cc * 16384, cc * 32, r, s0);
+          else
+            tma_store_3d(&out_map, A + cc * 16384, cc * 32, s0, r);
+        }
+        tma_store_commit();
+        tma_store_wait_all();
       }
     }
   } else if (warp == 4) {
@@ -1183,13 +1198,21 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
       return st;
   }
   AttnOutArgs oa{z_loc, delta_out, n, rows, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
-  const long long npairs = (long long)rows * n;
-  const unsigned tiles = (unsigned)((npairs + 127) / 128);
+  // store map over the written tensor (z, or delta_out) as [a][b][128]
+  CUtensorMap om;
+  {
+    const uint64_t arows = trans ? (uint64_t)n : (uint64_t)rows;
+    float* dst = delta_out ? delta_out : z_loc;
+    if (!make_map_3d(&om, dst, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, n, arows, 512,
+                     512ull * n, 32, trans ? 1 : 128, trans ? 128 : 1))
+      return kErrArg;
+  }
+  const unsigned tiles = (unsigned)(rows * ((n + 127) / 128));
   const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
   auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
                   : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, oa));
+  FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, om, oa));
   return launch_status();
 }
 

@@ -1,11 +1,13 @@
 #!/usr/bin/env python
-"""Pairformer pair-block throughput on B200 (blocks/s at N=1536).
+"""Pairformer block throughput on B200 (blocks/s at N=1536).
 
-One step = the pair stack of one Pairformer block (TriMul out, TriMul in,
-TriAttn start, TriAttn end, pair transition) on a synthetic pair tensor of
-BASELINE config 3's shape: N=1536, c_z=128, padding mask with valid length
-1480, seeded N(0,1) inputs and random-init N(0, 1/fan_in) weights. Consecutive
-steps chain (step k+1 runs on step k's output), i.e. a K-block stack.
+One step = one whole Pairformer block: the pair stack (TriMul out, TriMul in,
+TriAttn start, TriAttn end, pair transition) and then the single stack
+(attention with pair bias, c_s=384, 16 heads of 24, and the single
+transition) on synthetic inputs of BASELINE config 3's shape: N=1536,
+c_z=128, padding mask with valid length 1480, seeded N(0,1) z and s and
+random-init N(0, 1/fan_in) weights. Consecutive steps chain (step k+1 runs
+on step k's output), i.e. a K-block stack.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--precision strict|fast]
   python bench.py --impl reference ...   # the native math on host CPU cores
@@ -40,11 +42,24 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "Pairformer blocks/s at N=1536 (strict/fast) at 1/2/4/8 B200; % TC roofline"
 C = 128
+CS = 384
+
+
+def pair_stack_flops(n: int) -> float:
+    """Algorithmic FLOPs of the pair stack: 1536 N^3 + 1,116,160 N^2."""
+    return 1536.0 * n ** 3 + 1_116_160.0 * n ** 2
+
+
+def single_stack_flops(n: int) -> float:
+    """Algorithmic FLOPs of the single stack: 5,632 N^2 + 5,013,504 N
+    (pair bias 4096 N^2, attention 1536 N^2, q/k/v/g/o projections
+    1,474,560 N, transition 3,538,944 N)."""
+    return 5632.0 * n ** 2 + 5_013_504.0 * n
 
 
 def block_flops(n: int) -> float:
-    """Algorithmic FLOPs of one pair block: 1536 N^3 + 1,116,160 N^2."""
-    return 1536.0 * n ** 3 + 1_116_160.0 * n ** 2
+    """Algorithmic FLOPs of one Pairformer block (pair + single stacks)."""
+    return pair_stack_flops(n) + single_stack_flops(n)
 
 
 def kernel_flops(name: str, n: int) -> float:
@@ -59,6 +74,8 @@ def kernel_flops(name: str, n: int) -> float:
         "triattn_core": 4.0 * n ** 3 * C,
         "triattn_out": 2.0 * n2 * C * 2 * C,
         "transition": 2.0 * n2 * (C * 8 * C + 4 * C * C),
+        "single_pair_bias": 2.0 * n2 * C * 16,
+        "single_attn": 4.0 * n2 * CS,
     }.get(name, 0.0)
 
 
@@ -198,10 +215,12 @@ def run_reference(args, world, rank):
 
 
 def _config(args):
-    return {"workload": (f"pair stack of one Pairformer block (TriMul out/in, TriAttn start/end, "
-                         f"pair transition), N={args.n}, c_z=128, H=4, d=32, {args.precision} "
-                         f"precision, padding mask valid {args.valid}"),
-            "n": args.n, "c_z": C, "precision": args.precision, "valid_length": args.valid,
+    return {"workload": (f"one Pairformer block: pair stack (TriMul out/in, TriAttn start/end "
+                         f"H=4 d=32, pair transition) and single stack (attention with pair "
+                         f"bias H=16 d=24, single transition), N={args.n}, c_z=128, c_s=384, "
+                         f"{args.precision} precision, padding mask valid {args.valid}"),
+            "n": args.n, "c_z": C, "c_s": CS, "precision": args.precision,
+            "valid_length": args.valid,
             "l2": "inputs larger than L2 (z alone is %.2f GB)" % (args.n ** 2 * C * 4 / 1e9),
             "parallelism": ("single GPU" if args.gpus == 1 else
                             f"rows of z sharded over {args.gpus} GPUs (NCCL all-gather, "
@@ -214,7 +233,7 @@ def _config(args):
 # ---------------------------------------------------------------------------
 def run_ours(args, world, rank, local):
     from fireprot_b200 import ops
-    from fireprot_b200.modules import PairformerPairBlock
+    from fireprot_b200.modules import PairformerBlock
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -224,49 +243,64 @@ def run_ours(args, world, rank, local):
     seed = 0 if sharded or world == 1 else rank
     gen = torch.Generator().manual_seed(1000 + seed)
     z_full = torch.randn(n, n, C, generator=gen)
+    s_host = torch.randn(n, CS, generator=gen).pin_memory()
     valid = torch.arange(n) < args.valid
     mask_host = (valid[:, None] & valid[None, :]).float().pin_memory()
-    block = PairformerPairBlock().init_random_(seed=1 + seed).to(dev)
+    block = PairformerBlock().init_random_(seed=1 + seed).to(dev)
     mask = mask_host.to(dev)
 
     if sharded:
         from fireprot_b200 import sharded as S
         shard = S.shard_plan(n, world, rank)
         comm = S.DistComm()
-        weights = S.block_weight_dicts(block)
+        weights = S.block_weight_dicts(block.pair)
+        w_single = block.single.weight_dict()
         z_host = S.local_rows(z_full, shard).pin_memory()
         rows_frac = shard.rows / n
 
         def make_step(precision):
             phases = S.CudaPhases(precision)
 
-            def step(zz, mm):
+            def step(zz, ss, mm):
+                # ss: [W * chunk, 384] all-gather buffer holding s in its first n rows
                 S.sharded_pair_block(zz, mm, weights, shard, comm, phases)
+                S.sharded_single_block(ss, zz, mm, w_single, shard, comm, phases)
             return step, phases.check
+
+        def s_device(src):
+            return S.single_buffer(src.to(dev), shard)
     else:
         z_host = z_full.pin_memory()
-        cw = block.c_weights()
+        cw, cw_single = block.pair.c_weights(), block.single.c_weights()
         rows_frac = 1.0
 
         def make_step(precision):
             ws = ops.pair_block_workspace(n, precision, True, dev)
+            ws_single = ops.single_block_workspace(n, n, dev)
 
-            def step(zz, mm):
+            def step(zz, ss, mm):
                 ops.pair_block(zz, mm, cw, precision=precision, workspace=ws)
+                ops.single_block(ss, zz, mm, cw_single, precision=precision,
+                                 workspace=ws_single)
 
             def check():
-                st = ops.workspace_status(ws)
-                if st != 0:
-                    raise RuntimeError(f"device status {st}")
+                for w in (ws, ws_single):
+                    st = ops.workspace_status(w)
+                    if st != 0:
+                        raise RuntimeError(f"device status {st}")
             return step, check
+
+        def s_device(src):
+            return src.to(dev)
     del z_full
     blocks_per_step = 1 if sharded else world
     z = z_host.to(dev)
+    s_dev = s_device(s_host)
     stream = torch.cuda.current_stream(dev)
     step_fn, check = make_step(args.precision)
 
     def step(zz):
-        step_fn(zz, mask)
+        step_fn(zz, s_dev, mask)
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -303,8 +337,8 @@ def run_ours(args, world, rank, local):
     ms_per_step = ms_max / args.steps
     value = blocks_per_step * args.steps / (ms_max / 1e3)
     check()
-    if not torch.isfinite(z).all():
-        raise RuntimeError("non-finite pair tensor after the timed steps")
+    if not torch.isfinite(z).all() or not torch.isfinite(s_dev).all():
+        raise RuntimeError("non-finite pair or single tensor after the timed steps")
 
     # ---- end to end: pinned host z in, result out, through the public API.
     # The e2e steps are independent blocks, pipelined as a serving loop
@@ -313,7 +347,9 @@ def run_ours(args, world, rank, local):
     # on two device buffers. Every step still moves its own bytes.
     e2e_steps = max(1, args.e2e_steps)
     out_host = [torch.empty_like(z_host).pin_memory() for _ in range(2)]
+    s_out_host = [torch.empty_like(s_host).pin_memory() for _ in range(2)]
     zbuf = [torch.empty_like(z) for _ in range(2)]
+    sbuf = [torch.empty_like(s_dev) for _ in range(2)]
     mbuf = [torch.empty_like(mask) for _ in range(2)]
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     loaded = [torch.cuda.Event() for _ in range(2)]
@@ -330,14 +366,16 @@ def run_ours(args, world, rank, local):
             if k >= 2:
                 h2d_s.wait_event(drained[b])
             zbuf[b].copy_(z_host, non_blocking=True)
+            sbuf[b][:n].copy_(s_host, non_blocking=True)
             mbuf[b].copy_(mask_host, non_blocking=True)
             loaded[b].record(h2d_s)
         stream.wait_event(loaded[b])
-        step_fn(zbuf[b], mbuf[b])
+        step_fn(zbuf[b], sbuf[b], mbuf[b])
         computed[b].record(stream)
         with torch.cuda.stream(d2h_s):
             d2h_s.wait_event(computed[b])
             out_host[b].copy_(zbuf[b], non_blocking=True)
+            s_out_host[b].copy_(sbuf[b][:n], non_blocking=True)
             drained[b].record(d2h_s)
     stream.wait_stream(d2h_s)
     f1.record(stream)
@@ -345,27 +383,29 @@ def run_ours(args, world, rank, local):
     barrier(world)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world, dev)
     e2e_value = blocks_per_step * e2e_steps / (e2e_ms / 1e3)
-    if not torch.isfinite(out_host[(e2e_steps - 1) % 2]).all():
+    last = (e2e_steps - 1) % 2
+    if not torch.isfinite(out_host[last]).all() or not torch.isfinite(s_out_host[last]).all():
         raise RuntimeError("non-finite end-to-end result")
-    # whole-job bytes per step: every rank copies its z rows (or replica) and
-    # the mask in, and its z rows out
-    h2d = world * (z_host.numel() * 4 + mask_host.numel() * 4)
-    d2h = world * z_host.numel() * 4
+    # whole-job bytes per step: every rank copies its z rows (or replica), s
+    # and the mask in, and its z rows and s out
+    h2d = world * (z_host.numel() + s_host.numel() + mask_host.numel()) * 4
+    d2h = world * (z_host.numel() + s_host.numel()) * 4
 
     # ---- fast-mode side measurement (strict is the headline)
     side = None
     if args.precision == "strict" and not args.no_side:
         fast_step, fast_check = make_step("fast")
         zf = z_host.to(dev)
+        sf = s_device(s_host)
         for _ in range(2):
-            fast_step(zf, mask)
+            fast_step(zf, sf, mask)
         torch.cuda.synchronize(dev)
         fast_check()
         barrier(world)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         for _ in range(args.steps):
-            fast_step(zf, mask)
+            fast_step(zf, sf, mask)
         g1.record(stream)
         torch.cuda.synchronize(dev)
         fms = max_over_ranks(g0.elapsed_time(g1), world, dev) / args.steps
@@ -374,7 +414,7 @@ def run_ours(args, world, rank, local):
                 "ms_per_step": fms,
                 "tc_frac_block": blocks_per_step * block_flops(n) / (fms / 1e3) / 1e12
                 / (pf * world)}
-        del zf
+        del zf, sf
 
     if rank != 0:
         return None

@@ -197,3 +197,110 @@ class PairformerPairBlock(nn.Module):
     def forward(self, z, mask=None, *, precision="strict", workspace=None):
         return ops.pair_block(z, mask, self.c_weights(), precision=precision,
                               workspace=workspace)
+
+
+# --------------------------------------------------------------------------
+# single stack
+# --------------------------------------------------------------------------
+class _GatedAttention(nn.Module):
+    """The projections of upstream ``Attention`` as AttentionPairBias builds
+    it (q with bias; k, v, gate and output bias-free)."""
+
+    def __init__(self, c: int = 384, heads: int = 16):
+        super().__init__()
+        self.num_heads, self.c_hidden = heads, c // heads
+        self.linear_q = _linear(c, c, bias=True)
+        self.linear_k = _linear(c, c)
+        self.linear_v = _linear(c, c)
+        self.linear_g = _linear(c, c)
+        self.linear_o = _linear(c, c)
+
+
+class AttentionPairBias(nn.Module):
+    """Protenix ``AttentionPairBias`` without conditioning (``has_s=False``):
+    LayerNorm of s, gated multi-head attention over all tokens with one pair
+    bias per head from ``linear_nobias_z(layernorm_z(z))``."""
+
+    def __init__(self, c_a: int = 384, c_z: int = 128, n_heads: int = 16):
+        super().__init__()
+        self.n_heads = n_heads
+        self.layernorm_a = nn.LayerNorm(c_a)
+        self.attention = _GatedAttention(c_a, n_heads)
+        self.layernorm_z = nn.LayerNorm(c_z)
+        self.linear_nobias_z = _linear(c_z, n_heads)
+
+    def weight_dict(self):
+        at = self.attention
+        return dict(ln_a_w=self.layernorm_a.weight, ln_a_b=self.layernorm_a.bias,
+                    w_q=at.linear_q.weight, b_q=at.linear_q.bias, w_k=at.linear_k.weight,
+                    w_v=at.linear_v.weight, w_g=at.linear_g.weight, w_o=at.linear_o.weight,
+                    ln_z_w=self.layernorm_z.weight, ln_z_b=self.layernorm_z.bias,
+                    w_z=self.linear_nobias_z.weight)
+
+
+class SingleBlockWeights(ctypes.Structure):
+    """Mirror of ``fpb_single_block_weights`` (include/fireprot_b200.h)."""
+    _fields_ = [(k, ctypes.c_void_p) for k in ops.SINGLE_WEIGHTS]
+
+
+class PairformerSingleBlock(nn.Module):
+    """Single stack of one Pairformer block (AF3 Algorithm 17, lines 6-7):
+    ``s += attention_pair_bias(s, z)``, ``s += single_transition(s)``;
+    c_s = 384, 16 heads of 24."""
+
+    def __init__(self, c_s: int = 384, c_z: int = 128, n_heads: int = 16):
+        super().__init__()
+        if c_s != 384 or c_z != 128 or n_heads != 16:
+            raise RuntimeError("the B200 kernels implement c_s=384, c_z=128, 16 heads")
+        self.attention_pair_bias = AttentionPairBias(c_s, c_z, n_heads)
+        self.single_transition = Transition(c_s, 4)
+        self._packed = None
+
+    def init_random_(self, seed: int = 1) -> "PairformerSingleBlock":
+        _init_normal_(self, torch.Generator().manual_seed(seed))
+        self._packed = None
+        return self
+
+    def weight_dict(self):
+        w = dict(self.attention_pair_bias.weight_dict())
+        t = self.single_transition.weight_dict()
+        w.update(tr_ln_w=t["ln_w"], tr_ln_b=t["ln_b"], tr_w_a=t["w_a"], tr_w_b=t["w_b"],
+                 tr_w_out=t["w_out"])
+        return w
+
+    def c_weights(self):
+        """ctypes weight struct (cached until the parameters change)."""
+        key = tuple((p.data_ptr(), p._version) for p in self.parameters())
+        if self._packed is None or self._packed[0] != key:
+            keep: list = []
+            w = SingleBlockWeights()
+            _fill(w, self.weight_dict(), keep)
+            self._packed = (key, w, keep)
+        return self._packed[1]
+
+    @torch.no_grad()
+    def forward(self, s, z, mask=None, *, precision="strict", workspace=None):
+        return ops.single_block(s, z, mask, self.c_weights(), precision=precision,
+                                eps=self.single_transition.layernorm1.eps, workspace=workspace)
+
+
+class PairformerBlock(nn.Module):
+    """One whole Pairformer block: the pair stack on z, then the single stack
+    on s reading the updated z (Protenix ``PairformerBlock`` order)."""
+
+    def __init__(self, c_z: int = 128, c_s: int = 384, n_heads: int = 16):
+        super().__init__()
+        self.pair = PairformerPairBlock(c_z)
+        self.single = PairformerSingleBlock(c_s, c_z, n_heads)
+
+    def init_random_(self, seed: int = 1) -> "PairformerBlock":
+        self.pair.init_random_(seed)
+        self.single.init_random_(seed + 1000)
+        return self
+
+    @torch.no_grad()
+    def forward(self, s, z, mask=None, *, precision="strict", workspace=None,
+                single_workspace=None):
+        self.pair(z, mask, precision=precision, workspace=workspace)
+        self.single(s, z, mask, precision=precision, workspace=single_workspace)
+        return s, z

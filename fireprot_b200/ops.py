@@ -271,6 +271,52 @@ def pair_block(z: torch.Tensor, mask, c_weights, *, precision="strict", eps: flo
     return (z, ws) if return_workspace else z
 
 
+SINGLE_WEIGHTS = ("ln_a_w", "ln_a_b", "w_q", "b_q", "w_k", "w_v", "w_g", "w_o", "ln_z_w",
+                  "ln_z_b", "w_z", "tr_ln_w", "tr_ln_b", "tr_w_a", "tr_w_b", "tr_w_out")
+
+
+def single_block_workspace(n: int, rows: int, device) -> torch.Tensor:
+    nbytes = _lib.load().fpb_single_block_workspace_size(n, rows, 384)
+    if nbytes == 0:
+        raise RuntimeError(f"unsupported single block size n={n} rows={rows}")
+    return workspace(nbytes, device)
+
+
+def single_block(s: torch.Tensor, z_loc: torch.Tensor, mask, c_weights, *, r0: int = 0,
+                 precision="strict", eps: float = 1e-5, workspace=None,
+                 return_workspace: bool = False):
+    """Single stack of one Pairformer block in place on rows ``[r0, r0 +
+    rows)`` of ``s`` ``[n, 384]``: ``s += AttentionPairBias(s, z)``, then
+    ``s += Transition(s)``.
+
+    ``z_loc`` holds the pair rows of those queries (``[rows, n, 128]``; the
+    whole ``z`` when unsharded), ``mask`` is the full ``[n, n]`` pair mask or
+    None, ``c_weights`` a ``modules.SingleBlockWeights`` struct. FP32 in both
+    precision modes.
+    """
+    _require_cuda(s, z_loc, mask)
+    if s.dtype != torch.float32 or s.ndim != 2 or s.shape[1] != 384:
+        raise RuntimeError("single_block takes a float32 [n, 384] single tensor")
+    n = s.shape[0]
+    if z_loc.dtype != torch.float32 or z_loc.ndim != 3 or z_loc.shape[1:] != (n, 128):
+        raise RuntimeError("z_loc must be a float32 [rows, n, 128] tensor")
+    rows = z_loc.shape[0]
+    for t, name in ((s, "s"), (z_loc, "z_loc")):
+        if not t.is_contiguous() or t.data_ptr() % 16:
+            raise RuntimeError(f"single_block needs a contiguous, 16-byte aligned {name}")
+    if mask is not None:
+        if tuple(mask.shape) != (n, n) or mask.dtype != torch.float32 or not mask.is_contiguous():
+            raise RuntimeError("mask must be a contiguous float32 [n, n] tensor")
+    lib = _lib.load()
+    p = precision_code(precision)
+    ws = workspace if workspace is not None else single_block_workspace(n, rows, s.device)
+    _lib.check(lib.fpb_single_block(s.data_ptr(), z_loc.data_ptr(),
+                                    0 if mask is None else mask.data_ptr(), n, rows, int(r0),
+                                    384, ctypes.byref(c_weights), float(eps), p, ws.data_ptr(),
+                                    ws.numel(), _stream_ptr(s.device)), "fpb_single_block")
+    return (s, ws) if return_workspace else s
+
+
 def timing_enable(on: bool = True) -> None:
     _lib.load().fpb_timing_enable(int(bool(on)))
 

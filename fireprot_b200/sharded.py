@@ -157,13 +157,6 @@ class CudaPhases:
     def _pair(self, planes):
         return planes[0].data_ptr(), (planes[1].data_ptr() if self.strict else 0)
 
-    def check(self) -> None:
-        """Raise if any wait of any phase kernel gave up (reads status words)."""
-        for name, ws in self._ws.items():
-            st = ops.workspace_status(ws)
-            if st:
-                raise RuntimeError(f"{name} phase kernel status {st}")
-
     # ---------------------------------------------------------------- TriMul
     def trimul_proj(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
         """Gated, masked a/b planes of the rank's rows: outgoing ``[128][chunk][ld(n)]``
@@ -295,6 +288,35 @@ class CudaPhases:
             self.eps, self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(z_loc.device)),
             "fpb_transition")
 
+    # ---------------------------------------------------------- single stack
+    def single_block(self, s, z_loc, mask, shard: RowShard, w: dict):
+        """``s [n, 384]`` (every row) += the single stack on the rank's rows;
+        ``z_loc`` holds the rank's pair rows."""
+        if shard.rows == 0:
+            return
+        from .modules import SingleBlockWeights, _fill
+        key = tuple((k, t.data_ptr(), t._version) for k, t in w.items())
+        cached = self._ws.get("_single_weights")
+        if cached is None or cached[0] != key:
+            keep: list = []
+            cw = SingleBlockWeights()
+            _fill(cw, w, keep)
+            cached = (key, cw, keep)
+            self._ws["_single_weights"] = cached
+        ws = self._ws_take("single", self.lib.fpb_single_block_workspace_size(
+            shard.n, shard.rows, 384), s.device)
+        ops.single_block(s, z_loc[:shard.rows], mask, cached[1], r0=shard.r0, precision=self.p,
+                         eps=self.eps, workspace=ws)
+
+    def check(self) -> None:
+        """Raise if any wait of any phase kernel gave up (reads status words)."""
+        for name, ws in self._ws.items():
+            if name.startswith("_"):
+                continue
+            st = ops.workspace_status(ws)
+            if st:
+                raise RuntimeError(f"{name} phase kernel status {st}")
+
 
 # ---------------------------------------------------------------------------
 # rank-local orchestration (every rank runs the same collective sequence)
@@ -346,6 +368,26 @@ def sharded_pair_block(z_loc, mask, weights: dict, shard: RowShard, comm, phases
     sharded_triattn(z_loc, mask, weights["tri_att_end"], shard, comm, phases, starting=False)
     phases.transition(z_loc, shard, weights["pair_transition"])
     return z_loc
+
+
+def single_buffer(s: torch.Tensor, shard: RowShard) -> torch.Tensor:
+    """``[W * chunk, 384]`` buffer holding ``s`` in its first ``n`` rows: the
+    all-gather target of ``sharded_single_block``."""
+    buf = s.new_zeros((shard.world * shard.chunk, s.shape[1]))
+    buf[:shard.n] = s
+    return buf
+
+
+def sharded_single_block(s_buf, z_loc, mask, w: dict, shard: RowShard, comm, phases):
+    """Single stack of one Pairformer block on the rank's query rows, then an
+    all-gather of the updated rows so that every rank holds all of ``s``.
+    ``s_buf`` is a ``single_buffer`` (rows past ``n`` are padding); ``w`` is
+    ``PairformerSingleBlock.weight_dict()``. Keys and values read every row
+    of ``s``, which is why ``s`` is replicated rather than sharded."""
+    phases.single_block(s_buf[:shard.n], z_loc, mask, shard, w)
+    local = s_buf[shard.r0:shard.r0 + shard.chunk].clone()
+    comm.all_gather(s_buf, local)
+    return s_buf
 
 
 def block_weight_dicts(block) -> dict:

@@ -261,6 +261,31 @@ int fpb_pair_block(float* z, const float* mask, int n, const fpb_pair_block_weig
                    float eps, int precision, void* workspace, size_t workspace_bytes,
                    cudaStream_t stream);
 
+/* Weights of the single stack of one block (torch Linear layouts, c_s = 384,
+ * 16 heads of 24): AttentionPairBias (layer_norm_a, linear_q with bias,
+ * bias-free linear_k/v/g/o, layer_norm_z + bias-free linear_z to 16 heads)
+ * and the single Transition (n = 4). */
+typedef struct {
+  const float *ln_a_w, *ln_a_b, *w_q, *b_q, *w_k, *w_v, *w_g, *w_o, *ln_z_w, *ln_z_b, *w_z;
+  const float *tr_ln_w, *tr_ln_b, *tr_w_a, *tr_w_b, *tr_w_out;
+} fpb_single_block_weights;
+
+/* Single stack of one Pairformer block on query rows [r0, r0 + rows) of
+ * s [n, 384] (in place): s += AttentionPairBias(s, z), then
+ * s += Transition(s) (AlphaFold 3 Algorithms 24 without conditioning and 11).
+ * z_loc holds pair rows [r0, r0 + rows) ([rows, n, 128]); mask is the full
+ * [n, n] pair mask (nullable). Every row of s is read (keys and values), so a
+ * row-sharded caller passes the whole s and all-gathers the rows afterwards;
+ * an unsharded caller passes rows = n, r0 = 0.
+ * No reference kernel: the reference runs this stack natively
+ * (docs/openfold3-performance.md:68-74, "Single attention with pair bias",
+ * "Single transition"). Runs in FP32 on CUDA cores in both precision modes
+ * (`precision` is validated, the result is the same). */
+size_t fpb_single_block_workspace_size(int n, int rows, int c_s);
+int fpb_single_block(float* s, const float* z_loc, const float* mask, int n, int rows, int r0,
+                     int c_s, const fpb_single_block_weights* weights, float eps, int precision,
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Per-launch device timing on the calling thread (CUDA events around every
  * kernel launch of this library). fpb_timing_collect synchronises and writes
  * {"kernel": {"launches": L, "total_ms": T}, ...} as JSON. */

@@ -3,14 +3,16 @@
 TEST / BASELINE INFRASTRUCTURE ONLY (used by ``bench.py``'s CPU-baseline leg
 and its ``--impl reference`` arm). It times the same torch operations as
 ``pairformer_oracle`` on the host cores, on a bounded sample of one
-Pairformer pair block:
+Pairformer block:
 
 - every O(N^2) stage (LayerNorms, all projections, gates, the transition)
   runs on the full N x N pair tensor;
 - the O(N^3) stages run on a sample and are scaled linearly: the triangle
   contraction on ``chan_sample`` of the 128 channel planes, the triangle
   attention core (scores, mask/bias, softmax, P V) on ``row_sample`` rows i of
-  N (the reference's own outer-chunk loop, ``triangle_attention.py:113-128``).
+  N (the reference's own outer-chunk loop, ``triangle_attention.py:113-128``);
+- the single stack (attention with pair bias over all N tokens, the single
+  transition) runs in full.
 
 Both directions of each operator have the same cost, so each is timed once
 and counted twice. Returns seconds per block.
@@ -32,8 +34,10 @@ def _timed(fn):
 
 
 def sampled_block_seconds(n: int = 1536, valid: int | None = None, *, row_sample: int = 16,
-                          chan_sample: int = 8, threads: int | None = None, seed: int = 0):
-    """Estimated seconds for one pair block at size n, and a breakdown."""
+                          chan_sample: int = 8, threads: int | None = None, seed: int = 0,
+                          single: bool = True):
+    """Estimated seconds for one Pairformer block at size n (the single stack
+    only when ``single``), and a breakdown."""
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     z = O.make_pair(n, seed=seed)
@@ -96,8 +100,15 @@ def sampled_block_seconds(n: int = 1536, valid: int | None = None, *, row_sample
         # --- transition
         _, t_tr = _timed(lambda: z + O.pair_transition(z, p.transition))
         parts["pair_transition"] = t_tr
+
+        # --- single stack (AttentionPairBias + single transition), in full
+        if single:
+            s = O.make_single(n, seed=seed + 2)
+            ps = O.make_single_params(seed=seed + 3)
+            _, parts["single_stack"] = _timed(lambda: O.single_block(s, z, mask, ps))
     total = sum(parts.values())
-    sample = (f"one pair block at N={n}: O(N^2) stages in full; triangle contraction on "
+    what = "one Pairformer block (pair and single stacks)" if single else "one pair block"
+    sample = (f"{what} at N={n}: O(N^2) stages in full; triangle contraction on "
               f"{chan_sample}/128 channel planes and attention core on {r}/{n} rows, "
               f"scaled linearly; torch fp32 on {threads} host threads")
     return total, parts, sample, threads

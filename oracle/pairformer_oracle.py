@@ -329,3 +329,94 @@ def rel_max_err(actual, expected):
     e = expected.detach().to("cpu", torch.float64)
     scale = e.abs().max().item()
     return (a - e).abs().max().item() / (scale if scale > 0 else 1.0)
+
+
+# --------------------------------------------------------------------------
+# single stack of a Pairformer block (next-row scope beyond the pair path)
+# --------------------------------------------------------------------------
+# Parity unpinned: the reference runs this stack natively through upstream
+# Protenix (commit bb3be993, not vendored; ``docs/openfold3-performance.md:68-74``
+# times it as "Single attention with pair bias" and "Single transition"), so
+# there is no reference function or golden vector to pin it to. The
+# restatement follows the published AlphaFold 3 supplement: Algorithm 24
+# (AttentionPairBias, without the conditioning signal) and Algorithm 11
+# (Transition), with the Pairformer's order s += APB(s, z); s += T(s).
+@dataclasses.dataclass
+class SingleBlockParams:
+    """Weights of the single stack: ``AttentionPairBias`` (LayerNorm of s,
+    q with bias, bias-free k/v/gate/output, LayerNorm + bias-free linear of z
+    to one bias per head) and the single ``Transition``."""
+    heads: int
+    head_dim: int
+    ln_a_w: torch.Tensor
+    ln_a_b: torch.Tensor
+    w_q: torch.Tensor   # [H*d, c_s]
+    b_q: torch.Tensor   # [H*d]
+    w_k: torch.Tensor   # [H*d, c_s]
+    w_v: torch.Tensor   # [H*d, c_s]
+    w_g: torch.Tensor   # [H*d, c_s]
+    w_o: torch.Tensor   # [c_s, H*d]
+    ln_z_w: torch.Tensor
+    ln_z_b: torch.Tensor
+    w_z: torch.Tensor   # [H, c_z]
+    transition: TransitionParams
+
+
+def make_single_params(c_s=384, c_z=128, heads=16, head_dim=24, seed=1, dtype=torch.float32,
+                       ln_affine_random=False) -> SingleBlockParams:
+    """Seeded random-init weights ~ N(0, 1/fan_in); defaults are the
+    Pairformer's single stack (c_s 384, 16 heads of 24)."""
+    g = torch.Generator().manual_seed(seed)
+    hd = heads * head_dim
+    if ln_affine_random:
+        ln = [1.0 + 0.1 * torch.randn(c_s, generator=g), 0.1 * torch.randn(c_s, generator=g),
+              1.0 + 0.1 * torch.randn(c_z, generator=g), 0.1 * torch.randn(c_z, generator=g)]
+    else:
+        ln = [torch.ones(c_s), torch.zeros(c_s), torch.ones(c_z), torch.zeros(c_z)]
+    s_s, s_h, s_z = 1.0 / math.sqrt(c_s), 1.0 / math.sqrt(hd), 1.0 / math.sqrt(c_z)
+    return SingleBlockParams(
+        heads=heads, head_dim=head_dim,
+        ln_a_w=ln[0].to(dtype), ln_a_b=ln[1].to(dtype),
+        w_q=_normal(g, (hd, c_s), s_s, dtype),
+        b_q=_normal(g, (hd,), 0.1, dtype),
+        w_k=_normal(g, (hd, c_s), s_s, dtype),
+        w_v=_normal(g, (hd, c_s), s_s, dtype),
+        w_g=_normal(g, (hd, c_s), s_s, dtype),
+        w_o=_normal(g, (c_s, hd), s_h, dtype),
+        ln_z_w=ln[2].to(dtype), ln_z_b=ln[3].to(dtype),
+        w_z=_normal(g, (heads, c_z), s_z, dtype),
+        transition=make_transition_params(c_s, seed=seed + 100, dtype=dtype,
+                                          ln_affine_random=ln_affine_random),
+    )
+
+
+def make_single(n, c=384, seed=0, dtype=torch.float32) -> torch.Tensor:
+    """Seeded s ~ N(0, 1) of shape [n, c]."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(n, c, generator=g, dtype=torch.float32).to(dtype)
+
+
+def attention_pair_bias(s, z, mask, p: SingleBlockParams):
+    """AlphaFold 3 Algorithm 24 without conditioning, returning the update:
+    ``a = LN(s)``; ``q = (a W_q^T + b_q) / sqrt(d)``; ``k, v, g`` bias-free;
+    ``b^h_ij = LN(z_ij) W_z^T + 1e9 (mask_ij - 1)``;
+    ``out = (sigmoid(a W_g^T) * softmax_j(q k^T + b) v) W_o^T``."""
+    n = s.shape[0]
+    h, d = p.heads, p.head_dim
+    a = layer_norm(s, p.ln_a_w, p.ln_a_b)
+    q = ((a @ p.w_q.T + p.b_q) / math.sqrt(d)).view(n, h, d).transpose(0, 1)
+    k = (a @ p.w_k.T).view(n, h, d).transpose(0, 1)
+    v = (a @ p.w_v.T).view(n, h, d).transpose(0, 1)
+    bias = (layer_norm(z, p.ln_z_w, p.ln_z_b) @ p.w_z.T).permute(2, 0, 1)  # [H, i, j]
+    biases = [bias]
+    if mask is not None:
+        biases = [(MASK_INF * (mask - 1.0)).to(s.dtype)[None], bias]
+    o = attention_core(q, k, v, biases).transpose(0, 1).reshape(n, h * d)
+    return (torch.sigmoid(a @ p.w_g.T) * o) @ p.w_o.T
+
+
+def single_block(s, z, mask, p: SingleBlockParams):
+    """Single stack of one Pairformer block: ``s += APB(s, z)``, then
+    ``s += Transition(s)`` (AlphaFold 3 Algorithm 17, lines 6-7)."""
+    s = s + attention_pair_bias(s, z, mask, p)
+    return s + pair_transition(s, p.transition)

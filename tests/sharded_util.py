@@ -126,6 +126,39 @@ class OraclePhases:
         p = O.TransitionParams(**{k: _d(w[k]) for k in ("ln_w", "ln_b", "w_a", "w_b", "w_out")})
         z_loc[:rows] = (zl + O.pair_transition(zl, p)).to(z_loc.dtype)
 
+    def single_block(self, s, z_loc, mask, shard, w):
+        """Query rows of the rank: the full oracle on a pair tensor holding
+        only the rank's rows (query i reads pair row i alone)."""
+        self.calls.append("single_block")
+        n, rows, r0 = shard.n, shard.rows, shard.r0
+        if rows == 0:
+            return
+        z = torch.zeros(n, n, 128, dtype=torch.float64)
+        z[r0:r0 + rows] = _d(z_loc[:rows])
+        out = O.single_block(_d(s), z, _d(mask), oracle_single_params(w))
+        s[r0:r0 + rows] = out[r0:r0 + rows].to(s.dtype)
+
+
+def single_weight_dict(p: "O.SingleBlockParams") -> dict:
+    """``PairformerSingleBlock.weight_dict()`` keys from oracle parameters."""
+    d = {k: getattr(p, k) for k in ("ln_a_w", "ln_a_b", "w_q", "b_q", "w_k", "w_v", "w_g",
+                                    "w_o", "ln_z_w", "ln_z_b", "w_z")}
+    t = p.transition
+    d.update(tr_ln_w=t.ln_w, tr_ln_b=t.ln_b, tr_w_a=t.w_a, tr_w_b=t.w_b, tr_w_out=t.w_out)
+    return d
+
+
+def oracle_single_params(w: dict, heads: int = 16, head_dim: int = 24,
+                         dtype=torch.float64) -> "O.SingleBlockParams":
+    """Inverse of ``single_weight_dict`` (CPU copies in ``dtype``)."""
+    def c(t):
+        return t.detach().to("cpu", dtype)
+    tr = O.TransitionParams(ln_w=c(w["tr_ln_w"]), ln_b=c(w["tr_ln_b"]), w_a=c(w["tr_w_a"]),
+                            w_b=c(w["tr_w_b"]), w_out=c(w["tr_w_out"]))
+    return O.SingleBlockParams(heads=heads, head_dim=head_dim, transition=tr, **{
+        k: c(w[k]) for k in ("ln_a_w", "ln_a_b", "w_q", "b_q", "w_k", "w_v", "w_g", "w_o",
+                             "ln_z_w", "ln_z_b", "w_z")})
+
 
 def oracle_weight_dicts(p: "O.PairBlockParams") -> dict:
     """``sharded_pair_block`` weight dicts from oracle block parameters."""

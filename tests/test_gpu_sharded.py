@@ -130,3 +130,30 @@ def test_split_tf32_exact(cuda_device, count, in_place):
     torch.cuda.synchronize(cuda_device)
     assert torch.equal(hi.view(torch.int32) & 0x1FFF, torch.zeros_like(hi, dtype=torch.int32))
     assert torch.equal((hi.double() + lo.double()), x.double())
+
+
+@pytest.mark.parametrize("world,n,mask_kind", [(2, 100, "random"), (3, 70, "padding"),
+                                               (5, 40, "none")])
+def test_sharded_single_block(cuda_device, world, n, mask_kind):
+    """Single stack on each rank's query rows, then the all-gather of s."""
+    from sharded_util import single_weight_dict
+    s = O.make_single(n, seed=71 + n)
+    z = O.make_pair(n, seed=72 + n)
+    mask = _mask(n, mask_kind)
+    p = O.make_single_params(seed=23, ln_affine_random=True)
+    ref = O.single_block(s, z, mask, p)
+    w = _dev(single_weight_dict(p), cuda_device)
+    md = None if mask is None else mask.to(cuda_device)
+
+    def rank_fn(r, comm):
+        sh = S.shard_plan(n, world, r)
+        z_loc = S.local_rows(z.to(cuda_device), sh)
+        s_buf = S.single_buffer(s.to(cuda_device), sh)
+        ph = S.CudaPhases("strict")
+        S.sharded_single_block(s_buf, z_loc, md, w, sh, comm, ph)
+        torch.cuda.synchronize(cuda_device)
+        ph.check()
+        return s_buf[:n].cpu()
+
+    for full in run_threads(world, rank_fn):
+        assert O.rel_max_err(full, ref) <= O.STRICT_TOL

@@ -2,7 +2,7 @@
 full block orchestration against the single-device oracle
 (``oracle/pairformer_oracle.py:pair_block``), on thread-emulated ranks and on
 real ``gloo`` process groups (world size 2 and 3, the latter with an empty
-rank). Phase math comes from ``tests/sharded_util.OraclePhases`` (float64),
+rank), followed by the single stack on each rank's query rows. Phase math comes from ``tests/sharded_util.OraclePhases`` (float64),
 so the comparison isolates the orchestration: tolerance 1e-10.
 """
 import os
@@ -15,7 +15,7 @@ import torch.multiprocessing as mp
 from fireprot_b200 import sharded as S
 from oracle import pairformer_oracle as O
 
-from sharded_util import OraclePhases, oracle_weight_dicts, run_threads
+from sharded_util import OraclePhases, oracle_weight_dicts, run_threads, single_weight_dict
 
 TOL = 1e-10
 
@@ -84,6 +84,37 @@ def test_sharded_block_threads(n, world, mask_kind):
         assert calls.count("trimul_finish") == 2 and calls.count("triattn_finish") == 2
 
 
+def _sharded_full_block(z, s, mask, p, ps, rank, comm):
+    """Whole Pairformer block: the sharded pair stack, then the single stack
+    on the rank's query rows with s all-gathered after it."""
+    sh = S.shard_plan(z.shape[0], comm.world, rank)
+    z_loc = S.local_rows(z, sh)
+    phases = OraclePhases()
+    S.sharded_pair_block(z_loc, mask, oracle_weight_dicts(p), sh, comm, phases)
+    s_buf = S.single_buffer(s, sh)
+    S.sharded_single_block(s_buf, z_loc, mask, single_weight_dict(ps), sh, comm, phases)
+    return S.gather_rows(z_loc, sh, comm), s_buf[:sh.n].clone(), phases.calls
+
+
+def _full_ref(z, s, mask, p, ps):
+    z1 = O.pair_block(z, mask, p)
+    return z1, O.single_block(s, z1, mask, ps)
+
+
+@pytest.mark.parametrize("n,world,mask_kind", [(40, 1, "padding"), (45, 2, "random"),
+                                               (70, 3, "none"), (33, 4, "padding")])
+def test_sharded_full_block_threads(n, world, mask_kind):
+    z, mask, p = _case(n, mask_kind)
+    s = O.make_single(n, seed=n, dtype=torch.float64)
+    ps = O.make_single_params(seed=7, dtype=torch.float64, ln_affine_random=True)
+    z_ref, s_ref = _full_ref(z, s, mask, p, ps)
+    outs = run_threads(world, lambda r, comm: _sharded_full_block(z, s, mask, p, ps, r, comm))
+    for z_full, s_full, calls in outs:
+        assert O.rel_max_err(z_full, z_ref) <= TOL
+        assert O.rel_max_err(s_full, s_ref) <= TOL
+        assert calls.count("single_block") == 1
+
+
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_sharded_trimul_add_false_threads(outgoing):
     n, world = 50, 2
@@ -114,8 +145,10 @@ def _gloo_rank(rank, world, port, n, mask_kind, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         z, mask, p = _case(n, mask_kind)
-        full, _ = _sharded_block(z, mask, p, rank, S.DistComm())
-        torch.save(full, os.path.join(out_dir, f"rank{rank}.pt"))
+        s = O.make_single(n, seed=n, dtype=torch.float64)
+        ps = O.make_single_params(seed=7, dtype=torch.float64)
+        z_full, s_full, _ = _sharded_full_block(z, s, mask, p, ps, rank, S.DistComm())
+        torch.save((z_full, s_full), os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -125,7 +158,9 @@ def test_sharded_block_gloo(tmp_path, n, world, mask_kind):
     mp.start_processes(_gloo_rank, args=(world, _free_port(), n, mask_kind, str(tmp_path)),
                        nprocs=world, start_method="spawn")
     z, mask, p = _case(n, mask_kind)
-    ref = O.pair_block(z, mask, p)
+    s = O.make_single(n, seed=n, dtype=torch.float64)
+    z_ref, s_ref = _full_ref(z, s, mask, p, O.make_single_params(seed=7, dtype=torch.float64))
     for r in range(world):
-        full = torch.load(tmp_path / f"rank{r}.pt")
-        assert O.rel_max_err(full, ref) <= TOL
+        z_full, s_full = torch.load(tmp_path / f"rank{r}.pt")
+        assert O.rel_max_err(z_full, z_ref) <= TOL
+        assert O.rel_max_err(s_full, s_ref) <= TOL

@@ -63,7 +63,9 @@ __global__ void ln_rows384_kernel(const float* __restrict__ x, float* __restrict
 // C[M][N] (op)= A[M][K] W[N][K]^T in FP32: 64 x 64 tiles, K steps of 16,
 // 256 threads with 4 x 4 outputs each. K is a multiple of 16 and every
 // leading dimension a multiple of 4 (384 or 1536 here).
-enum SgemmEpi { kEpiStore = 0, kEpiBias = 1, kEpiSigmoid = 2, kEpiAdd = 3 };
+// kEpiHeads stores head-major: column h*24 + d of row m goes to
+// Cm[(h * M + m) * 24 + d] (the attention's key / value layout).
+enum SgemmEpi { kEpiStore = 0, kEpiBias = 1, kEpiSigmoid = 2, kEpiAdd = 3, kEpiHeads = 4 };
 
 template <int kEpi>
 __global__ void __launch_bounds__(256)
@@ -114,7 +116,9 @@ __global__ void __launch_bounds__(256)
       const int nn = n0 + tx * 4 + v;
       if (nn >= N) continue;
       float r = acc[u][v];
-      float* dst = Cm + (size_t)m * ldc + nn;
+      float* dst = kEpi == kEpiHeads
+                       ? Cm + ((size_t)(nn / kSDim) * M + m) * kSDim + nn % kSDim
+                       : Cm + (size_t)m * ldc + nn;
       if constexpr (kEpi == kEpiBias) r += bias[nn];
       if constexpr (kEpi == kEpiSigmoid) r = sigmoidf_(r);
       if constexpr (kEpi == kEpiAdd) r += *dst;
@@ -132,66 +136,155 @@ void sgemm_nt(const float* A, int lda, const float* W, int ldw, float* Cm, int l
                                                               bias)));
 }
 
+// ---------------------------------------------------------------- cp.async
+// 16-byte global -> shared copies (no register staging); completion is the
+// hardware group wait, not a spin loop.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
 // ---------------------------------------------------------------- pair bias
+// LayerNorm affine folded into the head weights, once per call:
+//   wp[c][h] = ln_w[c] Wz[h][c],  bp[h] = sum_c ln_b[c] Wz[h][c]
+// so that LN(z) Wz^T = rs * sum_c (z_c - mean) wp[c][h] + bp[h].
+constexpr int kPBWeights = 128 * kSHeads + kSHeads;
+
+__global__ void single_bias_weights_kernel(const float* __restrict__ ln_w,
+                                           const float* __restrict__ ln_b,
+                                           const float* __restrict__ wz, float* __restrict__ out) {
+  __shared__ float part[4][kSHeads];
+  const int c = threadIdx.x, lane = c & 31, warp = c >> 5;  // 128 threads = channels
+#pragma unroll
+  for (int h = 0; h < kSHeads; ++h) {
+    const float w = wz[h * 128 + c];
+    out[c * kSHeads + h] = ln_w[c] * w;
+    const float t = warp_sum(ln_b[c] * w);
+    if (lane == 0) part[warp][h] = t;
+  }
+  __syncthreads();
+  if (c < kSHeads) out[128 * kSHeads + c] = part[0][c] + part[1][c] + part[2][c] + part[3][c];
+}
+
 // biasT[h][j][i - r0] = LN(z_ij) Wz^T + 1e9 (mask_ij - 1) for the call's query
-// rows i. One warp per (key j, 32 query rows): each pair row is a coalesced
-// 512-byte load, and lane l keeps the 16 head values of query i0 + l, so the
-// stores are 128-byte rows.
-__global__ void single_pair_bias_kernel(const float* __restrict__ z_loc,
-                                        const float* __restrict__ mask, int n, int rows, int r0,
-                                        const float* __restrict__ ln_w,
-                                        const float* __restrict__ ln_b,
-                                        const float* __restrict__ wz, float eps,
-                                        float* __restrict__ biasT) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int iblocks = (rows + 31) / 32;
-  if (warp >= n * iblocks) return;
-  const int j = warp / iblocks, i0 = (warp % iblocks) * 32;
-  const float4 lw = reinterpret_cast<const float4*>(ln_w)[lane];
-  const float4 lb = reinterpret_cast<const float4*>(ln_b)[lane];
-  float4 wh[kSHeads];
+// rows i. A block takes 128 query rows i of one key column j; warp w copies
+// the pair rows of its own 32 queries (512 bytes each, one warp-wide
+// 16-byte cp.async per row) into shared memory and waits for its own copies
+// only, so the warps of a block overlap loading and computing. Lane l then
+// normalises its row (two passes) and forms its 16 head values: every store
+// is a 32-query coalesced segment of biasT.
+constexpr int kPBRows = 128;
+constexpr int kPBStride = 132;  // floats per staged row: 16-byte aligned, no bank conflicts
+constexpr int kPBSmem = (kPBRows * kPBStride + kPBWeights) * 4;
+
+__global__ void __launch_bounds__(kPBRows)
+    single_pair_bias_kernel(const float* __restrict__ z_loc, const float* __restrict__ mask,
+                            int n, int rows, int r0, const float* __restrict__ wfold, float eps,
+                            float* __restrict__ biasT) {
+  extern __shared__ float4 pb_smem4[];
+  float* xs = reinterpret_cast<float*>(pb_smem4);
+  float* wp = xs + kPBRows * kPBStride;
+  const int iblocks = (rows + kPBRows - 1) / kPBRows;
+  const int j = blockIdx.x / iblocks;
+  const int i0 = (blockIdx.x % iblocks) * kPBRows;
+  const int cnt = min(kPBRows, rows - i0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < kPBWeights; e += kPBRows) wp[e] = wfold[e];
+  __syncthreads();  // the folded weights; the only block-wide barrier
+  // warp w: rows [32 w, 32 w + 32), lane = 16-byte chunk of the row
+  const int wr = min(32, cnt - warp * 32);
+#pragma unroll 4
+  for (int rr = 0; rr < wr; ++rr) {
+    const int r = warp * 32 + rr;
+    cp_async16(xs + r * kPBStride + lane * 4,
+               z_loc + ((size_t)(i0 + r) * n + j) * 128 + lane * 4);
+  }
+  cp_async_commit();
+  const int il = i0 + tid;
+  const float mb =
+      (mask && tid < cnt) ? kSMaskInf * (mask[(size_t)(r0 + il) * n + j] - 1.0f) : 0.f;
+  cp_async_wait<0>();
+  __syncwarp();
+  if (tid >= cnt) return;
+  const float4* xr = reinterpret_cast<const float4*>(xs + tid * kPBStride);
+  float sum = 0.f;
+#pragma unroll 8
+  for (int c4 = 0; c4 < 32; ++c4) {
+    const float4 x = xr[c4];
+    sum += (x.x + x.y) + (x.z + x.w);
+  }
+  const float mean = sum * (1.0f / 128.0f);
+  float acc[kSHeads];
 #pragma unroll
-  for (int h = 0; h < kSHeads; ++h) wh[h] = reinterpret_cast<const float4*>(wz + h * 128)[lane];
-  float mine[kSHeads];
+  for (int h = 0; h < kSHeads; ++h) acc[h] = 0.f;
+  float var = 0.f;
+  const float4* w4 = reinterpret_cast<const float4*>(wp);
+#pragma unroll 2
+  for (int c4 = 0; c4 < 32; ++c4) {
+    const float4 x = xr[c4];
+    const float xc[4] = {x.x - mean, x.y - mean, x.z - mean, x.w - mean};
 #pragma unroll
-  for (int h = 0; h < kSHeads; ++h) mine[h] = 0.f;
-  const int cnt = min(32, rows - i0);
-#pragma unroll 1
-  for (int ii = 0; ii < cnt; ++ii) {
-    const int il = i0 + ii;
-    const float4 x =
-        __ldg(reinterpret_cast<const float4*>(z_loc + ((size_t)il * n + j) * 128) + lane);
-    const float4 y = ln_row_warp(x, lw, lb, eps);
-    const float mb = mask ? kSMaskInf * (mask[(size_t)(r0 + il) * n + j] - 1.0f) : 0.f;
+    for (int u = 0; u < 4; ++u) {
+      var = fmaf(xc[u], xc[u], var);
 #pragma unroll
-    for (int h = 0; h < kSHeads; ++h) {
-      const float d = warp_sum(y.x * wh[h].x + y.y * wh[h].y + y.z * wh[h].z + y.w * wh[h].w);
-      if (lane == ii) mine[h] = d + mb;
+      for (int hq = 0; hq < kSHeads / 4; ++hq) {
+        const float4 w = w4[(c4 * 4 + u) * (kSHeads / 4) + hq];
+        acc[hq * 4 + 0] = fmaf(xc[u], w.x, acc[hq * 4 + 0]);
+        acc[hq * 4 + 1] = fmaf(xc[u], w.y, acc[hq * 4 + 1]);
+        acc[hq * 4 + 2] = fmaf(xc[u], w.z, acc[hq * 4 + 2]);
+        acc[hq * 4 + 3] = fmaf(xc[u], w.w, acc[hq * 4 + 3]);
+      }
     }
   }
-  const int il = i0 + lane;
-  if (il < rows) {
+  const float rs = rsqrtf(var * (1.0f / 128.0f) + eps);
+  const float* bp = wp + 128 * kSHeads;
 #pragma unroll
-    for (int h = 0; h < kSHeads; ++h) biasT[((size_t)h * n + j) * rows + il] = mine[h];
-  }
+  for (int h = 0; h < kSHeads; ++h)
+    biasT[((size_t)h * n + j) * rows + il] = fmaf(rs, acc[h], bp[h]) + mb;
 }
 
 // ---------------------------------------------------------------- attention
-// o[i][h*24 + d] for the call's query rows: one thread per query, 64
-// queries x one head per block, 32-key tiles of k and v in shared memory
-// (every thread reads the same key: broadcasts), online softmax with one
-// rescale per tile.
-constexpr int kSAttnThreads = 64;
+// o[i][h*24 + d] for the call's query rows. A block takes 32 queries (one
+// per lane) of one head; its 4 warps split every 64-key tile (16 keys each)
+// and keep their own online-softmax state, merged through shared memory at
+// the end. k and v are head-major ([16][n][24]), so a tile of one head is one
+// contiguous 6 KB block per operand, double-buffered by cp.async; the pair
+// bias of the next tile is loaded into registers while the current one runs.
+constexpr int kSAttnQ = 32;
+constexpr int kSAttnWarps = 4;
+constexpr int kSAttnTile = 64;
+constexpr int kSAttnKW = kSAttnTile / kSAttnWarps;  // keys per warp per tile
+constexpr int kSAttnTileF = kSAttnTile * kSDim;      // floats per operand tile
 
-__global__ void __launch_bounds__(kSAttnThreads)
-    single_attn_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                       const float* __restrict__ v, const float* __restrict__ biasT, int n,
+__device__ __forceinline__ void single_attn_load_tile(float* dst_k, float* dst_v,
+                                                      const float* kg, const float* vg, int j0,
+                                                      int n) {
+  const int chunks = min(kSAttnTile, n - j0) * (kSDim / 4);  // 16-byte chunks per operand
+  for (int e = threadIdx.x; e < chunks; e += kSAttnQ * kSAttnWarps) {
+    cp_async16(dst_k + e * 4, kg + (size_t)j0 * kSDim + e * 4);
+    cp_async16(dst_v + e * 4, vg + (size_t)j0 * kSDim + e * 4);
+  }
+}
+
+__global__ void __launch_bounds__(kSAttnQ * kSAttnWarps, 3)
+    single_attn_kernel(const float* __restrict__ q, const float* __restrict__ kh,
+                       const float* __restrict__ vh, const float* __restrict__ biasT, int n,
                        int rows, float* __restrict__ o) {
-  __shared__ float ks[32][kSDim];
-  __shared__ float vs[32][kSDim];
+  __shared__ __align__(16) float kv[2][2][kSAttnTileF];  // [buffer][k | v][key][24]
   const int h = blockIdx.y;
-  const int il = blockIdx.x * kSAttnThreads + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int il = blockIdx.x * kSAttnQ + lane;
   const bool valid = il < rows;
+  const float* kg = kh + (size_t)h * n * kSDim;
+  const float* vg = vh + (size_t)h * n * kSDim;
+  const float* bg = biasT + (size_t)h * n * rows + (valid ? il : 0);
   const float scale = rsqrtf((float)kSDim);
   float qv[kSDim], ov[kSDim];
 #pragma unroll
@@ -200,48 +293,115 @@ __global__ void __launch_bounds__(kSAttnThreads)
     ov[d] = 0.f;
   }
   float m_run = -INFINITY, l_run = 0.f;
-  for (int j0 = 0; j0 < n; j0 += 32) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < 32 * kSDim; e += kSAttnThreads) {
-      const int jj = e / kSDim, d = e % kSDim;
-      const int j = j0 + jj;
-      ks[jj][d] = j < n ? k[(size_t)j * kCs + h * kSDim + d] : 0.f;
-      vs[jj][d] = j < n ? v[(size_t)j * kCs + h * kSDim + d] : 0.f;
+  const int ntiles = (n + kSAttnTile - 1) / kSAttnTile;
+  single_attn_load_tile(kv[0][0], kv[0][1], kg, vg, 0, n);
+  cp_async_commit();
+  float bnext[kSAttnKW];
+#pragma unroll
+  for (int jj = 0; jj < kSAttnKW; ++jj) {
+    const int j = warp * kSAttnKW + jj;
+    bnext[jj] = (j < n && valid) ? bg[(size_t)j * rows] : 0.f;
+  }
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      single_attn_load_tile(kv[buf ^ 1][0], kv[buf ^ 1][1], kg, vg, (t + 1) * kSAttnTile, n);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    float sc[32];
+    const int jw = t * kSAttnTile + warp * kSAttnKW;  // first key of this warp's slice
+    float sc[kSAttnKW];
     float mx = -INFINITY;
+    const float4* k4 = reinterpret_cast<const float4*>(kv[buf][0] + warp * kSAttnKW * kSDim);
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int j = j0 + jj;
+    for (int jj = 0; jj < kSAttnKW; ++jj) {
       float s = -INFINITY;
-      if (j < n) {
-        s = valid ? biasT[((size_t)h * n + j) * rows + il] : 0.f;
+      if (jw + jj < n) {
+        float p0 = bnext[jj], p1 = 0.f;
 #pragma unroll
-        for (int d = 0; d < kSDim; ++d) s = fmaf(qv[d], ks[jj][d], s);
+        for (int d4 = 0; d4 < kSDim / 4; ++d4) {
+          const float4 kk = k4[jj * (kSDim / 4) + d4];
+          p0 = fmaf(qv[d4 * 4 + 0], kk.x, p0);
+          p1 = fmaf(qv[d4 * 4 + 1], kk.y, p1);
+          p0 = fmaf(qv[d4 * 4 + 2], kk.z, p0);
+          p1 = fmaf(qv[d4 * 4 + 3], kk.w, p1);
+        }
+        s = p0 + p1;
       }
       sc[jj] = s;
       mx = fmaxf(mx, s);
     }
-    const float m_new = fmaxf(m_run, mx);  // finite: key j0 < n is in the tile
-    const float alpha = __expf(m_run - m_new);  // 0 on the first tile
-    float ls = 0.f;
+    // bias of the next tile: in flight while this tile's P V runs
+    if (t + 1 < ntiles) {
 #pragma unroll
-    for (int d = 0; d < kSDim; ++d) ov[d] *= alpha;
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const float pj = __expf(sc[jj] - m_new);  // 0 for keys past n
-      ls += pj;
-#pragma unroll
-      for (int d = 0; d < kSDim; ++d) ov[d] = fmaf(pj, vs[jj][d], ov[d]);
+      for (int jj = 0; jj < kSAttnKW; ++jj) {
+        const int j = jw + kSAttnTile + jj;
+        bnext[jj] = (j < n && valid) ? bg[(size_t)j * rows] : 0.f;
+      }
     }
-    l_run = l_run * alpha + ls;
-    m_run = m_new;
-  }
-  if (valid) {
-    const float inv = 1.0f / l_run;
+    const float m_new = fmaxf(m_run, mx);
+    if (m_new != -INFINITY) {  // uniform: -inf only while no key of the slice is < n
+      const float alpha = __expf(m_run - m_new);
+      const float4* v4 = reinterpret_cast<const float4*>(kv[buf][1] + warp * kSAttnKW * kSDim);
+      float ls = 0.f;
 #pragma unroll
-    for (int d = 0; d < kSDim; ++d) o[(size_t)il * kCs + h * kSDim + d] = ov[d] * inv;
+      for (int d = 0; d < kSDim; ++d) ov[d] *= alpha;
+#pragma unroll
+      for (int jj = 0; jj < kSAttnKW; ++jj) {
+        if (jw + jj < n) {
+          const float pj = __expf(sc[jj] - m_new);
+          ls += pj;
+#pragma unroll
+          for (int d4 = 0; d4 < kSDim / 4; ++d4) {
+            const float4 vv = v4[jj * (kSDim / 4) + d4];
+            ov[d4 * 4 + 0] = fmaf(pj, vv.x, ov[d4 * 4 + 0]);
+            ov[d4 * 4 + 1] = fmaf(pj, vv.y, ov[d4 * 4 + 1]);
+            ov[d4 * 4 + 2] = fmaf(pj, vv.z, ov[d4 * 4 + 2]);
+            ov[d4 * 4 + 3] = fmaf(pj, vv.w, ov[d4 * 4 + 3]);
+          }
+        }
+      }
+      l_run = l_run * alpha + ls;
+      m_run = m_new;
+    }
+    __syncthreads();  // the buffer is refilled by the next iteration's copy
+  }
+  // merge the 4 key splits: state [warp][lane] = (m, l, o[24]) in the k/v space
+  float* st = &kv[0][0][0];
+  constexpr int kStateF = kSDim + 2;
+  float* mine = st + (warp * kSAttnQ + lane) * kStateF;
+  mine[0] = m_run;
+  mine[1] = l_run;
+#pragma unroll
+  for (int d = 0; d < kSDim; ++d) mine[2 + d] = ov[d];
+  __syncthreads();
+  if (!valid) return;
+  float mw[kSAttnWarps], M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kSAttnWarps; ++w) {
+    mw[w] = st[(w * kSAttnQ + lane) * kStateF];
+    M = fmaxf(M, mw[w]);  // finite: warp 0 always holds key 0
+  }
+  float den = 0.f, sw[kSAttnWarps];
+#pragma unroll
+  for (int w = 0; w < kSAttnWarps; ++w) {
+    sw[w] = __expf(mw[w] - M);  // 0 for a split that saw no key
+    den = fmaf(sw[w], st[(w * kSAttnQ + lane) * kStateF + 1], den);
+  }
+  const float inv = 1.0f / den;
+  // warp w writes dims [6w, 6w + 6) of its query
+  constexpr int kDW = kSDim / kSAttnWarps;
+#pragma unroll
+  for (int u = 0; u < kDW; ++u) {
+    const int d = warp * kDW + u;
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSAttnWarps; ++w)
+      acc = fmaf(sw[w], st[(w * kSAttnQ + lane) * kStateF + 2 + d], acc);
+    o[(size_t)il * kCs + h * kSDim + d] = acc * inv;
   }
 }
 
@@ -264,11 +424,12 @@ __global__ void single_swiglu_kernel(float* __restrict__ a, const float* __restr
 template <class Alloc>
 struct SinglePlan {
   float *a = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *o = nullptr;
-  float *biasT = nullptr, *ta = nullptr, *tb = nullptr;
+  float *biasT = nullptr, *ta = nullptr, *tb = nullptr, *wfold = nullptr;
   void plan(Alloc& al, int n, int rows) {
+    wfold = al.template take<float>(kPBWeights);
     a = al.template take<float>((size_t)n * kCs);  // LN(s), all rows
     q = al.template take<float>((size_t)rows * kCs);
-    k = al.template take<float>((size_t)n * kCs);
+    k = al.template take<float>((size_t)n * kCs);  // head-major [16][n][24]
     v = al.template take<float>((size_t)n * kCs);
     g = al.template take<float>((size_t)rows * kCs);
     o = al.template take<float>((size_t)rows * kCs);
@@ -327,19 +488,25 @@ extern "C" int fpb_single_block(float* s, const float* z_loc, const float* mask,
              (ln_rows384_kernel<<<(n + 7) / 8, 256, 0, stream>>>(s, pl.a, n, w->ln_a_w,
                                                                  w->ln_a_b, eps)));
   sgemm_nt<kEpiBias>(a_mine, kCs, w->w_q, kCs, pl.q, kCs, rows, kCs, kCs, w->b_q, stream);
-  sgemm_nt<kEpiStore>(pl.a, kCs, w->w_k, kCs, pl.k, kCs, n, kCs, kCs, nullptr, stream);
-  sgemm_nt<kEpiStore>(pl.a, kCs, w->w_v, kCs, pl.v, kCs, n, kCs, kCs, nullptr, stream);
+  sgemm_nt<kEpiHeads>(pl.a, kCs, w->w_k, kCs, pl.k, kCs, n, kCs, kCs, nullptr, stream);
+  sgemm_nt<kEpiHeads>(pl.a, kCs, w->w_v, kCs, pl.v, kCs, n, kCs, kCs, nullptr, stream);
   sgemm_nt<kEpiSigmoid>(a_mine, kCs, w->w_g, kCs, pl.g, kCs, rows, kCs, kCs, nullptr, stream);
+  FPB_LAUNCH("single_bias_weights", stream,
+             (single_bias_weights_kernel<<<1, 128, 0, stream>>>(w->ln_z_w, w->ln_z_b, w->w_z,
+                                                                pl.wfold)));
   {
-    const long long warps = (long long)n * ((rows + 31) / 32);
+    const long long blocks = (long long)n * ((rows + kPBRows - 1) / kPBRows);
+    if (blocks > 0x7fffffffll) return kErrShape;
+    cudaFuncSetAttribute(single_pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kPBSmem);
     FPB_LAUNCH("single_pair_bias", stream,
-               (single_pair_bias_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
-                   z_loc, mask, n, rows, r0, w->ln_z_w, w->ln_z_b, w->w_z, eps, pl.biasT)));
+               (single_pair_bias_kernel<<<(unsigned)blocks, kPBRows, kPBSmem, stream>>>(
+                   z_loc, mask, n, rows, r0, pl.wfold, eps, pl.biasT)));
   }
   FPB_LAUNCH("single_attn", stream,
-             (single_attn_kernel<<<dim3((rows + kSAttnThreads - 1) / kSAttnThreads, kSHeads),
-                                   kSAttnThreads, 0, stream>>>(pl.q, pl.k, pl.v, pl.biasT, n,
-                                                               rows, pl.o)));
+             (single_attn_kernel<<<dim3((rows + kSAttnQ - 1) / kSAttnQ, kSHeads),
+                                   kSAttnQ * kSAttnWarps, 0, stream>>>(pl.q, pl.k, pl.v,
+                                                                       pl.biasT, n, rows, pl.o)));
   const size_t cnt = (size_t)rows * kCs;
   FPB_LAUNCH("single_elementwise", stream,
              (single_mul_kernel<<<grid_for(cnt), 256, 0, stream>>>(pl.g, pl.o, cnt)));

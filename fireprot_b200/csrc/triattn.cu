@@ -570,12 +570,12 @@ __global__ void __launch_bounds__(192, 2)
     constexpr float kLog2e = 1.4426950408889634f;
     constexpr float kRescale = 8.0f / kLog2e;  // move the reference max past 2^8
     const uint64_t pol_bias = policy_evict_last();
-    // Additive terms of key tile t: the pair bias (a different row per
-    // thread) is loaded in one batch a tile ahead and added to q.k first;
-    // the mask bias row (the same for every thread, an L1 hit) and -inf past
-    // n are applied when the tile is consumed. (q.k + bias) + mask equals the
-    // reference's (q.k + mask) + bias: unmasked keys add 0, and for masked
-    // keys -1e9 absorbs any |x| < 32 in FP32 either way.
+    // Additive terms of key tile t, loaded in one batch a tile ahead: the
+    // pair bias (a different row per thread) plus the mask bias row (the
+    // same for every thread, an L1 hit); -inf past n is applied when the
+    // tile is consumed. q.k + (bias + mask) equals the reference's
+    // (q.k + mask) + bias: unmasked keys add 0, and for masked keys -1e9
+    // absorbs any |x| < 32 in FP32 in either order.
     auto load_bias = [&](int t, float (&cb)[C::BKV]) {
       const int k0 = t * C::BKV;
       if (jvalid && k0 + C::BKV <= n) {
@@ -587,33 +587,31 @@ __global__ void __launch_bounds__(192, 2)
           cb[4 * e4 + 2] = b.z;
           cb[4 * e4 + 3] = b.w;
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < C::BKV; ++e) {
-          const int k = k0 + e;
-          cb[e] = (jvalid && k < n) ? brow[(k >> 2) * 128 + (k & 3)] : 0.f;
-        }
-      }
-    };
-    auto add_mask = [&](int t, float (&sv)[C::BKV]) {
-      const int k0 = t * C::BKV;
-      if (k0 + C::BKV <= n) {
         if (mrow) {
 #pragma unroll
           for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
             const float4 m = ldg_f4_hint(mrow + k0 + 4 * e4, pol_bias);
-            sv[4 * e4] += m.x;
-            sv[4 * e4 + 1] += m.y;
-            sv[4 * e4 + 2] += m.z;
-            sv[4 * e4 + 3] += m.w;
+            cb[4 * e4] += m.x;
+            cb[4 * e4 + 1] += m.y;
+            cb[4 * e4 + 2] += m.z;
+            cb[4 * e4 + 3] += m.w;
           }
         }
       } else {
 #pragma unroll
         for (int e = 0; e < C::BKV; ++e) {
           const int k = k0 + e;
-          sv[e] = k < n ? sv[e] + (mrow ? mrow[k] : 0.f) : -INFINITY;
+          cb[e] = (jvalid && k < n) ? brow[(k >> 2) * 128 + (k & 3)] + (mrow ? mrow[k] : 0.f)
+                                    : 0.f;
         }
+      }
+    };
+    auto mask_tail = [&](int t, float (&sv)[C::BKV]) {
+      const int k0 = t * C::BKV;
+      if (k0 + C::BKV > n) {
+#pragma unroll
+        for (int e = 0; e < C::BKV; ++e)
+          if (k0 + e >= n) sv[e] = -INFINITY;
       }
     };
     float m_ref = -INFINITY, l_run = 0.f;
@@ -657,15 +655,17 @@ __global__ void __launch_bounds__(192, 2)
         break;
       }
       tc_fence_after();
+      {
+        uint32_t r[C::BKV / 16][16];
 #pragma unroll
-      for (int c = 0; c < C::BKV / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(buf + c * 16, r);
-        tmem_ld_wait();
+        for (int c = 0; c < C::BKV / 16; ++c) tmem_ld16(buf + c * 16, r[c]);
+        tmem_ld_wait();  // one round trip for the whole tile
 #pragma unroll
-        for (int e = 0; e < 16; ++e) sv[c * 16 + e] = __uint_as_float(r[e]) + cb[c * 16 + e];
+        for (int c = 0; c < C::BKV / 16; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sv[c * 16 + e] = __uint_as_float(r[c][e]) + cb[c * 16 + e];
       }
-      add_mask(t, sv);
+      mask_tail(t, sv);
       if (t + 1 < nt) load_bias(t + 1, cb);
       // four independent partial maxima / sums (short dependency chains)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};

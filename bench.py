@@ -485,7 +485,7 @@ def main():
     ap.add_argument("--precision", choices=["strict", "fast"], default="strict")
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--valid", type=int, default=1480)
-    ap.add_argument("--e2e-steps", type=int, default=4)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--mode", choices=["sharded", "replicas"], default="sharded",
                     help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")

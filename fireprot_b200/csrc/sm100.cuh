@@ -396,6 +396,13 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 // saturates to 0 / 1 for large |x|.
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
+// max of three (one instruction on sm_100; inputs are never NaN here)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // 2^x on the SFU (PTX ex2.approx.ftz.f32).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

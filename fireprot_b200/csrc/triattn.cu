@@ -576,46 +576,42 @@ __global__ void __launch_bounds__(192, 2)
     // tile is consumed. q.k + (bias + mask) equals the reference's
     // (q.k + mask) + bias: unmasked keys add 0, and for masked keys -1e9
     // absorbs any |x| < 32 in FP32 in either order.
-    auto load_bias = [&](int t, float (&cb)[C::BKV]) {
+    // key pairs (2e, 2e + 1) of a tile live in one float2: the adds,
+    // subtractions, scalings and sums run as packed FP32 pair instructions
+    // (the same rounding as two scalar operations)
+    constexpr int NP = C::BKV / 2;
+    auto load_bias = [&](int t, float2 (&cb)[NP]) {
       const int k0 = t * C::BKV;
       if (jvalid && k0 + C::BKV <= n) {
 #pragma unroll
         for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
           const float4 b = ldg_f4_hint(brow + ((k0 >> 2) + e4) * 128, pol_bias);
-          cb[4 * e4] = b.x;
-          cb[4 * e4 + 1] = b.y;
-          cb[4 * e4 + 2] = b.z;
-          cb[4 * e4 + 3] = b.w;
+          cb[2 * e4] = make_float2(b.x, b.y);
+          cb[2 * e4 + 1] = make_float2(b.z, b.w);
         }
         if (mrow) {
 #pragma unroll
           for (int e4 = 0; e4 < C::BKV / 4; ++e4) {
             const float4 m = ldg_f4_hint(mrow + k0 + 4 * e4, pol_bias);
-            cb[4 * e4] += m.x;
-            cb[4 * e4 + 1] += m.y;
-            cb[4 * e4 + 2] += m.z;
-            cb[4 * e4 + 3] += m.w;
+            cb[2 * e4] = __fadd2_rn(cb[2 * e4], make_float2(m.x, m.y));
+            cb[2 * e4 + 1] = __fadd2_rn(cb[2 * e4 + 1], make_float2(m.z, m.w));
           }
         }
       } else {
 #pragma unroll
         for (int e = 0; e < C::BKV; ++e) {
           const int k = k0 + e;
-          cb[e] = (jvalid && k < n) ? brow[(k >> 2) * 128 + (k & 3)] + (mrow ? mrow[k] : 0.f)
-                                    : 0.f;
+          const float v = (jvalid && k < n) ? brow[(k >> 2) * 128 + (k & 3)] + (mrow ? mrow[k] : 0.f)
+                                            : 0.f;
+          if (e & 1)
+            cb[e >> 1].y = v;
+          else
+            cb[e >> 1].x = v;
         }
       }
     };
-    auto mask_tail = [&](int t, float (&sv)[C::BKV]) {
-      const int k0 = t * C::BKV;
-      if (k0 + C::BKV > n) {
-#pragma unroll
-        for (int e = 0; e < C::BKV; ++e)
-          if (k0 + e >= n) sv[e] = -INFINITY;
-      }
-    };
     float m_ref = -INFINITY, l_run = 0.f;
-    float cb[C::BKV];
+    float2 cb[NP];
     load_bias(0, cb);
     // this thread's query row of Q (hi) -> TMEM, the A operand of the S MMAs
     bool ok = mbar_wait(q_full, 0, g, 20);
@@ -649,7 +645,7 @@ __global__ void __launch_bounds__(192, 2)
     }
     for (int t = 0; t < nt && ok; ++t) {
       const uint32_t buf = tb + (t & 1) * C::BUF_COLS;
-      float sv[C::BKV];
+      float2 sv[NP];
       if (!mbar_wait(&s_full[t & 1], (t >> 1) & 1, g, 26)) {
         ok = false;
         break;
@@ -663,51 +659,73 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
         for (int c = 0; c < C::BKV / 16; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) sv[c * 16 + e] = __uint_as_float(r[c][e]) + cb[c * 16 + e];
+          for (int e = 0; e < 16; e += 2)
+            sv[c * 8 + e / 2] = __fadd2_rn(
+                make_float2(__uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1])),
+                cb[c * 8 + e / 2]);
       }
-      mask_tail(t, sv);
+      if (t * C::BKV + C::BKV > n) {  // -inf past n (last tile only)
+#pragma unroll
+        for (int e = 0; e < NP; ++e) {
+          if (t * C::BKV + 2 * e >= n) sv[e].x = -INFINITY;
+          if (t * C::BKV + 2 * e + 1 >= n) sv[e].y = -INFINITY;
+        }
+      }
       if (t + 1 < nt) load_bias(t + 1, cb);
-      // four independent partial maxima / sums (short dependency chains)
+      // four independent partial maxima (3-input max: two keys per step)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 0; e < C::BKV; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], sv[e]);
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      for (int e = 0; e < NP; ++e) mx4[e & 3] = fmax3f(mx4[e & 3], sv[e].x, sv[e].y);
+      const float mx = fmax3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
       const bool move = mx > m_ref + kRescale;  // always on the first tile
       const float m_new = move ? mx : m_ref;
       const float alpha = move ? ex2_approx((m_ref - m_new) * kLog2e) : 1.0f;
       m_ref = m_new;
       // P(t) over S(t) (A operand of P V), 16 keys at a time
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 neg_m = make_float2(-m_ref, -m_ref);
+      const float2 l2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
       for (int c = 0; c < C::BKV / 16; ++c) {
-        float pv[16];
+        float2 pv[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          pv[e] = ex2_approx((sv[c * 16 + e] - m_ref) * kLog2e);
-          ls4[e & 3] += pv[e];
+        for (int e = 0; e < 8; ++e) {
+          const float2 a = __fmul2_rn(__fadd2_rn(sv[c * 8 + e], neg_m), l2e);
+          pv[e] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+          ls2[e & 1] = __fadd2_rn(ls2[e & 1], pv[e]);
         }
         if constexpr (kStrict) {
           // hi at columns [0, BKV), lo = x - hi (exact) at [BKV, 2 BKV)
           uint32_t part[16];
+          float2 hi[8];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) part[e] = __float_as_uint(pv[e]) & 0xFFFFE000u;
+          for (int e = 0; e < 8; ++e) {
+            hi[e] = make_float2(__uint_as_float(__float_as_uint(pv[e].x) & 0xFFFFE000u),
+                                __uint_as_float(__float_as_uint(pv[e].y) & 0xFFFFE000u));
+            part[2 * e] = __float_as_uint(hi[e].x);
+            part[2 * e + 1] = __float_as_uint(hi[e].y);
+          }
           tmem_st16(buf + c * 16, part);
+          const float2 neg1 = make_float2(-1.0f, -1.0f);
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            part[e] = __float_as_uint(pv[e] - __uint_as_float(__float_as_uint(pv[e]) & 0xFFFFE000u));
+          for (int e = 0; e < 8; ++e) {
+            const float2 lo = __ffma2_rn(hi[e], neg1, pv[e]);  // x - hi, exact
+            part[2 * e] = __float_as_uint(lo.x);
+            part[2 * e + 1] = __float_as_uint(lo.y);
+          }
           tmem_st16(buf + C::BKV + c * 16, part);
         } else {
           // bf16 pairs: 16 keys -> 8 columns
           uint32_t pk[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[2 * e], pv[2 * e + 1]);
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[e].x, pv[e].y);
             pk[e] = *reinterpret_cast<uint32_t*>(&b2);
           }
           tmem_st8(buf + c * 8, pk);
         }
       }
-      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+      l_run = l_run * alpha + ((ls2[0].x + ls2[0].y) + (ls2[1].x + ls2[1].y));
       // Observe every completion of pv_done in order (a parity wait cannot
       // tell phase k from phase k - 2): P V(t-1) was issued when this tile
       // started, so it has normally retired by now. Then a moved reference

@@ -7,7 +7,10 @@ Runs one operator (or the whole pair block) on a seeded synthetic pair tensor
 ``--iters`` times after ``--warmup`` runs and prints one JSON line with the
 mean device time per call and the per-kernel device times (CUDA events around
 every launch). Ops: trimul_out, trimul_in, triattn_start, triattn_end,
-transition, block, packed_bmm.
+transition, block, packed_bmm, single (the single stack, s [n, 384]),
+openfold3_attention (the OpenFold3 ``_attention`` scope on q, k, v
+[n, 4, n, 32] with a [1, 1, 1, n] mask and a [1, 4, n, n] bias, i.e. one
+triangle attention of an OpenFold3 trunk through the scope).
 """
 from __future__ import annotations
 
@@ -58,6 +61,34 @@ def main(argv=None):
     elif a.op == "transition":
         def run():
             blk.pair_transition(z, precision=a.precision)
+    elif a.op == "single":
+        from .modules import PairformerSingleBlock
+        sblk = PairformerSingleBlock().init_random_(2).to(dev)
+        s = torch.randn(n, 384, generator=g).to(dev)
+        sws = ops.single_block_workspace(n, n, dev)
+        cws = sblk.c_weights()
+
+        def run():
+            ops.single_block(s, z, mask, cws, precision=a.precision, workspace=sws)
+    elif a.op == "openfold3_attention":
+        from types import SimpleNamespace
+
+        from . import backend
+        from .openfold3 import AttentionCoreKernel, AttentionDispatcher, _scoped_hook
+        backend.set_precision(a.precision)
+        del z
+        q = (torch.randn(n, 4, n, 32, generator=g) / 32 ** 0.5).to(dev)
+        k = torch.randn(n, 4, n, 32, generator=g).to(dev)
+        v = torch.randn(n, 4, n, 32, generator=g).to(dev)
+        valid = (torch.arange(n) < n - n // 32).float()
+        biases = [(1e9 * (valid - 1.0)).view(1, 1, 1, n).to(dev),
+                  torch.randn(1, 4, n, n, generator=g).to(dev)]
+        target = SimpleNamespace(_attention=None)
+        disp = AttentionDispatcher(AttentionCoreKernel(0))
+
+        def run():
+            with torch.no_grad(), _scoped_hook(target, disp):
+                target._attention(q, k, v, biases)
     elif a.op == "packed_bmm":
         x = torch.randn(128, n, n, generator=g).to(dev)
         y = torch.randn(128, n, n, generator=g).to(dev)

@@ -194,7 +194,8 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
 
     q (pre-scaled), k, v: ``[B, 4, N, 32]`` float32, any strides; ``biases``
     is ``[triangle_bias]`` or ``[mask_bias, triangle_bias]`` with
-    ``mask_bias [B, 1, 1, N]`` and ``triangle_bias [1, 4, N, N]``. Returns
+    ``mask_bias [B, 1, 1, N]`` (or ``[1, 1, 1, N]``, shared by every batch
+    entry) and ``triangle_bias [1, 4, N, N]``, any non-negative strides. Returns
     ``[B, N, 4, 32]`` (``triangle_attention.py:129``).
     """
     _require_cuda(q, k, v, *biases)
@@ -212,8 +213,11 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
         raise RuntimeError("attention_core takes one or two biases")
     if tuple(tri.shape) != (1, 4, n, n):
         raise RuntimeError("triangle bias must be [1, 4, N, N]")
-    if mask_bias is not None and tuple(mask_bias.shape) != (batch, 1, 1, n):
-        raise RuntimeError("mask bias must be [B, 1, 1, N]")
+    if mask_bias is not None and (mask_bias.ndim != 4 or mask_bias.shape[0] not in (1, batch)
+                                  or tuple(mask_bias.shape[1:]) != (1, 1, n)):
+        raise RuntimeError("mask bias must be [B, 1, 1, N] or [1, 1, 1, N]")
+    if any(st < 0 for t in (q, k, v, *biases) for st in t.stride()):
+        raise RuntimeError("attention_core takes non-negative strides")
     lib = _lib.load()
     p = precision_code(precision)
     out = torch.empty(batch, n, 4, 32, dtype=torch.float32, device=q.device)
@@ -222,13 +226,17 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
 
     keep = []
 
-    def strides(t):
-        arr = (ctypes.c_longlong * 4)(*t.stride())
+    def strides(t, broadcast_batch=False):
+        st = list(t.stride())
+        if broadcast_batch:
+            st[0] = 0  # one mask row for every batch entry
+        arr = (ctypes.c_longlong * 4)(*st)
         keep.append(arr)
         return ctypes.cast(arr, ctypes.c_void_p)
 
     qs, ks, vs, ts = strides(q), strides(k), strides(v), strides(tri)
-    ms = strides(mask_bias) if mask_bias is not None else None
+    ms = (strides(mask_bias, broadcast_batch=mask_bias.shape[0] == 1)
+          if mask_bias is not None else None)
     _lib.check(lib.fpb_attention_core(
         q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, batch, n, 4, 32, tri.data_ptr(), ts,
         0 if mask_bias is None else mask_bias.data_ptr(), ms, out.data_ptr(), p, ws.data_ptr(),

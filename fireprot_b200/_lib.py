@@ -52,6 +52,9 @@ SIGNATURES = {
     "fpb_single_block_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "fpb_single_block": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                  c_void_p, c_float, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_triangle_contract_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "fpb_triangle_contract": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                      c_void_p, c_size_t, c_void_p]),
     "fpb_timing_enable": (c_int, [c_int]),
     "fpb_timing_collect": (c_int, [ctypes.c_char_p, c_size_t]),
     "fpb_attention_core_workspace_size": (c_size_t, [c_int] * 6),

@@ -178,7 +178,10 @@ __global__ void __launch_bounds__(192, 1)
         OutT* out;
         if (args.blocked)
           out = reinterpret_cast<OutT*>(args.out) +
-                ((((size_t)row * args.njb + (col0 >> 7)) * 128 + ch) << 7) + (col0 & 127) - col0;
+                ((((size_t)row * args.njb + (col0 >> 7)) * (args.bchannels ? args.bchannels : 128) +
+                   ch)
+                 << 7) +
+                (col0 & 127) - col0;
         else
           out = reinterpret_cast<OutT*>(args.out) + (size_t)ch * args.out_channel_stride +
                 (size_t)row * args.ldo;

@@ -38,9 +38,10 @@ struct ContractArgs {
   int* status;
   // blocked layout (when blocked != 0): out[i][j / 128][c][j % 128] with
   // njb = ceil(n / 128) column blocks; one pair-row tile of the output
-  // kernel (128 columns x 128 channels) is then one contiguous block.
+  // kernel (128 columns x all channels) is then one contiguous block.
   int blocked;
   int njb;
+  int bchannels;  // channels per block of the blocked layout (0: 128)
 };
 
 int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream);

@@ -10,7 +10,9 @@ every launch). Ops: trimul_out, trimul_in, triattn_start, triattn_end,
 transition, block, packed_bmm, single (the single stack, s [n, 384]),
 openfold3_attention (the OpenFold3 ``_attention`` scope on q, k, v
 [n, 4, n, 32] with a [1, 1, 1, n] mask and a [1, 4, n, n] bias, i.e. one
-triangle attention of an OpenFold3 trunk through the scope).
+triangle attention of an OpenFold3 trunk through the scope),
+esm_contract_out / esm_contract_in (ESMFold2's channels-last triangle
+contraction, [1, n, n, 256]).
 """
 from __future__ import annotations
 
@@ -89,6 +91,14 @@ def main(argv=None):
         def run():
             with torch.no_grad(), _scoped_hook(target, disp):
                 target._attention(q, k, v, biases)
+    elif a.op in ("esm_contract_out", "esm_contract_in"):
+        del z
+        lt = torch.randn(1, n, n, 256, generator=g).to(dev)
+        rt = torch.randn(1, n, n, 256, generator=g).to(dev)
+
+        def run():
+            ops.triangle_contract(lt, rt, outgoing=a.op == "esm_contract_out",
+                                  precision=a.precision)
     elif a.op == "packed_bmm":
         x = torch.randn(128, n, n, generator=g).to(dev)
         y = torch.randn(128, n, n, generator=g).to(dev)

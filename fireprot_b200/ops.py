@@ -325,6 +325,36 @@ def single_block(s: torch.Tensor, z_loc: torch.Tensor, mask, c_weights, *, r0: i
     return (s, ws) if return_workspace else s
 
 
+def triangle_contract(left: torch.Tensor, right: torch.Tensor, *, outgoing: bool,
+                      precision="strict", return_workspace: bool = False):
+    """ESMFold2's triangle contraction on channels-last ``[n, n, C]`` (or
+    ``[1, n, n, C]``) FP32 tensors: outgoing ``x_ijc = sum_k l_ikc r_jkc``,
+    incoming ``x_ijc = sum_k l_kic r_kjc``. Returns a new tensor shaped like
+    ``left``."""
+    _require_cuda(left, right)
+    if left.shape != right.shape or left.dtype != torch.float32 or right.dtype != torch.float32:
+        raise RuntimeError("triangle_contract takes two float32 tensors of one shape")
+    shape = tuple(left.shape)
+    if len(shape) == 4 and shape[0] == 1:
+        shape3 = shape[1:]
+    elif len(shape) == 3:
+        shape3 = shape
+    else:
+        raise RuntimeError("triangle_contract takes [n, n, C] or [1, n, n, C]")
+    n, n2, c = shape3
+    if n != n2 or c % 32:
+        raise RuntimeError("triangle_contract needs a square pair tensor and C % 32 == 0")
+    left, right = left.contiguous(), right.contiguous()
+    lib = _lib.load()
+    p = precision_code(precision)
+    out = torch.empty_like(left)
+    ws = workspace(lib.fpb_triangle_contract_workspace_size(n, c, p), left.device)
+    _lib.check(lib.fpb_triangle_contract(left.data_ptr(), right.data_ptr(), out.data_ptr(), n, c,
+                                         int(bool(outgoing)), p, ws.data_ptr(), ws.numel(),
+                                         _stream_ptr(left.device)), "fpb_triangle_contract")
+    return (out, ws) if return_workspace else out
+
+
 def timing_enable(on: bool = True) -> None:
     _lib.load().fpb_timing_enable(int(bool(on)))
 

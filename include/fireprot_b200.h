@@ -286,6 +286,19 @@ int fpb_single_block(float* s, const float* z_loc, const float* mask, int n, int
                      int c_s, const fpb_single_block_weights* weights, float eps, int precision,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Triangle contraction on channels-last tensors, ESMFold2's form
+ * (TriangleMultiplicativeBlock._triangular_contract_chunked as dispatched by
+ * python/fireprot/adapters/esmfold2/triangle.py:19-33, C = 256 there):
+ *   outgoing (outgoing = 1): out[i][j][c] = sum_k left[i][k][c] * right[j][k][c]
+ *   incoming (outgoing = 0): out[i][j][c] = sum_k left[k][i][c] * right[k][j][c]
+ * left, right, out: [n, n, channels] FP32, channels a multiple of 32. The
+ * reference's chunking over i (chunk_size 64) only bounds its memory and is
+ * not part of the result. */
+size_t fpb_triangle_contract_workspace_size(int n, int channels, int precision);
+int fpb_triangle_contract(const float* left, const float* right, float* out, int n, int channels,
+                          int outgoing, int precision, void* workspace, size_t workspace_bytes,
+                          cudaStream_t stream);
+
 /* Per-launch device timing on the calling thread (CUDA events around every
  * kernel launch of this library). fpb_timing_collect synchronises and writes
  * {"kernel": {"launches": L, "total_ms": T}, ...} as JSON. */

@@ -316,6 +316,20 @@ def pair_block(z, mask, p: PairBlockParams, *, attn_chunk: int = 64):
 
 
 # --------------------------------------------------------------------------
+# ESMFold2 triangle contraction (channels last, C = 256 upstream)
+# --------------------------------------------------------------------------
+def triangle_contract(left, right, *, outgoing: bool):
+    """``python/fireprot/adapters/esmfold2/triangle.py:19-33``: outgoing
+    ``x_ijc = sum_k l_ikc r_jkc``, incoming ``x_ijc = sum_k l_kic r_kjc`` on
+    ``[..., n, n, C]`` tensors. Its loop over chunks of i only bounds memory
+    (every output element is one dot product over k), so the restatement is
+    one einsum per direction."""
+    if outgoing:
+        return torch.einsum("...ikc,...jkc->...ijc", left, right)
+    return torch.einsum("...kic,...kjc->...ijc", left, right)
+
+
+# --------------------------------------------------------------------------
 # tolerance checks (north star: strict 1e-4, fast 1e-2, relative to the
 # fp32 output scale max|ref|)
 # --------------------------------------------------------------------------

@@ -3,8 +3,9 @@
 The fixtures come from ``tests/golden/make_golden.py`` (reference functions
 ``adapters/atlasfold/runtime.py:32-87``,
 ``backends/amd/triangle_multiplication.py:136-193``,
-``backends/amd/recycle.py:203-227`` and
-``backends/amd/triangle_attention.py:83-129``). The tolerance is the
+``backends/amd/recycle.py:203-227``,
+``backends/amd/triangle_attention.py:83-129`` and
+``adapters/esmfold2/triangle.py:19-33``). The tolerance is the
 reference's own op-level FP32 agreement, ``2e-5`` (``tests/operators/
 test_ck_attention.py:79``), relative to the output scale.
 """
@@ -146,3 +147,15 @@ def test_float64_second_opinion_agrees():
     # logits (uniform weights) while fp64 keeps them; valid entries never read
     # padded ones, so compare the valid 10x10 region.
     assert O.rel_max_err(out32[:10, :10], out64[:10, :10]) < 1e-5
+
+
+@pytest.mark.parametrize("case", ["n10_c32", "n6_c256"])
+@pytest.mark.parametrize("flow", ["outgoing", "incoming"])
+def test_esmfold2_contraction_matches_reference(case, flow):
+    """``adapters/esmfold2/triangle.py:19-33`` ``packed_contract`` (chunk 4,
+    ragged last chunk at n = 10) against the one-einsum restatement."""
+    data, meta = _load(f"esm_contract_{case}_{flow}")
+    left = O.make_pair(meta["n"], meta["c"], seed=meta["left_seed"]).unsqueeze(0)
+    right = O.make_pair(meta["n"], meta["c"], seed=meta["right_seed"]).unsqueeze(0)
+    assert _checksum(left, right) == pytest.approx(float(data["inputs_checksum"]), rel=1e-12)
+    _compare(data, O.triangle_contract(left, right, outgoing=flow == "outgoing")[0])

@@ -337,14 +337,18 @@ struct AttnCfg {
   static constexpr int QK_STEPS = QK_ROW / 32;         // 32-byte K steps over d
   static constexpr int KSTEP_KEYS = kStrict ? 8 : 16;  // keys per P V K step
   static constexpr int PV_STEPS = BKV / KSTEP_KEYS;
-  // TMEM: two S/P buffers (S(t) is read, then P(t) overwrites it: tf32
-  // hi | lo = 2 BKV columns, bf16 pairs = BKV / 2), O (32 columns) and the
-  // query tile's A operand for the S MMAs (Q_hi, tf32: 32 columns; Q, bf16
-  // pairs: 16 columns), so those MMAs read only K from shared memory
-  static constexpr int BUF_COLS = kStrict ? 2 * BKV : BKV;
-  static constexpr uint32_t kO = 2 * BUF_COLS;
+  // TMEM: two S/P buffers of BKV columns (S(t) is read, then P(t)
+  // overwrites it: tf32 P_hi, or bf16 pairs), O (32 columns) and the A
+  // operands of the S MMAs (Q_hi and Q_lo, 32 columns each; bf16 Q pairs,
+  // 16), so every MMA reads only B from shared memory. Strict mode keeps
+  // P_lo of the tile in flight in one region of BKV columns shared by both
+  // buffers: the softmax writes P_lo(t) only after P V(t-1) has retired.
+  static constexpr int BUF_COLS = BKV;
+  static constexpr uint32_t kPLO = 2 * BUF_COLS;  // strict only
+  static constexpr uint32_t kO = kStrict ? kPLO + BKV : 2 * BUF_COLS;
   static constexpr uint32_t kQ = kO + 32;
-  static constexpr int Q_COLS = kStrict ? 32 : 16;
+  static constexpr uint32_t kQL = kQ + 32;  // strict only
+  static constexpr int Q_COLS = kStrict ? 64 : 16;
   static constexpr int TMEM_COLS = 256;
   static_assert(kQ + Q_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(BKV % KSTEP_KEYS == 0 && BKV % 16 == 0, "key tile shape");
@@ -474,7 +478,6 @@ __global__ void __launch_bounds__(192, 2)
     if (lane == 0) {
       const uint32_t id_s = kStrict ? idesc_tf32(128, C::BKV) : idesc_bf16(128, C::BKV);
       const uint32_t id_o = kStrict ? idesc_tf32(128, 32) : idesc_bf16(128, 32);
-      const uint32_t q_lo = smem_u32(Q) + C::Q_BYTES;
       auto issue_s = [&](int t) {
         const uint32_t kst = smem_u32(KV + (t % C::KV_STAGES) * C::KV_STAGE);
         const uint32_t sbuf = tmem + (t & 1) * C::BUF_COLS;
@@ -485,11 +488,10 @@ __global__ void __launch_bounds__(192, 2)
           const uint64_t dkh = qk_desc<kStrict>(kst + off);
           const uint32_t acc = kk == 0 ? 0u : 1u;
           if constexpr (kStrict) {
-            const uint64_t dql = qk_desc<kStrict>(q_lo + off);
             const uint64_t dkl = qk_desc<kStrict>(kst + C::K_BYTES + off);
-            umma_tf32_ts(sbuf, qa, dkh, id_s, acc);  // Q_hi K_hi
-            umma_tf32_ts(sbuf, qa, dkl, id_s, 1u);   // Q_hi K_lo
-            umma_tf32(sbuf, dql, dkh, id_s, 1u);     // Q_lo K_hi
+            umma_tf32_ts(sbuf, qa, dkh, id_s, acc);                      // Q_hi K_hi
+            umma_tf32_ts(sbuf, qa, dkl, id_s, 1u);                       // Q_hi K_lo
+            umma_tf32_ts(sbuf, tmem + C::kQL + kk * 8, dkh, id_s, 1u);   // Q_lo K_hi
           } else {
             umma_bf16_ts(sbuf, qa, dkh, id_s, acc);
           }
@@ -513,7 +515,7 @@ __global__ void __launch_bounds__(192, 2)
             const uint64_t dvl = umma_desc_sw64(vst + C::V_BYTES + vo);
             umma_tf32_ts(d_o, pa + kk * 8, dvh, id_o, acc);             // P_hi V_hi
             umma_tf32_ts(d_o, pa + kk * 8, dvl, id_o, 1u);              // P_hi V_lo
-            umma_tf32_ts(d_o, pa + C::BKV + kk * 8, dvh, id_o, 1u);     // P_lo V_hi
+            umma_tf32_ts(d_o, tmem + C::kPLO + kk * 8, dvh, id_o, 1u);  // P_lo V_hi
           } else {
             umma_bf16_ts(d_o, pa + kk * 8, umma_desc_sw128(vst + vo), id_o, acc);
           }
@@ -613,20 +615,25 @@ __global__ void __launch_bounds__(192, 2)
     float m_ref = -INFINITY, l_run = 0.f;
     float2 cb[NP];
     load_bias(0, cb);
-    // this thread's query row of Q (hi) -> TMEM, the A operand of the S MMAs
+    // this thread's query row of Q (hi and lo) -> TMEM, the A operands of
+    // the S MMAs
     bool ok = mbar_wait(q_full, 0, g, 20);
     if (ok) {
       if constexpr (kStrict) {
-        uint32_t qr[32];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const uint4 v = *reinterpret_cast<const uint4*>(Q + sw128_offset(t_row, e * 16));
-          qr[4 * e] = v.x;
-          qr[4 * e + 1] = v.y;
-          qr[4 * e + 2] = v.z;
-          qr[4 * e + 3] = v.w;
+        for (int part = 0; part < 2; ++part) {
+          uint32_t qr[32];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint4 v = *reinterpret_cast<const uint4*>(Q + part * C::Q_BYTES +
+                                                            sw128_offset(t_row, e * 16));
+            qr[4 * e] = v.x;
+            qr[4 * e + 1] = v.y;
+            qr[4 * e + 2] = v.z;
+            qr[4 * e + 3] = v.w;
+          }
+          tmem_st32(tb + (part == 0 ? C::kQ : C::kQL), qr);
         }
-        tmem_st32(tb + C::kQ, qr);
       } else {
         uint32_t qr[16];
 #pragma unroll
@@ -681,8 +688,10 @@ __global__ void __launch_bounds__(192, 2)
       const float m_new = move ? mx : m_ref;
       const float alpha = move ? ex2_approx((m_ref - m_new) * kLog2e) : 1.0f;
       m_ref = m_new;
-      // P(t) over S(t) (A operand of P V), 16 keys at a time
+      // P(t) over S(t) (A operand of P V), 16 keys at a time; strict P_lo
+      // waits in registers until P V(t-1) has read the shared P_lo region
       float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint32_t plo[kStrict ? C::BKV : 1];
       const float2 neg_m = make_float2(-m_ref, -m_ref);
       const float2 l2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
@@ -695,7 +704,7 @@ __global__ void __launch_bounds__(192, 2)
           ls2[e & 1] = __fadd2_rn(ls2[e & 1], pv[e]);
         }
         if constexpr (kStrict) {
-          // hi at columns [0, BKV), lo = x - hi (exact) at [BKV, 2 BKV)
+          // P_hi over S(t); lo = x - hi (exact) kept for the shared region
           uint32_t part[16];
           float2 hi[8];
 #pragma unroll
@@ -710,10 +719,9 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float2 lo = __ffma2_rn(hi[e], neg1, pv[e]);  // x - hi, exact
-            part[2 * e] = __float_as_uint(lo.x);
-            part[2 * e + 1] = __float_as_uint(lo.y);
+            plo[c * 16 + 2 * e] = __float_as_uint(lo.x);
+            plo[c * 16 + 2 * e + 1] = __float_as_uint(lo.y);
           }
-          tmem_st16(buf + C::BKV + c * 16, part);
         } else {
           // bf16 pairs: 16 keys -> 8 columns
           uint32_t pk[8];
@@ -736,6 +744,15 @@ __global__ void __launch_bounds__(192, 2)
           break;
         }
         tc_fence_after();
+      }
+      if constexpr (kStrict) {
+#pragma unroll
+        for (int c = 0; c < C::BKV / 16; ++c) {
+          uint32_t part[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) part[e] = plo[c * 16 + e];
+          tmem_st16(tb + C::kPLO + c * 16, part);
+        }
       }
       if (t > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll

@@ -1,7 +1,9 @@
 """torchrun worker for ``test_gpu_sharded_nccl.py``: one process per GPU,
-NCCL process group, the sharded pair block on each rank's rows, then rank 0
-compares the all-gathered result with the CPU oracle and writes a JSON
-verdict to ``argv[1]``. Every rank runs the same collective sequence."""
+NCCL process group, the whole Pairformer block on each rank's rows (the
+sharded pair stack, then the single stack on the rank's query rows and the
+all-gather of s), then rank 0 compares the all-gathered z and s with the CPU
+oracle and writes a JSON verdict to ``argv[1]``. Every rank runs the same
+collective sequence."""
 import datetime
 import json
 import os
@@ -17,7 +19,7 @@ import torch.distributed as dist  # noqa: E402
 
 from fireprot_b200 import sharded as S  # noqa: E402
 from oracle import pairformer_oracle as O  # noqa: E402
-from sharded_util import oracle_weight_dicts  # noqa: E402
+from sharded_util import oracle_weight_dicts, single_weight_dict  # noqa: E402
 
 
 def main(out_path: str) -> None:
@@ -35,20 +37,28 @@ def main(out_path: str) -> None:
             w = {k: {kk: (None if vv is None else vv.to(dev)) for kk, vv in d.items()}
                  for k, d in oracle_weight_dicts(p).items()}
             md = None if mask is None else mask.to(dev)
+            s = O.make_single(n, seed=n)
+            ps = O.make_single_params(seed=19, ln_affine_random=True)
+            ws = {k: v.to(dev) for k, v in single_weight_dict(ps).items()}
             sh = S.shard_plan(n, comm.world, comm.rank)
             ref = O.pair_block(z, mask, p) if comm.rank == 0 else None
+            s_ref = O.single_block(s, ref, mask, ps) if comm.rank == 0 else None
             for precision in ("strict", "fast"):
                 z_loc = S.local_rows(z.to(dev), sh)
+                s_buf = S.single_buffer(s.to(dev), sh)
                 ph = S.CudaPhases(precision)
                 S.sharded_pair_block(z_loc, md, w, sh, comm, ph)
+                S.sharded_single_block(s_buf, z_loc, md, ws, sh, comm, ph)
                 torch.cuda.synchronize(dev)
                 ph.check()
                 full = S.gather_rows(z_loc, sh, comm).cpu()
                 if comm.rank == 0:
                     tol = O.STRICT_TOL if precision == "strict" else O.FAST_TOL
                     err = O.rel_max_err(full, ref)
-                    results[f"n{n}_{mask_kind}_{precision}"] = {"err": err, "tol": tol,
-                                                               "ok": err <= tol}
+                    err_s = O.rel_max_err(s_buf[:n].cpu(), s_ref)
+                    results[f"n{n}_{mask_kind}_{precision}"] = {"err": err, "err_s": err_s,
+                                                               "tol": tol,
+                                                               "ok": err <= tol and err_s <= tol}
         dist.barrier()
     finally:
         dist.destroy_process_group()

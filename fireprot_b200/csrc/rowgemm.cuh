@@ -75,21 +75,21 @@ __device__ __forceinline__ float4 ln_row_warp(float4 x, float4 w, float4 b, floa
                      d3 * rs * w.w + b.w);
 }
 
-// LayerNorm of the 32 pair rows [row0, row0 + 32) of a tile into the A
-// operand, warp-cooperative (lane l owns channels 4l..4l+3). `src(row)`
+// LayerNorm of the kRows pair rows [row0, row0 + kRows) of a tile into the
+// A operand, warp-cooperative (lane l owns channels 4l..4l+3). `src(row)`
 // returns the row's float4 base pointer, or nullptr for a padding row
 // (normalised from zeros). Every load of a batch of kBatch rows is issued
-// before the batch's first row is normalised, so a warp pays 32 / kBatch
+// before the batch's first row is normalised, so a warp pays kRows / kBatch
 // memory round trips per tile. `per_row(row, y)` sees each normalised row
 // (called by the whole warp). kNC: the rows are not written during the
 // kernel by anyone but this CTA, after this call (non-coherent loads).
-template <bool kStrict, int kBatch, bool kNC, class Src, class PerRow>
+template <bool kStrict, int kBatch, bool kNC, class Src, class PerRow, int kRows = 32>
 __device__ __forceinline__ void ln_rows_to_a(uint8_t* A, int row0, const Src& src, float4 lw,
                                              float4 lb, float eps, const PerRow& per_row) {
-  static_assert(32 % kBatch == 0, "batch must divide the warp's 32 rows");
+  static_assert(kRows % kBatch == 0, "batch must divide the warp's rows");
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
-  for (int b0 = 0; b0 < 32; b0 += kBatch) {
+  for (int b0 = 0; b0 < kRows; b0 += kBatch) {
     float4 x[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {

@@ -396,6 +396,22 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 // saturates to 0 / 1 for large |x|.
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
+// True on every thread of named barrier `id` (`count` threads) when `pred`
+// is true on any of them: the threads of a loop that ends on a failed
+// bounded wait leave it together, so none is left at a later bar.sync.
+__device__ __forceinline__ bool bar_any(bool pred, int id, int count) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // max of three (one instruction on sm_100; inputs are never NaN here)
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float r;

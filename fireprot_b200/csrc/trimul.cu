@@ -40,24 +40,26 @@ struct TriMulProjArgs {
   size_t cs;
   int* status;
   int b_plain;  // strict: write b unsplit (FP32) into the b_hi planes
+  int ntiles;   // yrows x ceil(ycols / 128) tiles, walked by a persistent grid
 };
+
+// Weight ring depth of the projection kernel: three 32 KB strict stages
+// plus the 128 KB A tile fit in 227 KB; the ring runs across tiles, so the
+// first weights of the next tile load during the current epilogue.
+constexpr int kProjWStages = 3;
 
 template <bool kStrict>
 constexpr int proj_smem_bytes() {
   using C = RowCfg<kStrict>;
-  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256, 512);
+  return tmem_safe_smem(C::A_BYTES + kProjWStages * C::WSTAGE_BYTES + 1024 + 256, 512);
 }
 
 template <bool kStrict, bool kTrans>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     trimul_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
-                       const __grid_constant__ CUtensorMap w_lo,
-                       const __grid_constant__ CUtensorMap st_a_hi,
-                       const __grid_constant__ CUtensorMap st_a_lo,
-                       const __grid_constant__ CUtensorMap st_b_hi,
-                       const __grid_constant__ CUtensorMap st_b_lo, TriMulProjArgs p) {
+                       const __grid_constant__ CUtensorMap w_lo, TriMulProjArgs p) {
   using C = RowCfg<kStrict>;
-  constexpr int WSTAGES = 2;
+  constexpr int WSTAGES = kProjWStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -66,17 +68,19 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(W + WSTAGES * C::WSTAGE_BYTES);
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
-  uint64_t* a_full = bars + 2 * WSTAGES;
-  uint64_t* done = a_full + 1;
-  uint64_t* drain = done + 1;
+  uint64_t* a_full = bars + 2 * WSTAGES;  // A of the tile written (LN warps)
+  uint64_t* done_a = a_full + 1;          // accumulators of part a ready (MMA)
+  uint64_t* done_b = done_a + 1;          // part b ready; every MMA of the tile read A
+  uint64_t* free_a = done_b + 1;          // part a accumulators read (epilogue warps)
+  uint64_t* free_b = free_a + 1;          // part b accumulators read
+  uint64_t* drain = free_b + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // tile = (y row r, 128-column block jb): a tile never straddles two y rows,
-  // so each output plane receives one [128 channels][128 columns] box
+  // tile = (y row r, 128-column block jb): a tile never straddles two y rows.
+  // The grid is persistent: CTA b takes tiles b, b + gridDim.x, ...
   const int njb = (p.ycols + 127) / 128;
-  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -84,12 +88,15 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&wempty[s], 1);
     }
     mbar_init(a_full, 128);
-    mbar_init(done, 1);
+    mbar_init(done_a, 1);
+    mbar_init(done_b, 1);
+    mbar_init(free_a, 128);
+    mbar_init(free_b, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -102,97 +109,133 @@ __global__ void __launch_bounds__(192, 1)
   constexpr int NLOADS = 4 * C::NKA;  // 4 chunks of 128 outputs x K atoms
 
   if (warp < 4) {
-    // ---- producer: LayerNorm of 32 rows per warp into the A tile
+    // ---- LayerNorm warps: 32 rows each into A, once the MMAs of the
+    // previous tile have read it
     const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
     const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
-    auto src = [&](int row) -> const float4* {
-      const int s = s0 + row;
-      if (s >= p.ycols) return nullptr;
-      return z4 + (kTrans ? ((long long)s * p.zcols + r) : ((long long)r * p.zcols + s)) * 32;
-    };
-    ln_rows_to_a<kStrict, 32, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
-    fence_proxy_async_smem();
-    mbar_arrive(a_full);
-
-    // ---- epilogue: thread t owns tile row t (TMEM lane t). Each part (a,
-    // then b) is staged in the A buffer as [channel][128 columns] planes and
-    // written by one TMA store per plane (columns past ycols are clipped).
-    const int t = warp * 32 + lane;
-    const int s = s0 + t;
-    float m = 1.f;
-    if (p.mask && s < p.ycols)
-      m = __ldg(p.mask + (kTrans ? ((size_t)(p.r0 + s) * p.zcols + r)
-                                 : ((size_t)(p.r0 + r) * p.zcols + s)));
-    if (mbar_wait(done, 0, g, 3)) {
-      tc_fence_after();
 #pragma unroll 1
-      for (int part = 0; part < 2; ++part) {
-        if (part == 1) {
-          // the stores of part a must have read the staging buffer
-          if (t == 0) tma_store_wait_read();
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+    for (int it = 0, tile = blockIdx.x; tile < p.ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      if (it > 0 && !mbar_wait(done_b, (it - 1) & 1, g, 5)) break;
+      auto src = [&](int row) -> const float4* {
+        const int sc = s0 + row;
+        if (sc >= p.ycols) return nullptr;
+        return z4 + (kTrans ? ((long long)sc * p.zcols + r) : ((long long)r * p.zcols + sc)) * 32;
+      };
+      ln_rows_to_a<kStrict, 16, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+    }
+  } else if (warp < 8) {
+    // ---- epilogue warps: thread t owns tile row t (TMEM lane t) =
+    // column s0 + t of every output plane; a warp's stores to one channel
+    // are 32 consecutive columns (128 coalesced bytes in strict mode)
+    const int quad = warp & 3;
+    const int t = quad * 32 + lane;
+#pragma unroll 1
+    for (int it = 0, tile = blockIdx.x; tile < p.ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      const int s = s0 + t;
+      const bool valid = s < p.ycols;
+      float m = 1.f;
+      if (p.mask && valid)
+        m = __ldg(p.mask + (kTrans ? ((size_t)(p.r0 + s) * p.zcols + r)
+                                   : ((size_t)(p.r0 + r) * p.zcols + s)));
+      const size_t pos = (size_t)r * p.ld + (valid ? s : 0);
+      bool ok = true;
+#pragma unroll 1
+      for (int part = 0; part < 2 && ok; ++part) {
+        if (!mbar_wait(part ? done_b : done_a, it & 1, g, 3)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
         const bool plain = kStrict && part == 1 && p.b_plain;
+        void* ph = part ? p.b_hi : p.a_hi;
+        void* pl = part ? p.b_lo : p.a_lo;
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
-          float pv[32], gv[32];
-          tmem_row32(tmem, warp, part * 256 + cc * 32, pv);
-          tmem_row32(tmem, warp, part * 256 + 128 + cc * 32, gv);
+          uint32_t pr[32], gr[32];
+          const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + part * 256 + cc * 32;
+          tmem_ld32(base, pr);
+          tmem_ld32(base + 128, gr);
+          tmem_ld_wait();
+          if (cc == 3) {
+            // the last TMEM read of this part: the next tile's MMAs may
+            // overwrite these columns while the values below are stored
+            tc_fence_before();
+            mbar_arrive(part ? free_b : free_a);
+          }
+          if (!valid) continue;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float v = sigmoidf_(gv[e]) * pv[e] * m;
-            const int c = cc * 32 + e;
+            const float v = sigmoidf_(__uint_as_float(gr[e])) * __uint_as_float(pr[e]) * m;
+            const size_t idx = (size_t)(cc * 32 + e) * p.cs + pos;
             if constexpr (kStrict) {
               float h, l;
               split_tf32(v, h, l);
-              reinterpret_cast<float*>(A)[c * 128 + t] = plain ? v : h;
-              reinterpret_cast<float*>(A)[128 * 128 + c * 128 + t] = l;
+              static_cast<float*>(ph)[idx] = plain ? v : h;
+              if (!plain) static_cast<float*>(pl)[idx] = l;
             } else {
-              reinterpret_cast<__nv_bfloat16*>(A)[c * 128 + t] = __float2bfloat16_rn(v);
+              static_cast<__nv_bfloat16*>(ph)[idx] = __float2bfloat16_rn(v);
             }
           }
         }
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (t == 0) {
-          tma_store_3d(part ? &st_b_hi : &st_a_hi, A, s0, r, 0);
-          if (kStrict && !plain) tma_store_3d(part ? &st_b_lo : &st_a_lo, A + 65536, s0, r, 0);
-          tma_store_commit();
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 8) {
+    if (lane == 0) {
+      // the same weight sequence for every tile; the ring runs across tiles
+      int seq = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+        for (int q = 0; q < NLOADS; ++q, ++seq) {
+          const int nc = q / C::NKA, ka = q % C::NKA;
+          if (!wring_push<kStrict>(ring, seq, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) {
+            ok = false;
+            break;
+          }
         }
       }
-      if (t == 0) tma_store_wait_all();
-    }
-  } else if (warp == 4) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int q = 0; q < NLOADS; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
-        ++issued;
-      }
-      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+      if (g.aborted()) wring_drain(ring, seq, abort_flag);
     }
   } else {
     if (lane == 0) {
       const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
       const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
-      bool ok = mbar_wait(a_full, 0, g, 4);
-      if (ok) tc_fence_after();
-      for (int q = 0; q < NLOADS && ok; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        const uint32_t w = wring_wait(ring, q, g);
-        if (!w) {
+      bool ok = true;
+      int seq = 0;
+      for (int it = 0, tile = blockIdx.x; tile < p.ntiles && ok; ++it, tile += gridDim.x) {
+        if (!mbar_wait(a_full, it & 1, g, 4)) {
           ok = false;
           break;
         }
-        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
-                            w, w + C::ATOM_BYTES, idesc, ka == 0);
-        wring_release(ring, q);
+        tc_fence_after();
+        // part a (chunks 0, 1: a_p, a_g), then part b (chunks 2, 3), each
+        // once the epilogue has read that part of the previous tile
+        for (int part = 0; part < 2 && ok; ++part) {
+          if (it > 0 && !mbar_wait(part ? free_b : free_a, (it - 1) & 1, g, 6)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int q = part * 2 * C::NKA; q < (part + 1) * 2 * C::NKA; ++q, ++seq) {
+            const int nc = q / C::NKA, ka = q % C::NKA;
+            const uint32_t w = wring_wait(ring, seq, g);
+            if (!w) {
+              ok = false;
+              break;
+            }
+            mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES,
+                                a_lo + ka * C::ATOM_BYTES, w, w + C::ATOM_BYTES, idesc, ka == 0);
+            wring_release(ring, seq);
+          }
+          if (ok) umma_commit(part ? done_b : done_a);
+        }
       }
-      if (ok) {
-        umma_commit(done);
-      } else {
+      if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
       }
@@ -201,7 +244,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -550,40 +593,20 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   if (st) return st;
   CUtensorMap mph, mpl;
   if (!make_weight_maps(wp_hi, wp_lo, 512, strict, &mph, &mpl)) return kErrArg;
-  // output planes [128 channels][plane rows][ld]: one store map per plane
-  const CUtensorMapDataType dt =
-      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const uint64_t esz = strict ? 4 : 2;
   const size_t cs = (size_t)plane_rows * ld;
-  CUtensorMap sah, sal, sbh, sbl;
-  bool ok = make_map_3d(&sah, a_hi, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
-                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
-            make_map_3d(&sbh, b_hi, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
-                        CU_TENSOR_MAP_SWIZZLE_NONE);
   // strict with no b_lo: b is written unsplit into the b_hi planes
   const int b_plain = (strict && b_lo == nullptr) ? 1 : 0;
-  if (strict)
-    ok = ok &&
-         make_map_3d(&sal, a_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1, 128,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) &&
-         (b_plain ? (sbl = sbh, true)
-                  : make_map_3d(&sbl, b_lo, dt, ycols, yrows, 128, ld * esz, cs * esz, 128, 1,
-                                128, CU_TENSOR_MAP_SWIZZLE_NONE));
-  else {
-    sal = sah;
-    sbl = sbh;
-  }
-  if (!ok) return kErrArg;
-  const unsigned tiles = (unsigned)(yrows * ((ycols + 127) / 128));
+  const int tiles = yrows * ((ycols + 127) / 128);
   TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0, eps, ln_w, ln_b, a_hi, a_lo, b_hi,
-                    b_lo, ld, cs, status, b_plain};
+                    b_lo, ld, cs, status, b_plain, tiles};
+  const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
                   : (transposed ? trimul_proj_kernel<false, true>
                                 : trimul_proj_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   FPB_LAUNCH("trimul_proj", stream,
-             k<<<tiles, 192, smem, stream>>>(mph, mpl, sah, sal, sbh, sbl, pa));
+             k<<<grid, 320, smem, stream>>>(mph, mpl, pa));
   return launch_status();
 }
 

@@ -106,6 +106,36 @@ __device__ __forceinline__ void ln_rows_to_a(uint8_t* A, int row0, const Src& sr
   }
 }
 
+// Strict-mode LayerNorm of the kRows rows [row0, row0 + kRows) from raw
+// FP32 rows already in shared memory: the tile's z rows were copied by TMA
+// (128-byte swizzle, one box per 32-channel K atom) into the lo half of A,
+// exactly where lo(row, c) belongs. Lane l reads channels 4l..4l+3 of a row,
+// normalises, and writes hi and lo over the same positions (each lane
+// overwrites only what it read). `per_row(row, y)` as in ln_rows_to_a.
+template <int kRows, class PerRow>
+__device__ __forceinline__ void ln_smem_rows_to_a(uint8_t* A, int row0, float4 lw, float4 lb,
+                                                  float eps, const PerRow& per_row) {
+  using C = RowCfg<true>;
+  constexpr int kBatch = 8;  // rows normalised together (independent reductions)
+  static_assert(kRows % kBatch == 0, "batch must divide the rows");
+  const int lane = threadIdx.x & 31;
+  const int atom = lane / 8, byte = (lane % 8) * 16;
+  const uint8_t* raw = A + C::A_SPLIT_BYTES + atom * C::ATOM_BYTES;
+#pragma unroll 1
+  for (int b0 = 0; b0 < kRows; b0 += kBatch) {
+    float4 x[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      x[u] = *reinterpret_cast<const float4*>(raw + sw128_offset(row0 + b0 + u, byte));
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const float4 y = ln_row_warp(x[u], lw, lb, eps);
+      a_store4<true>(A, row0 + b0 + u, lane * 4, y.x, y.y, y.z, y.w);
+      per_row(row0 + b0 + u, y);
+    }
+  }
+}
+
 struct NoRowHook {
   __device__ __forceinline__ void operator()(int, float4) const {}
 };

@@ -70,26 +70,38 @@ struct AttnProjArgs {
   int* status;
 };
 
+// Weight ring depth of the projection (two 32 KB strict stages beside the
+// 128 KB A tile and the bias tables); the ring runs across the persistent
+// tiles, so the next tile's first weights load during the epilogue.
+constexpr int kAttnProjWStages = 2;
+
 template <bool kStrict>
 constexpr int attn_proj_smem_bytes() {
   using C = RowCfg<kStrict>;
-  return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 2 * 4 * 128 * 4, 512);
+  return tmem_safe_smem(
+      C::A_BYTES + kAttnProjWStages * C::WSTAGE_BYTES + 1024 + 256 + 2 * 4 * 128 * 4, 512);
 }
 
-// Maps of the outputs written by TMA stores from the freed A buffer: q / k
-// [row*4 + h][j][32] (boxes of 128 j x 32, swizzled like the core's loads),
-// v^T [(row*4 + h)*32 + d][key] (boxes of 32 d x 128 keys).
-struct AttnProjStoreMaps {
-  CUtensorMap q_hi, q_lo, k_hi, k_lo, v_hi, v_lo;
-};
-
+// Persistent, warp-specialised: CTA b takes tiles b, b + gridDim.x, ...
+//   LN warps (0-3):       LayerNorm of the tile into A once the previous
+//                         tile's MMAs have read it, the 4-head pair bias on
+//                         the CUDA cores, the pair / mask bias rows;
+//   epilogue warps (4-7): q, k and v^T parts from TMEM to global memory,
+//                         each part released as soon as it is read, so the
+//                         next tile's MMAs of that part overlap the rest;
+//   TMA warp (8):         the weight ring, continuous across tiles;
+//   MMA warp (9):         part q, part k, part v of each tile.
+// Outputs (plain layouts, written by coalesced stores): q / k
+// [row*4 + h][j][32] (one thread = one j: 128 contiguous bytes per head),
+// v^T [(row*4 + h)*32 + d][key] (a warp's stores to one d are 32
+// consecutive keys).
 template <bool kStrict, bool kTrans>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
                      const __grid_constant__ CUtensorMap w_lo,
-                     const __grid_constant__ AttnProjStoreMaps sm, AttnProjArgs p) {
+                     const __grid_constant__ CUtensorMap zmap, AttnProjArgs p) {
   using C = RowCfg<kStrict>;
-  constexpr int WSTAGES = 2;
+  constexpr int WSTAGES = kAttnProjWStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -101,8 +113,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
   uint64_t* a_full = bars + 2 * WSTAGES;
-  uint64_t* done = a_full + 1;
-  uint64_t* drain = done + 1;
+  uint64_t* done = a_full + 1;  // [3]: part q, k, v accumulated
+  uint64_t* freed = done + 3;   // [3]: part read by the epilogue
+  uint64_t* z_full = freed + 3; // strict: raw z rows of the tile in A (TMA)
+  uint64_t* drain = z_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -110,7 +124,7 @@ __global__ void __launch_bounds__(192, 1)
   const int n = p.n;
   // tile = (y row r, 128-column block): a tile never straddles two rows
   const int njb = (n + 127) / 128;
-  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
+  const int ntiles = p.yrows * njb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
@@ -118,13 +132,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&wempty[s], 1);
     }
     mbar_init(a_full, 128);
-    mbar_init(done, 1);
+    for (int q = 0; q < 3; ++q) {
+      mbar_init(&done[q], 1);
+      mbar_init(&freed[q], 128);
+    }
+    mbar_init(z_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) wb[i] = p.w_bias[i];
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -143,152 +161,191 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
     for (int h = 0; h < 4; ++h) wbh[h] = reinterpret_cast<const float4*>(wb + h * 128)[lane];
     const float4* z4 = reinterpret_cast<const float4*>(p.z);
-    auto src = [&](int row) -> const float4* {
-      const int s = s0 + row;
-      if (s >= n) return nullptr;
-      return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
-    };
-    // the 4-head pair bias of each row, on the CUDA cores
-    auto head_bias = [&](int row, float4 y) {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const float b = warp_sum(y.x * wbh[h].x + y.y * wbh[h].y + y.z * wbh[h].z +
-                                 y.w * wbh[h].w);
-        if (lane == h) bias_tile[h * 128 + row] = b;
-      }
-    };
-    ln_rows_to_a<kStrict, 16, true>(A, warp * 32, src, lw, lb, p.eps, head_bias);
-    fence_proxy_async_smem();
-    mbar_arrive(a_full);
-    // named barrier over the 128 row threads: bias_tile complete
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-
     const int t = warp * 32 + lane;
-    const int s = s0 + t;
-    if (s < n) {
+#pragma unroll 1
+    for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      if (it > 0 && !mbar_wait(&done[2], (it - 1) & 1, g, 5)) break;
+      auto src = [&](int row) -> const float4* {
+        const int s = s0 + row;
+        if (s >= n) return nullptr;
+        return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
+      };
+      // the 4-head pair bias of each row, on the CUDA cores
+      auto head_bias = [&](int row, float4 y) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h)
-        p.bias[bias_index(p.r0 + r, h, s, p.ldb)] = bias_tile[h * 128 + t];
-      if (p.mbias) {
-        const float m =
-            __ldg(p.mask + (kTrans ? ((size_t)s * n + r) : ((size_t)(p.r0 + r) * n + s)));
-        p.mbias[(size_t)r * p.ldb + s] = kMaskInf * (m - 1.0f);
+        for (int h = 0; h < 4; ++h) {
+          const float b = warp_sum(y.x * wbh[h].x + y.y * wbh[h].y + y.z * wbh[h].z +
+                                   y.w * wbh[h].w);
+          if (lane == h) bias_tile[h * 128 + row] = b;
+        }
+      };
+      if constexpr (kStrict) {
+        // the tile's raw z rows into the lo half of A by TMA, then
+        // LayerNorm in place
+        if (threadIdx.x == 0) {
+          mbar_arrive_expect_tx(z_full, C::A_SPLIT_BYTES);
+#pragma unroll
+          for (int a = 0; a < C::NKA; ++a)
+            tma_load_3d(A + C::A_SPLIT_BYTES + a * C::ATOM_BYTES, &zmap, z_full, a * C::KATOM,
+                        kTrans ? r : s0, kTrans ? s0 : r);
+        }
+        if (!mbar_wait(z_full, it & 1, g, 7)) break;
+        ln_smem_rows_to_a<32>(A, warp * 32, lw, lb, p.eps, head_bias);
+      } else {
+        ln_rows_to_a<kStrict, 8, true>(A, warp * 32, src, lw, lb, p.eps, head_bias);
       }
+      fence_proxy_async_smem();
+      mbar_arrive(a_full);
+      __syncwarp();  // this warp's rows of bias_tile are complete
+      const int s = s0 + t;
+      if (s < n) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          p.bias[bias_index(p.r0 + r, h, s, p.ldb)] = bias_tile[h * 128 + t];
+        if (p.mbias) {
+          const float m =
+              __ldg(p.mask + (kTrans ? ((size_t)s * n + r) : ((size_t)(p.r0 + r) * n + s)));
+          p.mbias[(size_t)r * p.ldb + s] = kMaskInf * (m - 1.0f);
+        }
+      }
+      __syncwarp();  // bias_tile is rewritten by the next tile's LayerNorm
     }
-    // q, k, v^T of the tile, one part at a time, staged in the freed A buffer
-    // (per head: 16 KB fp32 / 8 KB bf16; strict lo planes 64 KB further)
-    // and written by TMA stores; rows / keys past n are clipped.
-    constexpr int HS = kStrict ? 16384 : 8192;
-    if (mbar_wait(done, 0, g, 3)) {
-      tc_fence_after();
+  } else if (warp < 8) {
+    const int quad = warp & 3;
+    const int t = quad * 32 + lane;
+    const size_t ldv = (size_t)p.ldv;
+#pragma unroll 1
+    for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      const int j = s0 + t;
+      const bool valid = j < n;
+      bool ok = true;
 #pragma unroll 1
       for (int part = 0; part < 3; ++part) {
-        if (part > 0) {
-          if (t == 0) tma_store_wait_read();
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!mbar_wait(&done[part], it & 1, g, 3)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        // two heads per TMEM round trip; the part is released after the last
 #pragma unroll 1
-        for (int h = 0; h < 4; ++h) {
-          float v[32];
-          tmem_row32(tmem, warp, part * 128 + h * 32, v);
-          uint8_t* sh = A + h * HS;
-          if (part < 2) {
-            // [128 rows j][32] in the swizzled layout of the store map
-            const float sc = part == 0 ? p.q_scale : 1.0f;
-            if constexpr (kStrict) {
+        for (int hp = 0; hp < 2; ++hp) {
+          uint32_t vr[2][32];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                float h0, l0, h1, l1, h2, l2, h3, l3;
-                split_tf32(v[4 * e] * sc, h0, l0);
-                split_tf32(v[4 * e + 1] * sc, h1, l1);
-                split_tf32(v[4 * e + 2] * sc, h2, l2);
-                split_tf32(v[4 * e + 3] * sc, h3, l3);
-                const uint32_t off = sw128_offset(t, e * 16);
-                *reinterpret_cast<float4*>(sh + off) = make_float4(h0, h1, h2, h3);
-                *reinterpret_cast<float4*>(sh + 65536 + off) = make_float4(l0, l1, l2, l3);
-              }
-            } else {
+          for (int u = 0; u < 2; ++u)
+            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + part * 128 + (2 * hp + u) * 32,
+                      vr[u]);
+          tmem_ld_wait();
+          if (hp == 1) {
+            tc_fence_before();
+            mbar_arrive(&freed[part]);  // the next tile's MMAs may reuse these columns
+          }
+          if (!valid) continue;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                uint32_t w4[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * e + 2 * u] * sc,
-                                                            v[8 * e + 2 * u + 1] * sc);
-                  w4[u] = *reinterpret_cast<uint32_t*>(&b2);
-                }
-                *reinterpret_cast<uint4*>(sh + sw64_offset(t, e * 16)) =
-                    make_uint4(w4[0], w4[1], w4[2], w4[3]);
-              }
-            }
-          } else {
-            // v^T: [32 d][128 keys]
-#pragma unroll
-            for (int d = 0; d < 32; ++d) {
+          for (int u = 0; u < 2; ++u) {
+            const size_t ih = (size_t)r * kHeads + 2 * hp + u;
+            if (part < 2) {
+              const float sc = part == 0 ? p.q_scale : 1.0f;
+              void* dh = part == 0 ? p.q_hi : p.k_hi;
+              void* dl = part == 0 ? p.q_lo : p.k_lo;
+              const size_t row = (ih * n + j) * 32;
               if constexpr (kStrict) {
-                float hh, ll;
-                split_tf32(v[d], hh, ll);
-                reinterpret_cast<float*>(sh)[d * 128 + t] = hh;
-                reinterpret_cast<float*>(sh + 65536)[d * 128 + t] = ll;
+                float4* oh = reinterpret_cast<float4*>(static_cast<float*>(dh) + row);
+                float4* ol = reinterpret_cast<float4*>(static_cast<float*>(dl) + row);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  float h0, l0, h1, l1, h2, l2, h3, l3;
+                  split_tf32(__uint_as_float(vr[u][4 * e]) * sc, h0, l0);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 1]) * sc, h1, l1);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 2]) * sc, h2, l2);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 3]) * sc, h3, l3);
+                  oh[e] = make_float4(h0, h1, h2, h3);
+                  ol[e] = make_float4(l0, l1, l2, l3);
+                }
               } else {
-                reinterpret_cast<__nv_bfloat16*>(sh)[d * 128 + t] = __float2bfloat16_rn(v[d]);
+                uint4* oh = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dh) + row);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  uint32_t w4[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    __nv_bfloat162 b2 =
+                        __floats2bfloat162_rn(__uint_as_float(vr[u][8 * e + 2 * q]) * sc,
+                                              __uint_as_float(vr[u][8 * e + 2 * q + 1]) * sc);
+                    w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+                  }
+                  oh[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+              }
+            } else {
+              // v^T: [ih * 32 + d][key j]
+#pragma unroll
+              for (int d = 0; d < 32; ++d) {
+                const size_t idx = (ih * 32 + d) * ldv + j;
+                if constexpr (kStrict) {
+                  float hh, ll;
+                  split_tf32(__uint_as_float(vr[u][d]), hh, ll);
+                  static_cast<float*>(p.v_hi)[idx] = hh;
+                  static_cast<float*>(p.v_lo)[idx] = ll;
+                } else {
+                  static_cast<__nv_bfloat16*>(p.v_hi)[idx] =
+                      __float2bfloat16_rn(__uint_as_float(vr[u][d]));
+                }
               }
             }
           }
         }
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (t == 0) {
-#pragma unroll 1
-          for (int h = 0; h < 4; ++h) {
-            const int ih = r * kHeads + h;
-            uint8_t* sh = A + h * HS;
-            if (part == 0) {
-              tma_store_3d(&sm.q_hi, sh, 0, s0, ih);
-              if constexpr (kStrict) tma_store_3d(&sm.q_lo, sh + 65536, 0, s0, ih);
-            } else if (part == 1) {
-              tma_store_3d(&sm.k_hi, sh, 0, s0, ih);
-              if constexpr (kStrict) tma_store_3d(&sm.k_lo, sh + 65536, 0, s0, ih);
-            } else {
-              tma_store_3d(&sm.v_hi, sh, s0, ih * 32, 0);
-              if constexpr (kStrict) tma_store_3d(&sm.v_lo, sh + 65536, s0, ih * 32, 0);
-            }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 8) {
+    if (lane == 0) {
+      int seq = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int q = 0; q < NLOADS; ++q, ++seq) {
+          const int nc = q / C::NKA, ka = q % C::NKA;
+          if (!wring_push<kStrict>(ring, seq, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) {
+            ok = false;
+            break;
           }
-          tma_store_commit();
         }
       }
-      if (t == 0) tma_store_wait_all();
-    }
-  } else if (warp == 4) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int q = 0; q < NLOADS; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
-        ++issued;
-      }
-      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+      if (g.aborted()) wring_drain(ring, seq, abort_flag);
     }
   } else {
     if (lane == 0) {
       const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
       const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
-      bool ok = mbar_wait(a_full, 0, g, 4);
-      if (ok) tc_fence_after();
-      for (int q = 0; q < NLOADS && ok; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        const uint32_t w = wring_wait(ring, q, g);
-        if (!w) {
+      bool ok = true;
+      int seq = 0;
+      for (int it = 0, tile = blockIdx.x; tile < ntiles && ok; ++it, tile += gridDim.x) {
+        if (!mbar_wait(a_full, it & 1, g, 4)) {
           ok = false;
           break;
         }
-        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
-                            w, w + C::ATOM_BYTES, idesc, ka == 0);
-        wring_release(ring, q);
+        tc_fence_after();
+        for (int nc = 0; nc < 3 && ok; ++nc) {
+          if (it > 0 && !mbar_wait(&freed[nc], (it - 1) & 1, g, 6)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int ka = 0; ka < C::NKA; ++ka, ++seq) {
+            const uint32_t w = wring_wait(ring, seq, g);
+            if (!w) {
+              ok = false;
+              break;
+            }
+            mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES,
+                                a_lo + ka * C::ATOM_BYTES, w, w + C::ATOM_BYTES, idesc, ka == 0);
+            wring_release(ring, seq);
+          }
+          if (ok) umma_commit(&done[nc]);
+        }
       }
-      if (ok) {
-        umma_commit(done);
-      } else {
+      if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
       }
@@ -297,7 +354,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1179,29 +1236,19 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
     return st;
   CUtensorMap mph, mpl;
   if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl)) return kErrArg;
-  const int esz = strict ? 4 : 2;
-  const CUtensorMapDataType dt =
-      strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const CUtensorMapSwizzle qsw = strict ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  const uint64_t rowb = 32ull * esz, nh = (uint64_t)rows * kHeads;
-  const uint64_t vrow = (uint64_t)pl.ldv * esz;
-  AttnProjStoreMaps sm{};
-  bool ok = make_map_3d(&sm.q_hi, pl.q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-            make_map_3d(&sm.k_hi, pl.k_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-            make_map_3d(&sm.v_hi, pl.v_hi, dt, n, nh * 32, 1, vrow, vrow * nh * 32, 128, 32, 1,
-                        CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (strict)
-    ok = ok && make_map_3d(&sm.q_lo, pl.q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-         make_map_3d(&sm.k_lo, pl.k_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
-         make_map_3d(&sm.v_lo, pl.v_lo, dt, n, nh * 32, 1, vrow, vrow * nh * 32, 128, 32, 1,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
-  else {
-    sm.q_lo = sm.q_hi;
-    sm.k_lo = sm.k_hi;
-    sm.v_lo = sm.v_hi;
+  // raw z rows of a tile (strict): [128 rows][32 channels] boxes, rows past
+  // n zero-filled; transposed: tile rows are rows of z at column r
+  CUtensorMap zm{};
+  if (strict) {
+    const uint64_t rowb = 128ull * 4, pitch = (uint64_t)n * rowb;
+    const bool zok = trans ? make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, rows,
+                                         n, rowb, pitch, 32, 1, 128)
+                           : make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, n,
+                                         rows, rowb, pitch, 32, 128, 1);
+    if (!zok) return kErrArg;
   }
-  if (!ok) return kErrArg;
-  const unsigned tiles = (unsigned)(rows * ((n + 127) / 128));
+  const int tiles = rows * ((n + 127) / 128);
+  const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   AttnProjArgs pa{z_loc, mask, n, rows, r0, eps, ln_w, ln_b, w_bias,
                   1.0f / sqrtf((float)kHeadDim), pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi,
                   pl.v_lo, pl.ldv, bias, pl.ldb, pl.mbias, status};
@@ -1209,7 +1256,7 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
   auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
                   : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  FPB_LAUNCH("triattn_proj", stream, k<<<tiles, 192, smem, stream>>>(mph, mpl, sm, pa));
+  FPB_LAUNCH("triattn_proj", stream, k<<<grid, 320, smem, stream>>>(mph, mpl, zm, pa));
   return launch_status();
 }
 

@@ -57,7 +57,8 @@ constexpr int proj_smem_bytes() {
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(320, 1)
     trimul_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
-                       const __grid_constant__ CUtensorMap w_lo, TriMulProjArgs p) {
+                       const __grid_constant__ CUtensorMap w_lo,
+                       const __grid_constant__ CUtensorMap zmap, TriMulProjArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = kProjWStages;
   extern __shared__ uint8_t smem_raw[];
@@ -73,7 +74,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* done_b = done_a + 1;          // part b ready; every MMA of the tile read A
   uint64_t* free_a = done_b + 1;          // part a accumulators read (epilogue warps)
   uint64_t* free_b = free_a + 1;          // part b accumulators read
-  uint64_t* drain = free_b + 1;
+  uint64_t* z_full = free_b + 1;          // strict: raw z rows of the tile in A (TMA)
+  uint64_t* drain = z_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -92,6 +94,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(done_b, 1);
     mbar_init(free_a, 128);
     mbar_init(free_b, 128);
+    mbar_init(z_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -118,12 +121,27 @@ __global__ void __launch_bounds__(320, 1)
     for (int it = 0, tile = blockIdx.x; tile < p.ntiles; ++it, tile += gridDim.x) {
       const int r = tile / njb, s0 = (tile % njb) * 128;
       if (it > 0 && !mbar_wait(done_b, (it - 1) & 1, g, 5)) break;
-      auto src = [&](int row) -> const float4* {
-        const int sc = s0 + row;
-        if (sc >= p.ycols) return nullptr;
-        return z4 + (kTrans ? ((long long)sc * p.zcols + r) : ((long long)r * p.zcols + sc)) * 32;
-      };
-      ln_rows_to_a<kStrict, 16, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
+      if constexpr (kStrict) {
+        // the tile's raw z rows into the lo half of A by TMA (one 64 KB
+        // transfer instead of per-warp row loads), then LayerNorm in place
+        if (threadIdx.x == 0) {
+          mbar_arrive_expect_tx(z_full, C::A_SPLIT_BYTES);
+#pragma unroll
+          for (int a = 0; a < C::NKA; ++a)
+            tma_load_3d(A + C::A_SPLIT_BYTES + a * C::ATOM_BYTES, &zmap, z_full, a * C::KATOM,
+                        kTrans ? r : s0, kTrans ? s0 : r);
+        }
+        if (!mbar_wait(z_full, it & 1, g, 7)) break;
+        ln_smem_rows_to_a<32>(A, warp * 32, lw, lb, p.eps, NoRowHook{});
+      } else {
+        auto src = [&](int row) -> const float4* {
+          const int sc = s0 + row;
+          if (sc >= p.ycols) return nullptr;
+          return z4 +
+                 (kTrans ? ((long long)sc * p.zcols + r) : ((long long)r * p.zcols + sc)) * 32;
+        };
+        ln_rows_to_a<kStrict, 16, true>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
+      }
       fence_proxy_async_smem();
       mbar_arrive(a_full);
     }
@@ -593,6 +611,19 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   if (st) return st;
   CUtensorMap mph, mpl;
   if (!make_weight_maps(wp_hi, wp_lo, 512, strict, &mph, &mpl)) return kErrArg;
+  // raw z rows of a tile (strict): [128 rows][32 channels] boxes, rows past
+  // ycols zero-filled; transposed: tile rows are rows of z at column r
+  CUtensorMap zm{};
+  if (strict) {
+    const uint64_t rowb = 128ull * 4, pitch = (uint64_t)zcols * rowb;
+    const bool zok =
+        transposed
+            ? make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, yrows, ycols, rowb,
+                          pitch, 32, 1, 128)
+            : make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, ycols, yrows, rowb,
+                          pitch, 32, 128, 1);
+    if (!zok) return kErrArg;
+  }
   const size_t cs = (size_t)plane_rows * ld;
   // strict with no b_lo: b is written unsplit into the b_hi planes
   const int b_plain = (strict && b_lo == nullptr) ? 1 : 0;
@@ -606,7 +637,7 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
                                 : trimul_proj_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   FPB_LAUNCH("trimul_proj", stream,
-             k<<<grid, 320, smem, stream>>>(mph, mpl, pa));
+             k<<<grid, 320, smem, stream>>>(mph, mpl, zm, pa));
   return launch_status();
 }
 

@@ -941,14 +941,27 @@ constexpr int attn_out_smem_bytes() {
   return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
 }
 
-// out_map: z (or delta) viewed as [a][b][128 channels] with z row a*n + b;
-// the tile's 128 rows are b = s0.. (box {32, 128, 1}) or, transposed,
-// a = s0.. (box {32, 1, 128}); rows past n are clipped by the store.
+// Gate, output projection and residual over tiles of 128 pair rows of y
+// (y row r, columns s0..), persistent and warp-specialised:
+//   A warps (0-3):        strict: the tile's z rows by TMA into A, LayerNorm
+//                         in place (fast: LayerNorm from global rows); after
+//                         GEMM 1: A = sigmoid(gate + b_g) * o (o from
+//                         global, one 32-channel chunk ahead);
+//   epilogue warps (4-7): y = GEMM 2 + b_o from TMEM, released to the next
+//                         GEMM 2 after its last read, residual added, rows
+//                         stored to z (or delta) while the next tile runs;
+//   TMA warp (8):         the weight ring [W_g; W_o], continuous across tiles;
+//   MMA warp (9):         GEMM 1 (gate) into TMEM columns [0, 128), GEMM 2
+//                         into [128, 256) once the epilogue has read the
+//                         previous y (which keeps every barrier in lockstep:
+//                         none can complete two phases ahead of a waiter).
+// z rows read and written by a tile are its own (row r * n + s, or s * n + r
+// transposed), so tiles in flight never touch each other's rows.
 template <bool kStrict, bool kTrans>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_out_kernel(const __grid_constant__ CUtensorMap w_hi,
                     const __grid_constant__ CUtensorMap w_lo,
-                    const __grid_constant__ CUtensorMap out_map, AttnOutArgs p) {
+                    const __grid_constant__ CUtensorMap zmap, AttnOutArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = 2;
   extern __shared__ uint8_t smem_raw[];
@@ -960,27 +973,32 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(bvec + 256);
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
-  uint64_t* a_full = bars + 2 * WSTAGES;
-  uint64_t* g_done = a_full + 1;
-  uint64_t* done = g_done + 1;
-  uint64_t* drain = done + 1;
+  uint64_t* a1_full = bars + 2 * WSTAGES;  // LN(z) in A
+  uint64_t* g1_done = a1_full + 1;         // gate in TMEM, A free for gate * o
+  uint64_t* a2_full = g1_done + 1;         // gate * o in A
+  uint64_t* g2_done = a2_full + 1;         // y in TMEM, A free for the next tile
+  uint64_t* y_free = g2_done + 1;          // y read by the epilogue
+  uint64_t* z_full = y_free + 1;           // strict: raw z rows in A (TMA)
+  uint64_t* drain = z_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = p.n;
-  // tile = (y row r, 128-column block): a tile never straddles two rows
   const int njb = (n + 127) / 128;
-  const int r = blockIdx.x / njb, s0 = (blockIdx.x % njb) * 128;
+  const int ntiles = p.rows * njb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&wempty[s], 1);
     }
-    mbar_init(a_full, 128);
-    mbar_init(g_done, 1);
-    mbar_init(done, 1);
+    mbar_init(a1_full, 128);
+    mbar_init(g1_done, 1);
+    mbar_init(a2_full, 128);
+    mbar_init(g2_done, 1);
+    mbar_init(y_free, 128);
+    mbar_init(z_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -989,7 +1007,7 @@ __global__ void __launch_bounds__(192, 1)
     bvec[threadIdx.x] = p.b_g ? p.b_g[threadIdx.x] : 0.f;
     bvec[128 + threadIdx.x] = p.b_o ? p.b_o[threadIdx.x] : 0.f;
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
@@ -1002,62 +1020,76 @@ __global__ void __launch_bounds__(192, 1)
   constexpr int NLOADS = 2 * C::NKA;
 
   if (warp < 4) {
-    {
-      const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
-      const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
-      const float4* z4 = reinterpret_cast<const float4*>(p.z);
-      auto src = [&](int row) -> const float4* {
-        const int s = s0 + row;
-        if (s >= n) return nullptr;
-        return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
-      };
-      ln_rows_to_a<kStrict, 32, false>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
-      fence_proxy_async_smem();
-      mbar_arrive(a_full);
-    }
+    // ---------------------------------------------------------------- A warps
+    const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
+    const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
+    const float4* z4 = reinterpret_cast<const float4*>(p.z);
     const int t = warp * 32 + lane;
-    const bool valid = s0 + t < n;
-    const long long pr = (long long)r * n + (valid ? s0 + t : 0);  // y pair (o row)
-    const long long zrow_idx = kTrans ? (long long)(valid ? s0 + t : 0) * n + r : pr;
-    // attention output chunk cc (32 channels) of this thread's row
-    auto load_o = [&](int cc, float (&ov)[32]) {
-      if (!valid) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = 0.f;
-        return;
-      }
+#pragma unroll 1
+    for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      // A is free once GEMM 2 of the previous tile has read it
+      if (it > 0 && !mbar_wait(g2_done, (it - 1) & 1, g, 5)) break;
       if constexpr (kStrict) {
-        const float4* src =
-            reinterpret_cast<const float4*>(static_cast<const float*>(p.o) + pr * 128 + cc * 32);
+        if (threadIdx.x == 0) {
+          mbar_arrive_expect_tx(z_full, C::A_SPLIT_BYTES);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 v = __ldg(src + e);
-          ov[4 * e] = v.x;
-          ov[4 * e + 1] = v.y;
-          ov[4 * e + 2] = v.z;
-          ov[4 * e + 3] = v.w;
+          for (int a = 0; a < C::NKA; ++a)
+            tma_load_3d(A + C::A_SPLIT_BYTES + a * C::ATOM_BYTES, &zmap, z_full, a * C::KATOM,
+                        kTrans ? r : s0, kTrans ? s0 : r);
         }
+        if (!mbar_wait(z_full, it & 1, g, 7)) break;
+        ln_smem_rows_to_a<32>(A, warp * 32, lw, lb, p.eps, NoRowHook{});
       } else {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.o) +
-                                                          pr * 128 + cc * 32);
+        auto src = [&](int row) -> const float4* {
+          const int s = s0 + row;
+          if (s >= n) return nullptr;
+          return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
+        };
+        ln_rows_to_a<kStrict, 16, false>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(a1_full);
+
+      // gate * o of this thread's row into A once GEMM 1 is done
+      const bool valid = s0 + t < n;
+      const long long pr = (long long)r * n + (valid ? s0 + t : 0);  // y pair (o row)
+      auto load_o = [&](int cc, float (&ov)[32]) {
+        if (!valid) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint4 v = __ldg(src + e);
-          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+          return;
+        }
+        if constexpr (kStrict) {
+          const float4* src =
+              reinterpret_cast<const float4*>(static_cast<const float*>(p.o) + pr * 128 + cc * 32);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-            ov[8 * e + 2 * u] = __bfloat162float(b2.x);
-            ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
+          for (int e = 0; e < 8; ++e) {
+            const float4 v = __ldg(src + e);
+            ov[4 * e] = v.x;
+            ov[4 * e + 1] = v.y;
+            ov[4 * e + 2] = v.z;
+            ov[4 * e + 3] = v.w;
+          }
+        } else {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              static_cast<const __nv_bfloat16*>(p.o) + pr * 128 + cc * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint4 v = __ldg(src + e);
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+              ov[8 * e + 2 * u] = __bfloat162float(b2.x);
+              ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
+            }
           }
         }
-      }
-    };
-    // gate from GEMM 1, times o -> A2 (after GEMM 1 retired); o chunks are
-    // loaded one step ahead, the first one while GEMM 1 is still running
-    float ocur[32];
-    load_o(0, ocur);
-    if (mbar_wait(g_done, 0, g, 5)) {
+      };
+      float ocur[32];
+      load_o(0, ocur);
+      if (!mbar_wait(g1_done, it & 1, g, 8)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
@@ -1078,24 +1110,30 @@ __global__ void __launch_bounds__(192, 1)
           for (int e = 0; e < 32; ++e) ocur[e] = onext[e];
         }
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(a2_full);
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    mbar_arrive(a_full);
-    // residual: z chunks loaded one step ahead, the first before GEMM 2 ends
-    // (delta mode: the update is written to p.delta and z is not read)
+  } else if (warp < 8) {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int t = quad * 32 + lane;
     const bool residual = p.delta == nullptr;
-    float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
-    float4* drow = residual ? zrow : reinterpret_cast<float4*>(p.delta) + zrow_idx * 32;
-    float4 zc[8];
+#pragma unroll 1
+    for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
+      const int r = tile / njb, s0 = (tile % njb) * 128;
+      const bool valid = s0 + t < n;
+      const long long zrow_idx =
+          kTrans ? (long long)(valid ? s0 + t : 0) * n + r : (long long)r * n + (valid ? s0 + t : 0);
+      float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
+      float4* drow = residual ? zrow : reinterpret_cast<float4*>(p.delta) + zrow_idx * 32;
+      float4 zc[8];
 #pragma unroll
-    for (int v4 = 0; v4 < 8; ++v4)
-      zc[v4] = (valid && residual) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
-    if (mbar_wait(done, 0, g, 3)) {
+      for (int v4 = 0; v4 < 8; ++v4)
+        zc[v4] = (valid && residual) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!mbar_wait(g2_done, it & 1, g, 3)) break;
       tc_fence_after();
-      // the finished rows are staged in the freed A buffer (and, in fast
-      // mode, the weight ring right behind it) as 4 boxes [128 rows][32
-      // channels] in the 128-byte swizzled layout, then written by TMA stores
+      const uint32_t ycol = 128;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         float4 zn[8];
@@ -1103,73 +1141,77 @@ __global__ void __launch_bounds__(192, 1)
         for (int v4 = 0; v4 < 8; ++v4)
           zn[v4] = (cc < 3 && valid && residual) ? zrow[(cc + 1) * 8 + v4]
                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-        float yv[32];
-        tmem_row32(tmem, warp, 128 + cc * 32, yv);
-        uint8_t* box = A + cc * 16384;
+        uint32_t yr[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + ycol + cc * 32, yr);
+        tmem_ld_wait();
+        if (cc == 3) {
+          tc_fence_before();
+          mbar_arrive(y_free);  // GEMM 2 of the next tile may overwrite y
+        }
+        if (valid) {
 #pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4) {
-          float4 o = zc[v4];
-          const int c = cc * 32 + 4 * v4;
-          o.x += yv[4 * v4] + bvec[128 + c];
-          o.y += yv[4 * v4 + 1] + bvec[129 + c];
-          o.z += yv[4 * v4 + 2] + bvec[130 + c];
-          o.w += yv[4 * v4 + 3] + bvec[131 + c];
-          *reinterpret_cast<float4*>(box + sw128_offset(t, v4 * 16)) = o;
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 o = zc[v4];
+            const int c = cc * 32 + 4 * v4;
+            o.x += __uint_as_float(yr[4 * v4]) + bvec[128 + c];
+            o.y += __uint_as_float(yr[4 * v4 + 1]) + bvec[129 + c];
+            o.z += __uint_as_float(yr[4 * v4 + 2]) + bvec[130 + c];
+            o.w += __uint_as_float(yr[4 * v4 + 3]) + bvec[131 + c];
+            drow[cc * 8 + v4] = o;
+          }
         }
 #pragma unroll
         for (int v4 = 0; v4 < 8; ++v4) zc[v4] = zn[v4];
       }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) {
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          if constexpr (kTrans)
-            tma_store_3d(&out_map, A + cc * 16384, cc * 32, r, s0);
-          else
-            tma_store_3d(&out_map, A + cc * 16384, cc * 32, s0, r);
-        }
-        tma_store_commit();
-        tma_store_wait_all();
-      }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     if (lane == 0) {
-      int issued = 0;
-      for (int q = 0; q < NLOADS; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (!wring_push<kStrict>(ring, q, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) break;
-        ++issued;
+      int seq = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int q = 0; q < NLOADS; ++q, ++seq) {
+          const int nc = q / C::NKA, ka = q % C::NKA;
+          if (!wring_push<kStrict>(ring, seq, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) {
+            ok = false;
+            break;
+          }
+        }
       }
-      if (g.aborted()) wring_drain(ring, issued, abort_flag);
+      if (g.aborted()) wring_drain(ring, seq, abort_flag);
     }
   } else {
     if (lane == 0) {
       const uint32_t idesc = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
       const uint32_t a_hi = smem_u32(A), a_lo = smem_u32(A + C::A_SPLIT_BYTES);
       bool ok = true;
-      for (int q = 0; q < NLOADS && ok; ++q) {
-        const int nc = q / C::NKA, ka = q % C::NKA;
-        if (ka == 0) {
-          if (nc == 1) umma_commit(g_done);
-          if (!mbar_wait(a_full, nc & 1, g, 4)) {
+      int seq = 0;
+      for (int it = 0, tile = blockIdx.x; tile < ntiles && ok; ++it, tile += gridDim.x) {
+        for (int gemm = 0; gemm < 2 && ok; ++gemm) {
+          if (!mbar_wait(gemm ? a2_full : a1_full, it & 1, g, 4)) {
+            ok = false;
+            break;
+          }
+          // GEMM 2 overwrites y once the epilogue has read the previous one
+          if (gemm == 1 && it >= 1 && !mbar_wait(y_free, (it - 1) & 1, g, 6)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t d = tmem + (gemm ? 128 : 0);
+          for (int ka = 0; ka < C::NKA; ++ka, ++seq) {
+            const uint32_t w = wring_wait(ring, seq, g);
+            if (!w) {
+              ok = false;
+              break;
+            }
+            mma_k_atom<kStrict>(d, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES, w,
+                                w + C::ATOM_BYTES, idesc, ka == 0);
+            wring_release(ring, seq);
+          }
+          if (ok) umma_commit(gemm ? g2_done : g1_done);
         }
-        const uint32_t w = wring_wait(ring, q, g);
-        if (!w) {
-          ok = false;
-          break;
-        }
-        mma_k_atom<kStrict>(tmem + nc * 128, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES,
-                            w, w + C::ATOM_BYTES, idesc, ka == 0);
-        wring_release(ring, q);
       }
-      if (ok) {
-        umma_commit(done);
-      } else {
+      if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
       }
@@ -1178,7 +1220,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
@@ -1280,21 +1322,24 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
       return st;
   }
   AttnOutArgs oa{z_loc, delta_out, n, rows, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
-  // store map over the written tensor (z, or delta_out) as [a][b][128]
-  CUtensorMap om;
-  {
-    const uint64_t arows = trans ? (uint64_t)n : (uint64_t)rows;
-    float* dst = delta_out ? delta_out : z_loc;
-    if (!make_map_3d(&om, dst, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, n, arows, 512,
-                     512ull * n, 32, trans ? 1 : 128, trans ? 128 : 1))
-      return kErrArg;
+  // raw z rows of a tile (strict LayerNorm by TMA): y row r = z row r, or
+  // z column r when transposed; rows past n zero-filled
+  CUtensorMap zm{};
+  if (strict) {
+    const uint64_t rowb = 128ull * 4, pitch = (uint64_t)n * rowb;
+    const bool zok = trans ? make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, rows,
+                                         n, rowb, pitch, 32, 1, 128)
+                           : make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, n,
+                                         rows, rowb, pitch, 32, 128, 1);
+    if (!zok) return kErrArg;
   }
-  const unsigned tiles = (unsigned)(rows * ((n + 127) / 128));
+  const int tiles = rows * ((n + 127) / 128);
+  const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
   auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
                   : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  FPB_LAUNCH("triattn_out", stream, k<<<tiles, 192, smem, stream>>>(moh, mol, om, oa));
+  FPB_LAUNCH("triattn_out", stream, k<<<grid, 320, smem, stream>>>(moh, mol, zm, oa));
   return launch_status();
 }
 

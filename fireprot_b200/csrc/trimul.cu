@@ -41,6 +41,7 @@ struct TriMulProjArgs {
   int* status;
   int b_plain;  // strict: write b unsplit (FP32) into the b_hi planes
   int ntiles;   // yrows x ceil(ycols / 128) tiles, walked by a persistent grid
+  int a_plain;  // strict: write a unsplit (FP32) into the a_hi planes
 };
 
 // Weight ring depth of the projection kernel: three 32 KB strict stages
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        const bool plain = kStrict && part == 1 && p.b_plain;
+        const bool plain = kStrict && (part ? p.b_plain : p.a_plain);
         void* ph = part ? p.b_hi : p.a_hi;
         void* pl = part ? p.b_lo : p.a_lo;
 #pragma unroll 1
@@ -625,11 +626,12 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
     if (!zok) return kErrArg;
   }
   const size_t cs = (size_t)plane_rows * ld;
-  // strict with no b_lo: b is written unsplit into the b_hi planes
+  // strict with no a_lo / b_lo: a / b written unsplit into the hi planes
+  const int a_plain = (strict && a_lo == nullptr) ? 1 : 0;
   const int b_plain = (strict && b_lo == nullptr) ? 1 : 0;
   const int tiles = yrows * ((ycols + 127) / 128);
-  TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0, eps, ln_w, ln_b, a_hi, a_lo, b_hi,
-                    b_lo, ld, cs, status, b_plain, tiles};
+  TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0,   eps,    ln_w,  ln_b,   a_hi,
+                    a_lo,  b_hi, b_lo,  ld,    cs,    status, b_plain, tiles, a_plain};
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
@@ -665,16 +667,17 @@ int trimul_finish_run(float* z_loc, int n, int rows, const void* x_blocked, cons
 int trimul_contract_run(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
                         const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
                         int b_chunks, size_t b_chunk_stride, int k, int ld, void* x_blocked,
-                        bool strict, int* status, cudaStream_t stream) {
+                        bool strict, int* status, cudaStream_t stream, int channels = 128) {
   ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, (size_t)a_plane_rows * ld,
                       (size_t)b_chunk_rows * ld,
-                      m, nn, k, b_chunk_rows, b_chunks, b_chunk_stride, 128, strict};
+                      m, nn, k, b_chunk_rows, b_chunks, b_chunk_stride, channels, strict};
   ContractArgs ca{};
   ca.out = x_blocked;
   ca.out_bf16 = strict ? 0 : 1;
   ca.status = status;
   ca.blocked = 1;
   ca.njb = (nn + 127) / 128;
+  ca.bchannels = channels;
   return launch_contract(op, ca, stream);
 }
 
@@ -784,7 +787,7 @@ extern "C" int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int 
     return kErrArg;
   if (precision != 0 && precision != 1) return kErrArg;
   const bool strict = precision == 0;
-  if (strict && !a_lo) return kErrArg;  // b_lo null: b unsplit (FP32)
+  // strict: a_lo / b_lo null writes a / b unsplit (FP32) into the hi planes
   if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
   const int yrows = transposed ? n : rows;
   const int ycols = transposed ? rows : n;
@@ -803,24 +806,35 @@ extern "C" int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int 
                          strict, wh, wl, static_cast<int*>(workspace), stream);
 }
 
+extern "C" int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m,
+                                         int a_plane_rows, const void* b_hi, const void* b_lo,
+                                         int nn, int b_chunk_rows, int b_chunks,
+                                         size_t b_chunk_stride, int k, int ld, int channels,
+                                         void* x_blocked, int precision, void* workspace,
+                                         size_t workspace_bytes, cudaStream_t stream) {
+  if (!a_hi || !b_hi || !x_blocked || !workspace) return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (strict && (!a_lo || !b_lo)) return kErrArg;
+  if (m <= 0 || nn <= 0 || k <= 0 || b_chunk_rows <= 0 || b_chunks <= 0 || a_plane_rows < m ||
+      (long long)b_chunk_rows * b_chunks < nn || channels <= 0 || channels > 128)
+    return kErrShape;
+  if (workspace_bytes < kWsHeader || !aligned16(workspace)) return kErrWorkspace;
+  if (reset_status(workspace, stream)) return kErrCuda;
+  return trimul_contract_run(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows, b_chunks,
+                             b_chunk_stride, k, ld, x_blocked, strict,
+                             static_cast<int*>(workspace), stream, channels);
+}
+
 extern "C" int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m,
                                          int a_plane_rows, const void* b_hi, const void* b_lo,
                                          int nn, int b_chunk_rows, int b_chunks,
                                          size_t b_chunk_stride, int k, int ld, void* x_blocked,
                                          int precision, void* workspace, size_t workspace_bytes,
                                          cudaStream_t stream) {
-  if (!a_hi || !b_hi || !x_blocked || !workspace) return kErrArg;
-  if (precision != 0 && precision != 1) return kErrArg;
-  const bool strict = precision == 0;
-  if (strict && (!a_lo || !b_lo)) return kErrArg;
-  if (m <= 0 || nn <= 0 || k <= 0 || b_chunk_rows <= 0 || b_chunks <= 0 || a_plane_rows < m ||
-      (long long)b_chunk_rows * b_chunks < nn)
-    return kErrShape;
-  if (workspace_bytes < kWsHeader || !aligned16(workspace)) return kErrWorkspace;
-  if (reset_status(workspace, stream)) return kErrCuda;
-  return trimul_contract_run(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows, b_chunks,
-                             b_chunk_stride, k, ld, x_blocked, strict,
-                             static_cast<int*>(workspace), stream);
+  return fpb_trimul_group_contract(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows,
+                                   b_chunks, b_chunk_stride, k, ld, 128, x_blocked, precision,
+                                   workspace, workspace_bytes, stream);
 }
 
 extern "C" int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked,

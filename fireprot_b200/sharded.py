@@ -16,6 +16,12 @@ batch split of ``python/fireprot/backends/amd/two_gcd_attention.py:53-101``):
 * TriMul incoming ``x_ij = sum_k a_ki b_kj``: the rank holds rows ``k`` of
   ``a`` and ``b`` -> partial contraction over its ``k`` for all ``(i, j)``,
   reduce-scatter of ``x`` by rows.
+* TriMul, channel-group scheme (``trimul_scheme``: four or more ranks): the
+  channels of the contraction are independent, so rank ``g`` takes channel
+  group ``g`` (``128 / W`` planes) of every rank's projected ``a`` and ``b``
+  (one all-to-all each), contracts it over the whole ``n x n`` grid and
+  returns each rank its rows of ``x`` (a third all-to-all). Per rank that
+  moves ``3/W`` of the row scheme's bytes.
 * TriAttn starting node: q/k/v/gate of row ``i`` come from row ``i``; only
   the pair bias ``b[h, j, k]`` spans all rows -> all-gather of the rank's
   rows of the row-blocked bias.
@@ -308,6 +314,91 @@ class CudaPhases:
         ops.single_block(s, z_loc[:shard.rows], mask, cached[1], r0=shard.r0, precision=self.p,
                          eps=self.eps, workspace=ws)
 
+    # ------------------------------------------------ TriMul, channel groups
+    def trimul_proj_groups(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
+        """Gated, masked a/b planes of the rank's rows, unsplit (FP32 strict,
+        BF16 fast) and channel-first ``[128][rows_p][ld]``, so that channel
+        group ``g`` is the ``g``-th contiguous block of the all-to-all:
+        outgoing ``rows_p = chunk``, ``ld = ld(n)``; incoming ``rows_p = n``,
+        ``ld = ld(chunk)`` with the columns past the rank's rows zero (they
+        are terms of the concatenated contraction index)."""
+        n, rows, chunk = shard.n, shard.rows, shard.chunk
+        dev = z_loc.device
+        if outgoing:
+            ld, plane_rows = int(self.lib.fpb_trimul_plane_ld(n, self.p)), chunk
+        else:
+            ld, plane_rows = int(self.lib.fpb_trimul_plane_ld(chunk, self.p)), n
+        a = torch.empty(128, plane_rows, ld, dtype=self._dtype(), device=dev)
+        b = torch.empty_like(a)
+        if rows:
+            ws = self._ws_take("trimul_proj", self.lib.fpb_trimul_shard_workspace_size(self.p),
+                               dev)
+            keys = ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p", "w_b_g")
+            wt = [w[k].contiguous() for k in keys]
+            _lib.check(self.lib.fpb_trimul_shard_proj(
+                z_loc.data_ptr(), self._ptr(mask), n, rows, shard.r0, int(not outgoing),
+                *[t.data_ptr() for t in wt], self.eps, a.data_ptr(), 0, b.data_ptr(), 0, ld,
+                plane_rows, self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)),
+                "fpb_trimul_shard_proj")
+        if not outgoing and rows < chunk:
+            a[:, :, rows:chunk].zero_()
+            b[:, :, rows:chunk].zero_()
+        return a, b, ld
+
+    def _split(self, t):
+        """Strict: ``[t (now hi), lo]`` split in place; fast: ``[t]``."""
+        if not self.strict:
+            return [t]
+        lo = torch.empty_like(t)
+        _lib.check(self.lib.fpb_split_tf32(t.data_ptr(), t.data_ptr(), lo.data_ptr(), t.numel(),
+                                           ops._stream_ptr(t.device)), "fpb_split_tf32")
+        return [t, lo]
+
+    def trimul_contract_groups(self, ra, rb, shard: RowShard, outgoing: bool, ld: int):
+        """This rank's channel group contracted over the whole grid. ``ra``,
+        ``rb``: the received ``[world][G][rows_p][ld]`` blocks. Returns x
+        blocked ``[world * chunk][njb][G][128]``; rows ``[r * chunk, (r + 1) *
+        chunk)`` are rank ``r``'s (the send block of the return all-to-all)."""
+        W, n, chunk = shard.world, shard.n, shard.chunk
+        G = 128 // W
+        dev = ra.device
+        if outgoing:
+            # A: the row blocks of every rank stacked; B: read as W chunks
+            a_op = self._split(ra.view(W, G, chunk, ld).transpose(0, 1).contiguous())
+            b_op = self._split(rb)
+            geo = dict(m=n, a_rows=W * chunk, nn=n, b_chunk_rows=chunk, b_chunks=W,
+                       b_chunk_stride=G * chunk * ld, k=n, ld=ld)
+        else:
+            # the contraction index k runs over every rank's rows: concatenate
+            # the ranks' column blocks
+            ldk = int(self.lib.fpb_trimul_plane_ld(W * chunk, self.p))
+
+            def cat(r):
+                t = torch.empty(G, n, ldk, dtype=r.dtype, device=dev)
+                t[:, :, :W * chunk].view(G, n, W, chunk).copy_(
+                    r.view(W, G, n, ld)[..., :chunk].permute(1, 2, 0, 3))
+                return t
+
+            a_op, b_op = self._split(cat(ra)), self._split(cat(rb))
+            geo = dict(m=n, a_rows=n, nn=n, b_chunk_rows=n, b_chunks=1, b_chunk_stride=0,
+                       k=W * chunk, ld=ldk)
+        x = torch.empty(W * chunk, (n + 127) // 128, G, 128, dtype=self._dtype(), device=dev)
+        ws = self._ws_take("trimul_contract", 256, dev)
+        _lib.check(self.lib.fpb_trimul_group_contract(
+            *self._pair(a_op), geo["m"], geo["a_rows"], *self._pair(b_op), geo["nn"],
+            geo["b_chunk_rows"], geo["b_chunks"], geo["b_chunk_stride"], geo["k"], geo["ld"], G,
+            x.data_ptr(), self.p, ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)),
+            "fpb_trimul_group_contract")
+        return x
+
+    def trimul_ungroup_x(self, rx, shard: RowShard):
+        """The rank's x rows ``[chunk][njb][128][128]`` from the received
+        ``[world][chunk][njb][G][128]`` (block ``g``: channel group ``g``)."""
+        W, chunk = shard.world, shard.chunk
+        njb = (shard.n + 127) // 128
+        return (rx.view(W, chunk, njb, 128 // W, 128).permute(1, 2, 0, 3, 4)
+                .reshape(chunk, njb, 128, 128))
+
     def check(self) -> None:
         """Raise if any wait of any phase kernel gave up (reads status words)."""
         for name, ws in self._ws.items():
@@ -321,9 +412,48 @@ class CudaPhases:
 # ---------------------------------------------------------------------------
 # rank-local orchestration (every rank runs the same collective sequence)
 # ---------------------------------------------------------------------------
+TRIMUL_SCHEMES = ("rows", "channels")
+
+
+def trimul_scheme(world: int) -> str:
+    """Exchange scheme of the TriMul contraction for ``world`` ranks. Per rank
+    and operator the row scheme moves ``(W-1)/W`` of the full ``n x n x 128``
+    planes (the all-gather of ``b`` or the reduce-scatter of ``x``); the
+    channel scheme moves ``(W-1)/W`` of three rank shares (``a``, ``b`` and
+    ``x``, each ``1/W`` of the planes), ``3/W`` of it, and splits only its own
+    group for the strict operands: channels from four ranks up, when the 128
+    channels divide evenly."""
+    return "channels" if world >= 4 and 128 % world == 0 else "rows"
+
+
+def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
+    a, b, ld = phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w)
+    ra = torch.empty_like(a)
+    comm.all_to_all(ra, a)
+    del a
+    rb = torch.empty_like(b)
+    comm.all_to_all(rb, b)
+    del b
+    xg = phases.trimul_contract_groups(ra, rb, shard, outgoing, ld)
+    del ra, rb
+    rx = torch.empty_like(xg)
+    comm.all_to_all(rx, xg)
+    del xg
+    phases.trimul_finish(z_loc, shard, phases.trimul_ungroup_x(rx, shard), w, add)
+    return z_loc
+
+
 def sharded_trimul(z_loc, mask, w: dict, shard: RowShard, comm, phases, *, outgoing: bool,
-                   add: bool = True):
-    """Triangle multiplicative update of the rank's rows, in place on ``z_loc``."""
+                   add: bool = True, scheme: str | None = None):
+    """Triangle multiplicative update of the rank's rows, in place on ``z_loc``.
+    ``scheme``: ``"rows"`` or ``"channels"`` (default ``trimul_scheme``)."""
+    scheme = trimul_scheme(shard.world) if scheme is None else scheme
+    if scheme not in TRIMUL_SCHEMES:
+        raise ValueError(f"unknown TriMul scheme {scheme!r}")
+    if scheme == "channels":
+        if 128 % shard.world:
+            raise ValueError(f"channel scheme needs 128 % world == 0 (world={shard.world})")
+        return _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add)
     a, b, ld = phases.trimul_proj(z_loc, mask, shard, outgoing, w)
     if outgoing:
         b_full = []
@@ -357,13 +487,17 @@ def sharded_triattn(z_loc, mask, w: dict, shard: RowShard, comm, phases, *,
     return z_loc
 
 
-def sharded_pair_block(z_loc, mask, weights: dict, shard: RowShard, comm, phases):
+def sharded_pair_block(z_loc, mask, weights: dict, shard: RowShard, comm, phases, *,
+                       scheme: str | None = None):
     """Pair stack of one Pairformer block on the rank's rows (AF3 Algorithm 17
     order): TriMul out, TriMul in, TriAttn start, TriAttn end, transition.
     ``weights`` maps ``tri_mul_out, tri_mul_in, tri_att_start, tri_att_end,
-    pair_transition`` to the operators' weight dicts."""
-    sharded_trimul(z_loc, mask, weights["tri_mul_out"], shard, comm, phases, outgoing=True)
-    sharded_trimul(z_loc, mask, weights["tri_mul_in"], shard, comm, phases, outgoing=False)
+    pair_transition`` to the operators' weight dicts; ``scheme`` the TriMul
+    exchange scheme (default ``trimul_scheme(world)``)."""
+    sharded_trimul(z_loc, mask, weights["tri_mul_out"], shard, comm, phases, outgoing=True,
+                   scheme=scheme)
+    sharded_trimul(z_loc, mask, weights["tri_mul_in"], shard, comm, phases, outgoing=False,
+                   scheme=scheme)
     sharded_triattn(z_loc, mask, weights["tri_att_start"], shard, comm, phases, starting=True)
     sharded_triattn(z_loc, mask, weights["tri_att_end"], shard, comm, phases, starting=False)
     phases.transition(z_loc, shard, weights["pair_transition"])

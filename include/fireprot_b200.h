@@ -195,15 +195,28 @@ int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int n, int rows
                           const float* w_b_g, float eps, void* a_hi, void* a_lo, void* b_hi,
                           void* b_lo, int ld, int plane_rows, int precision, void* workspace,
                           size_t workspace_bytes, cudaStream_t stream);
-/* Strict mode may pass b_lo = NULL to fpb_trimul_shard_proj: b is then
- * written unsplit (FP32) into the b_hi planes, half the bytes of the
- * outgoing all-gather; after it, fpb_split_tf32 splits the gathered planes
- * exactly (hi = x with the low 13 mantissa bits cleared, lo = x - hi; hi may
- * alias src). No reference counterpart (the reference has no sharded path). */
+/* Strict mode may pass a_lo and/or b_lo = NULL to fpb_trimul_shard_proj: a
+ * or b is then written unsplit (FP32) into its hi planes, half the bytes of
+ * the exchange that follows; after it, fpb_split_tf32 splits the received
+ * planes exactly (hi = x with the low 13 mantissa bits cleared, lo = x - hi;
+ * hi may alias src). No reference counterpart (the reference has no sharded
+ * path). */
 int fpb_split_tf32(const float* src, void* hi, void* lo, size_t count, cudaStream_t stream);
 int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
                               const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
                               int b_chunks, size_t b_chunk_stride, int k, int ld,
+                              void* x_blocked, int precision, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
+/* Channel-group form of the contraction (the channel-sharded TriMul: every
+ * rank projects its rows, an all-to-all hands channel group g of every rank's
+ * planes to rank g, which contracts its `channels` planes over the whole
+ * n x n grid; a second all-to-all returns the output rows). The operands are
+ * `channels` planes laid out as for fpb_trimul_shard_contract; the output is
+ * blocked [m][ceil(nn/128)][channels][128]. fpb_trimul_shard_contract is this
+ * call with channels = 128. */
+int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
+                              const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
+                              int b_chunks, size_t b_chunk_stride, int k, int ld, int channels,
                               void* x_blocked, int precision, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
 int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked,

@@ -79,6 +79,41 @@ class OraclePhases:
         delta = torch.sigmoid(zn @ _d(w["w_g"]).T) * x
         z_loc[:rows] = (zl + delta if add else delta).to(z_loc.dtype)
 
+    # TriMul, channel groups: planes [128][rows_p][cols] float64
+    def trimul_proj_groups(self, z_loc, mask, shard, outgoing, w):
+        self.calls.append("trimul_proj_groups")
+        n, rows, chunk = shard.n, shard.rows, shard.chunk
+        pa = torch.zeros(128, chunk, n, dtype=torch.float64) if outgoing else \
+            torch.zeros(128, n, chunk, dtype=torch.float64)
+        pb = torch.zeros_like(pa)
+        if rows:
+            a, b, _ = self.trimul_proj(z_loc, mask, shard, True, w)
+            self.calls.pop()
+            a, b = a[0][:rows].permute(2, 0, 1), b[0][:rows].permute(2, 0, 1)  # [c][i][k]
+            if outgoing:
+                pa[:, :rows], pb[:, :rows] = a, b
+            else:
+                pa[:, :, :rows], pb[:, :, :rows] = a.transpose(1, 2), b.transpose(1, 2)
+        return pa, pb, (n if outgoing else chunk)
+
+    def trimul_contract_groups(self, ra, rb, shard, outgoing, ld):
+        self.calls.append("trimul_contract_groups")
+        W, n, chunk = shard.world, shard.n, shard.chunk
+        G = 128 // W
+        if outgoing:
+            def op(r):
+                return r.view(W, G, chunk, n).transpose(0, 1).reshape(G, W * chunk, n)[:, :n]
+        else:
+            def op(r):
+                return r.view(W, G, n, chunk).permute(1, 2, 0, 3).reshape(G, n, W * chunk)
+        xg = torch.zeros(W * chunk, n, G, dtype=torch.float64)
+        xg[:n] = torch.einsum("cik,cjk->ijc", op(ra), op(rb))
+        return xg
+
+    def trimul_ungroup_x(self, rx, shard):
+        W, chunk, n = shard.world, shard.chunk, shard.n
+        return rx.view(W, chunk, n, 128 // W).permute(1, 2, 0, 3).reshape(chunk, n, 128)
+
     # TriAttn: bias buffer [world*chunk][4][n] (j-major), state = mask rows
     def triattn_bias_buffer(self, shard, device):
         return torch.zeros(shard.world * shard.chunk, 4, shard.n, dtype=torch.float64)

@@ -51,10 +51,12 @@ def _run(world, n, z, mask, device, body):
     return run_threads(world, rank_fn)
 
 
-@pytest.mark.parametrize("world,n", [(2, 100), (3, 70), (4, 40)])
+@pytest.mark.parametrize("world,n,scheme", [(2, 100, "rows"), (3, 70, "rows"), (4, 40, "rows"),
+                                            (2, 100, "channels"), (4, 200, "channels"),
+                                            (8, 33, "channels"), (8, 300, "channels")])
 @pytest.mark.parametrize("outgoing", [True, False])
 @pytest.mark.parametrize("precision", ["strict", "fast"])
-def test_sharded_trimul(cuda_device, world, n, outgoing, precision):
+def test_sharded_trimul(cuda_device, world, n, scheme, outgoing, precision):
     z = O.make_pair(n, seed=21 + n)
     mask = _mask(n, "random")
     p = O.make_trimul_params(seed=5, ln_affine_random=True)
@@ -65,7 +67,7 @@ def test_sharded_trimul(cuda_device, world, n, outgoing, precision):
 
     def body(z_loc, md, sh, comm):
         ph = S.CudaPhases(precision)
-        S.sharded_trimul(z_loc, md, w, sh, comm, ph, outgoing=outgoing)
+        S.sharded_trimul(z_loc, md, w, sh, comm, ph, outgoing=outgoing, scheme=scheme)
         return ph
 
     for full in _run(world, n, z, mask, cuda_device, body):
@@ -94,7 +96,8 @@ def test_sharded_triattn(cuda_device, world, n, starting, precision, mask_kind):
 
 
 @pytest.mark.parametrize("world,n,mask_kind", [(1, 96, "padding"), (2, 150, "padding"),
-                                               (3, 100, "none"), (5, 130, "random")])
+                                               (3, 100, "none"), (5, 130, "random"),
+                                               (4, 130, "random"), (8, 260, "padding")])
 @pytest.mark.parametrize("precision", ["strict", "fast"])
 def test_sharded_block(cuda_device, world, n, mask_kind, precision):
     z = O.make_pair(n, seed=41 + n)

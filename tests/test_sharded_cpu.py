@@ -132,6 +132,43 @@ def test_sharded_trimul_add_false_threads(outgoing):
         assert O.rel_max_err(full, ref) <= TOL
 
 
+@pytest.mark.parametrize("n,world,scheme", [(50, 2, "channels"), (45, 4, "channels"),
+                                            (45, 4, "rows"), (33, 8, "channels"),
+                                            (70, 8, "channels")])
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_sharded_trimul_schemes_threads(n, world, scheme, outgoing):
+    """Both exchange schemes of the TriMul contraction, including ranks with
+    ragged and empty row ranges (n=33 over 8 ranks: 32 + 1 + six empty)."""
+    z, mask, p = _case(n, "random")
+    w = oracle_weight_dicts(p)["tri_mul_out" if outgoing else "tri_mul_in"]
+    ref = O.triangle_multiplication(z, mask, p.tri_mul_out if outgoing else p.tri_mul_in,
+                                    outgoing=outgoing, add=True)
+
+    def rank_fn(r, comm):
+        sh = S.shard_plan(n, world, r)
+        z_loc = S.local_rows(z, sh)
+        ph = OraclePhases()
+        S.sharded_trimul(z_loc, mask, w, sh, comm, ph, outgoing=outgoing, scheme=scheme)
+        return S.gather_rows(z_loc, sh, comm), ph.calls
+
+    for full, calls in run_threads(world, rank_fn):
+        assert O.rel_max_err(full, ref) <= TOL
+        assert ("trimul_contract_groups" in calls) == (scheme == "channels")
+
+
+def test_trimul_scheme_choice():
+    assert [S.trimul_scheme(w) for w in (1, 2, 3, 4, 5, 6, 8, 16)] == \
+        ["rows", "rows", "rows", "channels", "rows", "rows", "channels", "channels"]
+    z, mask, p = _case(40, "none")
+    sh = S.shard_plan(40, 3, 0)
+    with pytest.raises(ValueError):
+        S.sharded_trimul(S.local_rows(z, sh), mask, oracle_weight_dicts(p)["tri_mul_out"], sh,
+                         None, OraclePhases(), outgoing=True, scheme="channels")
+    with pytest.raises(ValueError):
+        S.sharded_trimul(S.local_rows(z, sh), mask, oracle_weight_dicts(p)["tri_mul_out"], sh,
+                         None, OraclePhases(), outgoing=True, scheme="columns")
+
+
 # ----------------------------------------------------------------- gloo ranks
 def _free_port():
     with socket.socket() as s:
@@ -153,7 +190,8 @@ def _gloo_rank(rank, world, port, n, mask_kind, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n,world,mask_kind", [(40, 2, "padding"), (40, 3, "random")])
+@pytest.mark.parametrize("n,world,mask_kind", [(40, 2, "padding"), (40, 3, "random"),
+                                               (70, 4, "random")])
 def test_sharded_block_gloo(tmp_path, n, world, mask_kind):
     mp.start_processes(_gloo_rank, args=(world, _free_port(), n, mask_kind, str(tmp_path)),
                        nprocs=world, start_method="spawn")

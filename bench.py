@@ -225,7 +225,14 @@ def _config(args):
             "parallelism": ("single GPU" if args.gpus == 1 else
                             f"rows of z sharded over {args.gpus} GPUs (NCCL all-gather, "
                             f"reduce-scatter, all-to-all)" if args.mode == "sharded" else
-                            f"independent replicas x{args.gpus}")}
+                            f"independent replicas x{args.gpus}"),
+            **({"trimul_exchange": _trimul_scheme(args)}
+               if args.gpus > 1 and args.mode == "sharded" else {})}
+
+
+def _trimul_scheme(args):
+    from fireprot_b200.sharded import trimul_scheme
+    return trimul_scheme(args.gpus) if args.trimul_scheme == "auto" else args.trimul_scheme
 
 
 # ---------------------------------------------------------------------------
@@ -257,13 +264,14 @@ def run_ours(args, world, rank, local):
         w_single = block.single.weight_dict()
         z_host = S.local_rows(z_full, shard).pin_memory()
         rows_frac = shard.rows / n
+        scheme = _trimul_scheme(args)
 
         def make_step(precision):
             phases = S.CudaPhases(precision)
 
             def step(zz, ss, mm):
                 # ss: [W * chunk, 384] all-gather buffer holding s in its first n rows
-                S.sharded_pair_block(zz, mm, weights, shard, comm, phases)
+                S.sharded_pair_block(zz, mm, weights, shard, comm, phases, scheme=scheme)
                 S.sharded_single_block(ss, zz, mm, w_single, shard, comm, phases)
             return step, phases.check
 
@@ -488,6 +496,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--mode", choices=["sharded", "replicas"], default="sharded",
                     help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
+    ap.add_argument("--trimul-scheme", choices=["auto", "rows", "channels"], default="auto",
+                    help="N>1 sharded: TriMul exchange (auto: channels from 4 GPUs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
     args = ap.parse_args()

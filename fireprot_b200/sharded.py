@@ -110,18 +110,30 @@ def gather_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
     return full[:shard.n]
 
 
-def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
+def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm, out=None) -> torch.Tensor:
     """Rows of ``z^T`` owned by this rank: ``zt[i, j] = z[j, i]`` for the
-    rank's ``i``. One all-to-all of ``[chunk, chunk, c]`` blocks; padded
-    columns travel as zeros and padded rows of the result are zero."""
+    rank's ``i``. One all-to-all of ``[chunk, chunk, c]`` blocks, packed and
+    unpacked in one pass each; padded columns travel as zeros and padded rows
+    of the result are zero. ``out``: optional ``[chunk, n, c]`` destination
+    (may be ``z_loc`` itself: the send block is packed before it is written)."""
     w, c, n = shard.world, shard.chunk, shard.n
     ch = z_loc.shape[-1]
-    zp = z_loc.new_zeros(c, w * c, ch)
-    zp[:, :n] = z_loc
-    send = zp.view(c, w, c, ch).permute(1, 0, 2, 3).contiguous()  # [dest][my i][dest j]
+    send = z_loc.new_empty(w, c, c, ch)  # [dest][my i][dest j]
+    for d in range(w):
+        cols = max(0, min(c, n - d * c))
+        if cols:
+            send[d, :, :cols].copy_(z_loc[:, d * c:d * c + cols])
+        if cols < c:
+            send[d, :, cols:].zero_()
     recv = torch.empty_like(send)
     comm.all_to_all(recv, send)  # [src][src rows][my cols]
-    return recv.permute(2, 0, 1, 3).reshape(c, w * c, ch)[:, :n].contiguous()
+    del send
+    res = z_loc.new_empty(c, n, ch) if out is None else out
+    for src in range(w):
+        rows = max(0, min(c, n - src * c))
+        if rows:
+            res[:, src * c:src * c + rows].copy_(recv[src, :rows].transpose(0, 1))
+    return res
 
 
 class CudaPhases:
@@ -477,7 +489,7 @@ def sharded_triattn(z_loc, mask, w: dict, shard: RowShard, comm, phases, *,
         zt = transpose_rows(z_loc, shard, comm)
         mt = None if mask is None else mask.transpose(0, 1).contiguous()
         sharded_triattn(zt, mt, w, shard, comm, phases, starting=True)
-        z_loc.copy_(transpose_rows(zt, shard, comm))
+        transpose_rows(zt, shard, comm, out=z_loc)
         return z_loc
     bias_full = phases.triattn_bias_buffer(shard, z_loc.device)
     state = phases.triattn_proj(z_loc, mask, shard, w, bias_full)

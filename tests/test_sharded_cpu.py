@@ -35,7 +35,7 @@ def test_shard_plan_covers_rows_once():
         S.shard_plan(10, 2, 2)
 
 
-@pytest.mark.parametrize("n,world", [(40, 2), (70, 3), (33, 4)])
+@pytest.mark.parametrize("n,world", [(40, 2), (70, 3), (33, 4), (33, 8)])
 def test_transpose_rows_threads(n, world):
     z = torch.randn(n, n, 6, dtype=torch.float64, generator=torch.Generator().manual_seed(n))
 
@@ -46,6 +46,8 @@ def test_transpose_rows_threads(n, world):
         assert not zt[sh.rows:].any()
         back = S.transpose_rows(zt, sh, comm)
         assert torch.equal(back[:sh.rows], z[sh.r0:sh.r0 + sh.rows])
+        S.transpose_rows(zt, sh, comm, out=zt)  # in place
+        assert torch.equal(zt[:sh.rows], z[sh.r0:sh.r0 + sh.rows])
         return S.gather_rows(S.local_rows(z, sh), sh, comm)
 
     for full in run_threads(world, rank_fn):

@@ -26,18 +26,9 @@ struct TransCfg {
   static constexpr int G1N = 2 * HC;           // GEMM 1 width (a_c | b_c)
   static constexpr int G1_STAGE = G1N * 128 * R::NSPLIT;   // bytes of one GEMM-1 W stage
   static constexpr int G2_STAGE = 128 * 128 * R::NSPLIT;   // bytes of one GEMM-2 W stage
-  // Weight ring of 16 KB slots: a GEMM-1 stage fills one, a GEMM-2 stage
-  // G2_SLOTS adjacent ones. The per-tile load sequence is G1(0), then per
-  // chunk c: G1(c+1) (NKA slots), G2(c), so every G2 stage starts at an even
-  // position; with an even slot count it never wraps around the ring.
-  static constexpr int SLOT = 16384;
-  static constexpr int G2_SLOTS = G2_STAGE / SLOT;
-  static constexpr int SLOTS = 12;  // two strict chunks (6 slots each) / four fast ones
-  static_assert(G1_STAGE == SLOT && G2_STAGE % SLOT == 0, "slot size");
-  static_assert(SLOTS % G2_SLOTS == 0 && (R::NKA % G2_SLOTS) == 0, "G2 stages must not wrap");
-  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows
-  // SwiGLU tiles: one in strict mode (its ring needs the room), two in fast
-  static constexpr int H_BUFS = kStrict ? 1 : 2;
+  static constexpr int STAGE = G1_STAGE > G2_STAGE ? G1_STAGE : G2_STAGE;
+  static constexpr int STAGES = 5;
+  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows (x2 buffers)
   // TMEM: A = LN(z) (tf32 hi | lo: 256 columns; bf16 pairs: 64), two
   // GEMM-1 buffers, the GEMM-2 accumulator (128)
   static constexpr uint32_t kA_LO = 128;
@@ -46,7 +37,7 @@ struct TransCfg {
   static constexpr int TMEM_COLS = 512;
   static_assert(kAcc + 128 <= TMEM_COLS, "TMEM budget");
   static constexpr int SMEM =
-      tmem_safe_smem(H_BUFS * H_BYTES + SLOTS * SLOT + 1024 + 256 + 1024, TMEM_COLS);
+      tmem_safe_smem(2 * H_BYTES + STAGES * STAGE + 1024 + 256 + 1024, TMEM_COLS);
 };
 
 struct TransArgs {
@@ -61,17 +52,12 @@ struct TransArgs {
 
 // One CTA per 128-row tile. The LayerNorm'd tile lives in TMEM (thread t =
 // row t normalises its own row and stores it as the A operand of GEMM 1), so
-// shared memory holds only the SwiGLU tiles H and a ring of twelve 16 KB
-// weight slots (two strict chunks, four fast ones, of prefetch: the weights
-// stream from L2 for every tile, and a ring one chunk deep left the tensor
-// pipe waiting on their latency):
+// shared memory holds only two SwiGLU tiles H and a 5-stage weight ring:
 //   GEMM 1 (chunk c): [a_c | b_c] = A [Wa_c; Wb_c]^T     (A from TMEM)
 //   row threads:      H = silu(a_c) * b_c -> shared memory (A operand)
 //   GEMM 2:           acc += H Wout_c^T
-// with GEMM 1 double-buffered in TMEM so that it runs one chunk ahead. In
-// fast mode H is double-buffered; in strict mode the SwiGLU of chunk c+1 is
-// computed while GEMM 2(c) runs and stored once it has read H, which GEMM
-// 1(c+2), issued behind GEMM 2(c), covers.
+// with GEMM 1 double-buffered in TMEM so that it runs one chunk ahead, and H
+// double-buffered so that the SwiGLU of chunk c+1 never waits for GEMM 2(c).
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 1)
     transition_kernel(const __grid_constant__ CUtensorMap w1_hi,
@@ -83,13 +69,13 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* H = smem;                 // [H_BUFS][H_BYTES]
-  uint8_t* W = H + C::H_BUFS * C::H_BYTES;
-  float* lnp = reinterpret_cast<float*>(W + C::SLOTS * C::SLOT);  // [2][128]
+  uint8_t* H = smem;                 // [2][H_BYTES]
+  uint8_t* W = H + 2 * C::H_BYTES;
+  float* lnp = reinterpret_cast<float*>(W + C::STAGES * C::STAGE);  // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(lnp + 256);
   uint64_t* wfull = bars;
-  uint64_t* wempty = wfull + C::SLOTS;
-  uint64_t* a_full = wempty + C::SLOTS;
+  uint64_t* wempty = wfull + C::STAGES;
+  uint64_t* a_full = wempty + C::STAGES;
   uint64_t* g1_full = a_full + 1;   // [2]
   uint64_t* g1_free = g1_full + 2;  // [2]
   uint64_t* h_full = g1_free + 2;  // [2]
@@ -104,7 +90,7 @@ __global__ void __launch_bounds__(192, 1)
   const long long p0 = (long long)blockIdx.x * 128;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::SLOTS; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&wempty[s], 1);
     }
@@ -218,17 +204,15 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(&g1_free[b]);
-      // H buffer hb was read by GEMM 2 of chunk c - H_BUFS
-      const int hb = c % C::H_BUFS;
-      if (c >= C::H_BUFS &&
-          !mbar_wait(&h_free[hb], ((c - C::H_BUFS) / C::H_BUFS) & 1, g, 32)) {
+      // H buffer b was read by GEMM 2 of chunk c-2
+      if (c >= 2 && !mbar_wait(&h_free[b], ((c - 2) >> 1) & 1, g, 32)) {
         ok = false;
         break;
       }
       // H row t: one K atom (HC elements)
 #pragma unroll
       for (int e = 0; e < C::HC; e += 4) {
-        uint8_t* dst = H + hb * C::H_BYTES + sw128_offset(t, e * R::ESZ);
+        uint8_t* dst = H + b * C::H_BYTES + sw128_offset(t, e * R::ESZ);
         if constexpr (kStrict) {
           float h0, l0, h1, l1, h2, l2, h3, l3;
           split_tf32(hv[e], h0, l0);
@@ -248,7 +232,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&h_full[hb]);
+      mbar_arrive(&h_full[b]);
     }
     if (ok && mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
@@ -282,28 +266,21 @@ __global__ void __launch_bounds__(192, 1)
       int seq = 0;
       bool ok = true;
       auto push = [&](bool g2, int c, int atom) -> bool {
-        const int uses = g2 ? C::G2_SLOTS : 1;
-        for (int u = 0; u < uses; ++u) {
-          const int q = seq + u;
-          if (q >= C::SLOTS && !mbar_wait(&wempty[q % C::SLOTS], ((q / C::SLOTS) & 1) ^ 1, g, 33))
-            return false;
-        }
-        const int s = seq % C::SLOTS;
-        uint8_t* st = W + s * C::SLOT;
+        const int s = seq % C::STAGES;
+        const uint32_t ph = (seq / C::STAGES) & 1;
+        if (seq >= C::STAGES && !mbar_wait(&wempty[s], ph ^ 1, g, 33)) return false;
+        uint8_t* st = W + s * C::STAGE;
         if (g2) {
           mbar_arrive_expect_tx(&wfull[s], C::G2_STAGE);
           tma_load_3d(st, &w2_hi, &wfull[s], c * C::HC, 0, 0);
           if constexpr (kStrict) tma_load_3d(st + R::ATOM_BYTES, &w2_lo, &wfull[s], c * C::HC, 0, 0);
-          // the stage's other slots carry no transaction of their own: their
-          // phase completes with this arrival (wfull[s] counts the bytes)
-          for (int u = 1; u < uses; ++u) mbar_arrive(&wfull[s + u]);
         } else {
           mbar_arrive_expect_tx(&wfull[s], C::G1_STAGE);
           tma_load_3d(st, &w1_hi, &wfull[s], atom * R::KATOM, c * C::G1N, 0);
           if constexpr (kStrict)
             tma_load_3d(st + C::G1N * 128, &w1_lo, &wfull[s], atom * R::KATOM, c * C::G1N, 0);
         }
-        seq += uses;
+        ++seq;
         return true;
       };
       for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, 0, a);
@@ -313,8 +290,8 @@ __global__ void __launch_bounds__(192, 1)
         if (ok) ok = push(true, c, 0);
       }
       if (g.aborted()) {
-        for (int q = (seq > C::SLOTS ? seq - C::SLOTS : 0); q < seq; ++q)
-          (void)mbar_wait(&wfull[q % C::SLOTS], (q / C::SLOTS) & 1, Guard{nullptr, abort_flag}, 0);
+        for (int q = (seq > C::STAGES ? seq - C::STAGES : 0); q < seq; ++q)
+          (void)mbar_wait(&wfull[q % C::STAGES], (q / C::STAGES) & 1, Guard{nullptr, abort_flag}, 0);
       }
     }
   } else {
@@ -323,17 +300,15 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t id2 = kStrict ? idesc_tf32(128, 128) : idesc_bf16(128, 128);
       const uint32_t h0 = smem_u32(H);
       int seq = 0;
-      auto take = [&](int uses) -> uint32_t {
-        for (int u = 0; u < uses; ++u) {
-          const int q = seq + u;
-          if (!mbar_wait(&wfull[q % C::SLOTS], (q / C::SLOTS) & 1, g, 34)) return 0;
-        }
+      auto take = [&]() -> uint32_t {
+        const int s = seq % C::STAGES;
+        if (!mbar_wait(&wfull[s], (seq / C::STAGES) & 1, g, 34)) return 0;
         tc_fence_after();
-        return smem_u32(W + (seq % C::SLOTS) * C::SLOT);
+        return smem_u32(W + s * C::STAGE);
       };
-      auto release = [&](int uses) {
-        for (int u = 0; u < uses; ++u) umma_commit(&wempty[(seq + u) % C::SLOTS]);
-        seq += uses;
+      auto release = [&]() {
+        umma_commit(&wempty[seq % C::STAGES]);
+        ++seq;
       };
       auto gemm1 = [&](int c) -> bool {
         const int b = c & 1;
@@ -341,7 +316,7 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d = tmem + C::kG1 + b * C::G1N;
         for (int a = 0; a < R::NKA; ++a) {
-          const uint32_t w = take(1);
+          const uint32_t w = take();
           if (!w) return false;
           // A atom a from TMEM: 4 K steps of 8 tf32 / 16 bf16 (8 columns each)
 #pragma unroll
@@ -358,7 +333,7 @@ __global__ void __launch_bounds__(192, 1)
               umma_bf16_ts(d, tmem + acol, dwh, id1, acc);
             }
           }
-          release(1);
+          release();
         }
         umma_commit(&g1_full[b]);
         return true;
@@ -368,13 +343,13 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = gemm1(0);
       for (int c = 0; c < C::NCH && ok; ++c) {
         if (c + 1 < C::NCH && !(ok = gemm1(c + 1))) break;
-        const int hb = c % C::H_BUFS;
-        if (!mbar_wait(&h_full[hb], (c / C::H_BUFS) & 1, g, 37)) {
+        const int hb = c & 1;
+        if (!mbar_wait(&h_full[hb], (c >> 1) & 1, g, 37)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t w = take(C::G2_SLOTS);
+        const uint32_t w = take();
         if (!w) {
           ok = false;
           break;
@@ -382,7 +357,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t h_hi = h0 + hb * C::H_BYTES;
         mma_k_atom<kStrict>(tmem + C::kAcc, h_hi, h_hi + R::ATOM_BYTES, w, w + R::ATOM_BYTES, id2,
                             c == 0);
-        release(C::G2_SLOTS);
+        release();
         umma_commit(&h_free[hb]);
       }
       if (ok) {

@@ -43,11 +43,14 @@ def main(out_path: str) -> None:
             sh = S.shard_plan(n, comm.world, comm.rank)
             ref = O.pair_block(z, mask, p) if comm.rank == 0 else None
             s_ref = O.single_block(s, ref, mask, ps) if comm.rank == 0 else None
-            for precision in ("strict", "fast"):
+            # both TriMul exchange schemes at every world size (the channel
+            # scheme is the default only from four ranks)
+            for precision, scheme in (("strict", "rows"), ("fast", "rows"),
+                                      ("strict", "channels"), ("fast", "channels")):
                 z_loc = S.local_rows(z.to(dev), sh)
                 s_buf = S.single_buffer(s.to(dev), sh)
                 ph = S.CudaPhases(precision)
-                S.sharded_pair_block(z_loc, md, w, sh, comm, ph)
+                S.sharded_pair_block(z_loc, md, w, sh, comm, ph, scheme=scheme)
                 S.sharded_single_block(s_buf, z_loc, md, ws, sh, comm, ph)
                 torch.cuda.synchronize(dev)
                 ph.check()
@@ -56,9 +59,9 @@ def main(out_path: str) -> None:
                     tol = O.STRICT_TOL if precision == "strict" else O.FAST_TOL
                     err = O.rel_max_err(full, ref)
                     err_s = O.rel_max_err(s_buf[:n].cpu(), s_ref)
-                    results[f"n{n}_{mask_kind}_{precision}"] = {"err": err, "err_s": err_s,
-                                                               "tol": tol,
-                                                               "ok": err <= tol and err_s <= tol}
+                    results[f"n{n}_{mask_kind}_{precision}_{scheme}"] = {
+                        "err": err, "err_s": err_s, "tol": tol,
+                        "ok": err <= tol and err_s <= tol}
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -252,6 +252,16 @@ __global__ void __launch_bounds__(320, 1)
               const size_t row = (ih * n + j) * 32;
               if constexpr (kStrict) {
                 float4* oh = reinterpret_cast<float4*>(static_cast<float*>(dh) + row);
+                if (dl == nullptr) {
+                  // q unsplit: the attention core splits it when staging Q
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    oh[e] = make_float4(__uint_as_float(vr[u][4 * e]) * sc,
+                                        __uint_as_float(vr[u][4 * e + 1]) * sc,
+                                        __uint_as_float(vr[u][4 * e + 2]) * sc,
+                                        __uint_as_float(vr[u][4 * e + 3]) * sc);
+                  continue;
+                }
                 float4* ol = reinterpret_cast<float4*>(static_cast<float*>(dl) + row);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -371,6 +381,7 @@ struct AttnCoreArgs {
   void* o;             // [rows*n][128] fp32 (strict or o_f32) / bf16 (fast)
   int* status;
   int o_f32;           // write fp32 output in fast mode too
+  int q_plain;         // strict: q unsplit (FP32) in q_hi, split while staged into TMEM
 };
 
 template <bool kStrict>
@@ -501,9 +512,10 @@ __global__ void __launch_bounds__(192, 2)
     if (lane == 0) {
       // the Q tile is read by this CTA only; keep L2 for the pair bias
       const uint64_t pol_q = policy_evict_first();
-      mbar_arrive_expect_tx(q_full, C::NSPLIT * C::Q_BYTES);
+      const bool q_split = kStrict && !p.q_plain;
+      mbar_arrive_expect_tx(q_full, (q_split ? 2 : 1) * C::Q_BYTES);
       tma_load_3d_hint(Q, &mq_hi, q_full, 0, jt * C::BQ, ih, pol_q);
-      if constexpr (kStrict) tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
+      if (q_split) tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int s = t % C::KV_STAGES;
@@ -677,19 +689,39 @@ __global__ void __launch_bounds__(192, 2)
     bool ok = mbar_wait(q_full, 0, g, 20);
     if (ok) {
       if constexpr (kStrict) {
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          uint32_t qr[32];
+        if (p.q_plain) {
+          // unsplit q row: split here (hi = tf32 truncation, lo = rest)
+          uint32_t qh[32], ql[32];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const uint4 v = *reinterpret_cast<const uint4*>(Q + part * C::Q_BYTES +
-                                                            sw128_offset(t_row, e * 16));
-            qr[4 * e] = v.x;
-            qr[4 * e + 1] = v.y;
-            qr[4 * e + 2] = v.z;
-            qr[4 * e + 3] = v.w;
+            const float4 v =
+                *reinterpret_cast<const float4*>(Q + sw128_offset(t_row, e * 16));
+            const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float h, l;
+              split_tf32(f[u], h, l);
+              qh[4 * e + u] = __float_as_uint(h);
+              ql[4 * e + u] = __float_as_uint(l);
+            }
           }
-          tmem_st32(tb + (part == 0 ? C::kQ : C::kQL), qr);
+          tmem_st32(tb + C::kQ, qh);
+          tmem_st32(tb + C::kQL, ql);
+        } else {
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {
+            uint32_t qr[32];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const uint4 v = *reinterpret_cast<const uint4*>(Q + part * C::Q_BYTES +
+                                                              sw128_offset(t_row, e * 16));
+              qr[4 * e] = v.x;
+              qr[4 * e + 1] = v.y;
+              qr[4 * e + 2] = v.z;
+              qr[4 * e + 3] = v.w;
+            }
+            tmem_st32(tb + (part == 0 ? C::kQ : C::kQL), qr);
+          }
         }
       } else {
         uint32_t qr[16];
@@ -890,8 +922,13 @@ int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const
             make_map_3d(&mkh, k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
             make_map_3d(&mvh, v_hi, dt, n, 32, nh, (uint64_t)ldv * esz,
                         (uint64_t)ldv * esz * 32, vkeys, 32, 1, vsw);
+  // strict with no q_lo: q arrives unsplit and the core splits it
+  AttnCoreArgs args = ca;
+  args.q_plain = (strict && q_lo == nullptr) ? 1 : 0;
   if (strict)
-    ok = ok && make_map_3d(&mql, q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+    ok = ok &&
+         make_map_3d(&mql, args.q_plain ? q_hi : q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128,
+                     1, qsw) &&
          make_map_3d(&mkl, k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
          make_map_3d(&mvl, v_lo, dt, n, 32, nh, (uint64_t)ldv * esz, (uint64_t)ldv * esz * 32,
                      vkeys, 32, 1, vsw);
@@ -907,13 +944,13 @@ int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
     FPB_LAUNCH("triattn_core", stream,
                k<<<grid, AttnCfg<true>::THREADS, AttnCfg<true>::SMEM, stream>>>(
-                   mqh, mql, mkh, mkl, mvh, mvl, ca));
+                   mqh, mql, mkh, mkl, mvh, mvl, args));
   } else {
     auto k = attn_core_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
     FPB_LAUNCH("triattn_core", stream,
                k<<<grid, AttnCfg<false>::THREADS, AttnCfg<false>::SMEM, stream>>>(
-                   mqh, mql, mkh, mkl, mvh, mvl, ca));
+                   mqh, mql, mkh, mkl, mvh, mvl, args));
   }
   return launch_status();
 }
@@ -1248,12 +1285,9 @@ struct TriAttnPlan {
     wo_hi = take(256 * 128);
     if (strict) wo_lo = take(256 * 128);
     const size_t qk = (size_t)rows * n * 128;
-    q_hi = take(qk);
+    q_hi = take(qk);  // strict: unsplit, split by the attention core
     k_hi = take(qk);
-    if (strict) {
-      q_lo = take(qk);
-      k_lo = take(qk);
-    }
+    if (strict) k_lo = take(qk);
     ldv = padded_ld(n, strict ? 4 : 2);
     const size_t vc = (size_t)rows * kHeads * 32 * ldv;
     v_hi = take(vc);

@@ -73,6 +73,8 @@ SIGNATURES = {
     "fpb_trimul_group_contract": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                           c_int, c_int, c_int, c_size_t, c_int, c_int, c_int,
                                           c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_group_gather": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                        c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "fpb_trimul_shard_finish": (c_int, [c_void_p, c_int, c_int, c_void_p] + [c_void_p] * 6
                                 + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_triattn_bias_ld": (c_size_t, [c_int]),

@@ -898,3 +898,71 @@ extern "C" int fpb_split_tf32(const float* src, void* hi, void* lo, size_t count
                                                            static_cast<float*>(lo), count));
   return launch_status();
 }
+
+// ----------------------------------------------------------------------------
+// channel-group gather of the received TriMul planes (channel-sharded
+// exchange): src [W][G][R][src_ld] -> the contraction operand, split into
+// hi/lo (strict) or copied (fast) in the same pass.
+//   rows mode: dst[c][r * R + i][k]       = src[r][c][i][k], k < seg
+//   cols mode: dst[c][i][r * seg + k]     = src[r][c][i][k], k < seg
+// One work unit = 4 consecutive k of one (r, c, i) segment.
+// ----------------------------------------------------------------------------
+namespace fpb {
+template <bool kStrict>
+__global__ void group_gather_kernel(const void* __restrict__ src, int W, int G, int R,
+                                    int src_ld, int seg, int cols_mode, void* __restrict__ hi,
+                                    void* __restrict__ lo, int dst_ld) {
+  const int s4 = seg / 4;
+  const size_t units = (size_t)W * G * R * s4;
+  for (size_t u = blockIdx.x * (size_t)blockDim.x + threadIdx.x; u < units;
+       u += (size_t)gridDim.x * blockDim.x) {
+    const int k = (int)(u % s4) * 4;
+    size_t rest = u / s4;
+    const int i = (int)(rest % R);
+    rest /= R;
+    const int c = (int)(rest % G);
+    const int r = (int)(rest / G);
+    const size_t so = (((size_t)r * G + c) * R + i) * src_ld + k;
+    const size_t dof = cols_mode ? ((size_t)c * R + i) * dst_ld + (size_t)r * seg + k
+                                 : ((size_t)c * W * R + (size_t)r * R + i) * dst_ld + k;
+    if constexpr (kStrict) {
+      const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + so);
+      float4 h, l;
+      split_tf32(x.x, h.x, l.x);
+      split_tf32(x.y, h.y, l.y);
+      split_tf32(x.z, h.z, l.z);
+      split_tf32(x.w, h.w, l.w);
+      *reinterpret_cast<float4*>(static_cast<float*>(hi) + dof) = h;
+      *reinterpret_cast<float4*>(static_cast<float*>(lo) + dof) = l;
+    } else {
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(hi) + dof) =
+          *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(src) + so);
+    }
+  }
+}
+}  // namespace fpb
+
+extern "C" int fpb_trimul_group_gather(const void* src, int world, int channels, int rows,
+                                       int src_ld, int seg, int cols_mode, void* dst_hi,
+                                       void* dst_lo, int dst_ld, int precision,
+                                       cudaStream_t stream) {
+  if (!src || !dst_hi) return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (strict && !dst_lo) return kErrArg;
+  if (world <= 0 || channels <= 0 || rows <= 0 || seg <= 0 || seg > src_ld) return kErrShape;
+  if (cols_mode ? dst_ld < (long long)world * seg : dst_ld < seg) return kErrShape;
+  if (seg % 4 || src_ld % 4 || dst_ld % 4) return kErrAlign;
+  if (!aligned16(src) || !aligned16(dst_hi) || (strict && !aligned16(dst_lo))) return kErrAlign;
+  const size_t units = (size_t)world * channels * rows * (seg / 4);
+  const unsigned blocks = (unsigned)min((size_t)sm_count() * 8, (units + 255) / 256);
+  if (strict)
+    FPB_LAUNCH("group_gather", stream,
+               (group_gather_kernel<true><<<blocks, 256, 0, stream>>>(
+                   src, world, channels, rows, src_ld, seg, cols_mode, dst_hi, dst_lo, dst_ld)));
+  else
+    FPB_LAUNCH("group_gather", stream,
+               (group_gather_kernel<false><<<blocks, 256, 0, stream>>>(
+                   src, world, channels, rows, src_ld, seg, cols_mode, dst_hi, nullptr, dst_ld)));
+  return launch_status();
+}

@@ -374,9 +374,19 @@ class CudaPhases:
         W, n, chunk = shard.world, shard.n, shard.chunk
         G = 128 // W
         dev = ra.device
+        def gather(r, rows, seg, cols_mode, dst_rows, dst_ld):
+            # reorder + hi/lo split (strict) of a received block, one pass
+            out = [torch.empty(G, dst_rows, dst_ld, dtype=r.dtype, device=dev)
+                   for _ in range(2 if self.strict else 1)]
+            _lib.check(self.lib.fpb_trimul_group_gather(
+                r.data_ptr(), W, G, rows, ld, seg, cols_mode, out[0].data_ptr(),
+                out[1].data_ptr() if self.strict else 0, dst_ld, self.p,
+                ops._stream_ptr(dev)), "fpb_trimul_group_gather")
+            return out
+
         if outgoing:
             # A: the row blocks of every rank stacked; B: read as W chunks
-            a_op = self._split(ra.view(W, G, chunk, ld).transpose(0, 1).contiguous())
+            a_op = gather(ra, chunk, ld, 0, W * chunk, ld)
             b_op = self._split(rb)
             geo = dict(m=n, a_rows=W * chunk, nn=n, b_chunk_rows=chunk, b_chunks=W,
                        b_chunk_stride=G * chunk * ld, k=n, ld=ld)
@@ -384,14 +394,8 @@ class CudaPhases:
             # the contraction index k runs over every rank's rows: concatenate
             # the ranks' column blocks
             ldk = int(self.lib.fpb_trimul_plane_ld(W * chunk, self.p))
-
-            def cat(r):
-                t = torch.empty(G, n, ldk, dtype=r.dtype, device=dev)
-                t[:, :, :W * chunk].view(G, n, W, chunk).copy_(
-                    r.view(W, G, n, ld)[..., :chunk].permute(1, 2, 0, 3))
-                return t
-
-            a_op, b_op = self._split(cat(ra)), self._split(cat(rb))
+            a_op = gather(ra, n, chunk, 1, n, ldk)
+            b_op = gather(rb, n, chunk, 1, n, ldk)
             geo = dict(m=n, a_rows=n, nn=n, b_chunk_rows=n, b_chunks=1, b_chunk_stride=0,
                        k=W * chunk, ld=ldk)
         x = torch.empty(W * chunk, (n + 127) // 128, G, 128, dtype=self._dtype(), device=dev)

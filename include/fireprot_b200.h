@@ -219,6 +219,18 @@ int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m, int a_p
                               int b_chunks, size_t b_chunk_stride, int k, int ld, int channels,
                               void* x_blocked, int precision, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
+/* Operand gather of the channel-group exchange: src is the all-to-all
+ * receive buffer [world][channels][rows][src_ld] (FP32 unsplit in strict
+ * mode, BF16 in fast mode); the call writes the contraction operand, split
+ * into hi/lo (strict) or copied (fast) in the same pass:
+ *   cols_mode 0: dst[c][r * rows + i][k]   = src[r][c][i][k], k < seg
+ *                (the ranks' row blocks stacked; dst_ld >= seg)
+ *   cols_mode 1: dst[c][i][r * seg + k]    = src[r][c][i][k], k < seg
+ *                (the ranks' k blocks concatenated; dst_ld >= world * seg)
+ * seg, src_ld and dst_ld are multiples of 4. No reference counterpart. */
+int fpb_trimul_group_gather(const void* src, int world, int channels, int rows, int src_ld,
+                            int seg, int cols_mode, void* dst_hi, void* dst_lo, int dst_ld,
+                            int precision, cudaStream_t stream);
 int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked,
                             const float* ln_in_w, const float* ln_in_b, const float* w_g,
                             const float* ln_out_w, const float* ln_out_b, const float* w_z,

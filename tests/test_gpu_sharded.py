@@ -135,6 +135,42 @@ def test_split_tf32_exact(cuda_device, count, in_place):
     assert torch.equal((hi.double() + lo.double()), x.double())
 
 
+@pytest.mark.parametrize("cols_mode", [0, 1])
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+def test_group_gather_exact(cuda_device, cols_mode, precision):
+    """``fpb_trimul_group_gather``: the stacked (rows) or concatenated (cols)
+    reorder of a received [world][G][rows][ld] block, bit-exact against the
+    same torch reorder, with the strict hi/lo split of every element."""
+    from fireprot_b200 import _lib
+    W, G, R, ld, seg = 4, 8, 40, 64, (64 if cols_mode == 0 else 32)
+    dt = torch.float32 if precision == "strict" else torch.bfloat16
+    g = torch.Generator().manual_seed(5 + cols_mode)
+    src = torch.randn(W, G, R, ld, generator=g).to(dt).to(cuda_device)
+    if cols_mode == 0:
+        ref = src[..., :seg].transpose(0, 1).reshape(G, W * R, seg)
+        dst_rows, dst_ld = W * R, ld
+    else:
+        ref = src[..., :seg].permute(1, 2, 0, 3).reshape(G, R, W * seg)
+        dst_rows, dst_ld = R, W * seg + 4
+    hi = torch.full((G, dst_rows, dst_ld), 7.0, dtype=dt, device=cuda_device)
+    lo = torch.full_like(hi, 7.0) if precision == "strict" else None
+    lib = _lib.load()
+    assert lib.fpb_trimul_group_gather(
+        src.data_ptr(), W, G, R, ld, seg, cols_mode, hi.data_ptr(),
+        0 if lo is None else lo.data_ptr(), dst_ld, 0 if precision == "strict" else 1,
+        torch.cuda.current_stream(cuda_device).cuda_stream) == 0
+    torch.cuda.synchronize(cuda_device)
+    width = ref.shape[-1]
+    assert torch.all(hi[..., width:] == 7.0)  # nothing written past the operand
+    if precision == "strict":
+        got_hi, got_lo = hi[..., :width], lo[..., :width]
+        assert torch.equal(got_hi.view(torch.int32) & 0x1FFF,
+                           torch.zeros_like(got_hi, dtype=torch.int32))
+        assert torch.equal(got_hi.double() + got_lo.double(), ref.double())
+    else:
+        assert torch.equal(hi[..., :width], ref)
+
+
 @pytest.mark.parametrize("world,n,mask_kind", [(2, 100, "random"), (3, 70, "padding"),
                                                (5, 40, "none")])
 def test_sharded_single_block(cuda_device, world, n, mask_kind):

@@ -21,23 +21,34 @@ namespace fpb {
 template <bool kStrict>
 struct TransCfg {
   using R = RowCfg<kStrict>;
-  static constexpr int HC = R::KATOM;          // hidden chunk = one K atom
-  static constexpr int NCH = 512 / HC;         // 16 / 8 chunks
-  static constexpr int G1N = 2 * HC;           // GEMM 1 width (a_c | b_c)
+  // hidden chunk: 64 columns in both modes (two fp32 K atoms / one bf16 atom).
+  // Each chunk pays a fixed latency chain (GEMM-1 commit, TMEM read, SwiGLU,
+  // shared-memory store, barrier round trips), so fewer, wider chunks keep
+  // the tensor pipe busier; GEMM 1 is then N = 128 (cheaper per column than
+  // N = 64 in the TS form).
+  static constexpr int NHA = kStrict ? 2 : 1;  // K atoms of GEMM 2 per chunk
+  static constexpr int HC = NHA * R::KATOM;    // 64
+  static constexpr int NCH = 512 / HC;         // 8 chunks
+  static constexpr int G1N = 2 * HC;           // GEMM 1 width (a_c | b_c) = 128
   static constexpr int G1_STAGE = G1N * 128 * R::NSPLIT;   // bytes of one GEMM-1 W stage
-  static constexpr int G2_STAGE = 128 * 128 * R::NSPLIT;   // bytes of one GEMM-2 W stage
+  static constexpr int G2_STAGE = 128 * 128 * R::NSPLIT;   // bytes of one GEMM-2 W stage (one atom)
   static constexpr int STAGE = G1_STAGE > G2_STAGE ? G1_STAGE : G2_STAGE;
   static constexpr int STAGES = 5;
-  static constexpr int H_BYTES = 128 * 128 * R::NSPLIT;   // one K atom of 128 rows (x2 buffers)
-  // TMEM: A = LN(z) (tf32 hi | lo: 256 columns; bf16 pairs: 64), two
-  // GEMM-1 buffers, the GEMM-2 accumulator (128)
+  static constexpr int H_ATOM = R::NSPLIT * R::ATOM_BYTES;  // one K atom of H (hi | lo)
+  static constexpr int H_BYTES = NHA * H_ATOM;              // one chunk of H
+  // strict: the 512 TMEM columns and 227 KB of shared memory hold one GEMM-1
+  // buffer and one H tile; fast: two of each
+  static constexpr int G1_BUFS = kStrict ? 1 : 2;
+  static constexpr int H_BUFS = kStrict ? 1 : 2;
+  // TMEM: A = LN(z) (tf32 hi | lo: 256 columns; bf16 pairs: 64), the GEMM-1
+  // buffer(s), the GEMM-2 accumulator (128)
   static constexpr uint32_t kA_LO = 128;
   static constexpr uint32_t kG1 = kStrict ? 256 : 64;
-  static constexpr uint32_t kAcc = kG1 + 2 * G1N;
+  static constexpr uint32_t kAcc = kG1 + G1_BUFS * G1N;
   static constexpr int TMEM_COLS = 512;
   static_assert(kAcc + 128 <= TMEM_COLS, "TMEM budget");
   static constexpr int SMEM =
-      tmem_safe_smem(2 * H_BYTES + STAGES * STAGE + 1024 + 256 + 1024, TMEM_COLS);
+      tmem_safe_smem(H_BUFS * H_BYTES + STAGES * STAGE + 1024 + 256 + 1024, TMEM_COLS);
 };
 
 struct TransArgs {
@@ -52,12 +63,14 @@ struct TransArgs {
 
 // One CTA per 128-row tile. The LayerNorm'd tile lives in TMEM (thread t =
 // row t normalises its own row and stores it as the A operand of GEMM 1), so
-// shared memory holds only two SwiGLU tiles H and a 5-stage weight ring:
+// shared memory holds only the SwiGLU tile(s) H and a 5-stage weight ring:
 //   GEMM 1 (chunk c): [a_c | b_c] = A [Wa_c; Wb_c]^T     (A from TMEM)
 //   row threads:      H = silu(a_c) * b_c -> shared memory (A operand)
 //   GEMM 2:           acc += H Wout_c^T
-// with GEMM 1 double-buffered in TMEM so that it runs one chunk ahead, and H
-// double-buffered so that the SwiGLU of chunk c+1 never waits for GEMM 2(c).
+// The MMA warp issues GEMM 1(c+1) once the row threads have read GEMM 1(c)
+// out of TMEM, and GEMM 2(c) once H(c) is written, so the tensor pipe runs
+// GEMM 1(c+1), GEMM 2(c), GEMM 1(c+2), ... while the row threads work on
+// chunk c+1. Fast mode double-buffers GEMM 1 and H as well.
 template <bool kStrict>
 __global__ void __launch_bounds__(192, 1)
     transition_kernel(const __grid_constant__ CUtensorMap w1_hi,
@@ -69,8 +82,8 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* H = smem;                 // [2][H_BYTES]
-  uint8_t* W = H + 2 * C::H_BYTES;
+  uint8_t* H = smem;                 // [H_BUFS][H_BYTES]
+  uint8_t* W = H + C::H_BUFS * C::H_BYTES;
   float* lnp = reinterpret_cast<float*>(W + C::STAGES * C::STAGE);  // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(lnp + 256);
   uint64_t* wfull = bars;
@@ -187,8 +200,8 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
 #pragma unroll 1
     for (int c = 0; c < C::NCH && ok; ++c) {
-      const int b = c & 1;
-      if (!mbar_wait(&g1_full[b], (c >> 1) & 1, g, 31)) {
+      const int b = c % C::G1_BUFS;
+      if (!mbar_wait(&g1_full[b], (c / C::G1_BUFS) & 1, g, 31)) {
         ok = false;
         break;
       }
@@ -204,15 +217,18 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(&g1_free[b]);
-      // H buffer b was read by GEMM 2 of chunk c-2
-      if (c >= 2 && !mbar_wait(&h_free[b], ((c - 2) >> 1) & 1, g, 32)) {
+      // H buffer hb was read by GEMM 2 of chunk c - H_BUFS
+      const int hb = c % C::H_BUFS;
+      if (c >= C::H_BUFS &&
+          !mbar_wait(&h_free[hb], ((c - C::H_BUFS) / C::H_BUFS) & 1, g, 32)) {
         ok = false;
         break;
       }
-      // H row t: one K atom (HC elements)
+      // H row t: HC elements over NHA K atoms
 #pragma unroll
       for (int e = 0; e < C::HC; e += 4) {
-        uint8_t* dst = H + b * C::H_BYTES + sw128_offset(t, e * R::ESZ);
+        uint8_t* dst = H + hb * C::H_BYTES + (e / R::KATOM) * C::H_ATOM +
+                       sw128_offset(t, (e % R::KATOM) * R::ESZ);
         if constexpr (kStrict) {
           float h0, l0, h1, l1, h2, l2, h3, l3;
           split_tf32(hv[e], h0, l0);
@@ -232,7 +248,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&h_full[b]);
+      mbar_arrive(&h_full[hb]);
     }
     if (ok && mbar_wait(done, 0, g, 3)) {
       tc_fence_after();
@@ -271,9 +287,10 @@ __global__ void __launch_bounds__(192, 1)
         if (seq >= C::STAGES && !mbar_wait(&wempty[s], ph ^ 1, g, 33)) return false;
         uint8_t* st = W + s * C::STAGE;
         if (g2) {
+          const int k0 = c * C::HC + atom * R::KATOM;
           mbar_arrive_expect_tx(&wfull[s], C::G2_STAGE);
-          tma_load_3d(st, &w2_hi, &wfull[s], c * C::HC, 0, 0);
-          if constexpr (kStrict) tma_load_3d(st + R::ATOM_BYTES, &w2_lo, &wfull[s], c * C::HC, 0, 0);
+          tma_load_3d(st, &w2_hi, &wfull[s], k0, 0, 0);
+          if constexpr (kStrict) tma_load_3d(st + R::ATOM_BYTES, &w2_lo, &wfull[s], k0, 0, 0);
         } else {
           mbar_arrive_expect_tx(&wfull[s], C::G1_STAGE);
           tma_load_3d(st, &w1_hi, &wfull[s], atom * R::KATOM, c * C::G1N, 0);
@@ -287,7 +304,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int c = 0; c < C::NCH && ok; ++c) {
         if (c + 1 < C::NCH)
           for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, c + 1, a);
-        if (ok) ok = push(true, c, 0);
+        for (int a = 0; a < C::NHA && ok; ++a) ok = push(true, c, a);
       }
       if (g.aborted()) {
         for (int q = (seq > C::STAGES ? seq - C::STAGES : 0); q < seq; ++q)
@@ -311,8 +328,10 @@ __global__ void __launch_bounds__(192, 1)
         ++seq;
       };
       auto gemm1 = [&](int c) -> bool {
-        const int b = c & 1;
-        if (c >= 2 && !mbar_wait(&g1_free[b], ((c - 2) >> 1) & 1, g, 35)) return false;
+        const int b = c % C::G1_BUFS;
+        if (c >= C::G1_BUFS &&
+            !mbar_wait(&g1_free[b], ((c - C::G1_BUFS) / C::G1_BUFS) & 1, g, 35))
+          return false;
         tc_fence_after();
         const uint32_t d = tmem + C::kG1 + b * C::G1N;
         for (int a = 0; a < R::NKA; ++a) {
@@ -343,21 +362,24 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = gemm1(0);
       for (int c = 0; c < C::NCH && ok; ++c) {
         if (c + 1 < C::NCH && !(ok = gemm1(c + 1))) break;
-        const int hb = c & 1;
-        if (!mbar_wait(&h_full[hb], (c >> 1) & 1, g, 37)) {
+        const int hb = c % C::H_BUFS;
+        if (!mbar_wait(&h_full[hb], (c / C::H_BUFS) & 1, g, 37)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t w = take();
-        if (!w) {
-          ok = false;
-          break;
+        for (int a = 0; a < C::NHA && ok; ++a) {
+          const uint32_t w = take();
+          if (!w) {
+            ok = false;
+            break;
+          }
+          const uint32_t h_hi = h0 + hb * C::H_BYTES + a * C::H_ATOM;
+          mma_k_atom<kStrict>(tmem + C::kAcc, h_hi, h_hi + R::ATOM_BYTES, w, w + R::ATOM_BYTES,
+                              id2, c == 0 && a == 0);
+          release();
         }
-        const uint32_t h_hi = h0 + hb * C::H_BYTES;
-        mma_k_atom<kStrict>(tmem + C::kAcc, h_hi, h_hi + R::ATOM_BYTES, w, w + R::ATOM_BYTES, id2,
-                            c == 0);
-        release();
+        if (!ok) break;
         umma_commit(&h_free[hb]);
       }
       if (ok) {

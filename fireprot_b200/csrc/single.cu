@@ -181,10 +181,11 @@ __global__ void single_bias_weights_kernel(const float* __restrict__ ln_w,
 // normalises its row (two passes) and forms its 16 head values: every store
 // is a 32-query coalesced segment of biasT.
 constexpr int kPBRows = 128;
+constexpr int kPBThreads = 2 * kPBRows;  // two threads per row, 8 heads each
 constexpr int kPBStride = 132;  // floats per staged row: 16-byte aligned, no bank conflicts
 constexpr int kPBSmem = (kPBRows * kPBStride + kPBWeights) * 4;
 
-__global__ void __launch_bounds__(kPBRows)
+__global__ void __launch_bounds__(kPBThreads)
     single_pair_bias_kernel(const float* __restrict__ z_loc, const float* __restrict__ mask,
                             int n, int rows, int r0, const float* __restrict__ wfold, float eps,
                             float* __restrict__ biasT) {
@@ -196,24 +197,26 @@ __global__ void __launch_bounds__(kPBRows)
   const int i0 = (blockIdx.x % iblocks) * kPBRows;
   const int cnt = min(kPBRows, rows - i0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int e = tid; e < kPBWeights; e += kPBRows) wp[e] = wfold[e];
-  __syncthreads();  // the folded weights; the only block-wide barrier
-  // warp w: rows [32 w, 32 w + 32), lane = 16-byte chunk of the row
-  const int wr = min(32, cnt - warp * 32);
+  for (int e = tid; e < kPBWeights; e += kPBThreads) wp[e] = wfold[e];
+  // warp w stages rows [16 w, 16 w + 16), lane = 16-byte chunk of the row
+  const int wr = max(0, min(16, cnt - warp * 16));
 #pragma unroll 4
   for (int rr = 0; rr < wr; ++rr) {
-    const int r = warp * 32 + rr;
+    const int r = warp * 16 + rr;
     cp_async16(xs + r * kPBStride + lane * 4,
                z_loc + ((size_t)(i0 + r) * n + j) * 128 + lane * 4);
   }
   cp_async_commit();
-  const int il = i0 + tid;
+  // thread (row, half): heads [8 half, 8 half + 8) of row `row`
+  const int row = tid & (kPBRows - 1), half = tid / kPBRows;
+  constexpr int kHalfHeads = kSHeads / 2;
+  const int il = i0 + row;
   const float mb =
-      (mask && tid < cnt) ? kSMaskInf * (mask[(size_t)(r0 + il) * n + j] - 1.0f) : 0.f;
+      (mask && row < cnt) ? kSMaskInf * (mask[(size_t)(r0 + il) * n + j] - 1.0f) : 0.f;
   cp_async_wait<0>();
-  __syncwarp();
-  if (tid >= cnt) return;
-  const float4* xr = reinterpret_cast<const float4*>(xs + tid * kPBStride);
+  __syncthreads();  // rows staged by other warps; the weights
+  if (row >= cnt) return;
+  const float4* xr = reinterpret_cast<const float4*>(xs + row * kPBStride);
   float sum = 0.f;
 #pragma unroll 8
   for (int c4 = 0; c4 < 32; ++c4) {
@@ -221,9 +224,9 @@ __global__ void __launch_bounds__(kPBRows)
     sum += (x.x + x.y) + (x.z + x.w);
   }
   const float mean = sum * (1.0f / 128.0f);
-  float acc[kSHeads];
+  float acc[kHalfHeads];
 #pragma unroll
-  for (int h = 0; h < kSHeads; ++h) acc[h] = 0.f;
+  for (int h = 0; h < kHalfHeads; ++h) acc[h] = 0.f;
   float var = 0.f;
   const float4* w4 = reinterpret_cast<const float4*>(wp);
 #pragma unroll 2
@@ -234,8 +237,8 @@ __global__ void __launch_bounds__(kPBRows)
     for (int u = 0; u < 4; ++u) {
       var = fmaf(xc[u], xc[u], var);
 #pragma unroll
-      for (int hq = 0; hq < kSHeads / 4; ++hq) {
-        const float4 w = w4[(c4 * 4 + u) * (kSHeads / 4) + hq];
+      for (int hq = 0; hq < kHalfHeads / 4; ++hq) {
+        const float4 w = w4[(c4 * 4 + u) * (kSHeads / 4) + half * (kHalfHeads / 4) + hq];
         acc[hq * 4 + 0] = fmaf(xc[u], w.x, acc[hq * 4 + 0]);
         acc[hq * 4 + 1] = fmaf(xc[u], w.y, acc[hq * 4 + 1]);
         acc[hq * 4 + 2] = fmaf(xc[u], w.z, acc[hq * 4 + 2]);
@@ -246,8 +249,10 @@ __global__ void __launch_bounds__(kPBRows)
   const float rs = rsqrtf(var * (1.0f / 128.0f) + eps);
   const float* bp = wp + 128 * kSHeads;
 #pragma unroll
-  for (int h = 0; h < kSHeads; ++h)
-    biasT[((size_t)h * n + j) * rows + il] = fmaf(rs, acc[h], bp[h]) + mb;
+  for (int hh = 0; hh < kHalfHeads; ++hh) {
+    const int h = half * kHalfHeads + hh;
+    biasT[((size_t)h * n + j) * rows + il] = fmaf(rs, acc[hh], bp[h]) + mb;
+  }
 }
 
 // ---------------------------------------------------------------- attention
@@ -500,7 +505,7 @@ extern "C" int fpb_single_block(float* s, const float* z_loc, const float* mask,
     cudaFuncSetAttribute(single_pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kPBSmem);
     FPB_LAUNCH("single_pair_bias", stream,
-               (single_pair_bias_kernel<<<(unsigned)blocks, kPBRows, kPBSmem, stream>>>(
+               (single_pair_bias_kernel<<<(unsigned)blocks, kPBThreads, kPBSmem, stream>>>(
                    z_loc, mask, n, rows, r0, pl.wfold, eps, pl.biasT)));
   }
   FPB_LAUNCH("single_attn", stream,

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long rows = p.n_rows;
-  const long long p0 = (long long)blockIdx.x * 128;
+  const int ntiles = (int)((rows + 127) / 128);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -140,7 +140,47 @@ __global__ void __launch_bounds__(192, 1)
   if (warp < 4) {
     const int t = warp * 32 + lane;
     const uint32_t lrow = tmem + ((uint32_t)(warp * 32) << 16);  // this thread's TMEM lane
-    const long long pr = p0 + t;
+    // residual epilogue of a finished tile (thread t owns its row pr)
+    auto epilogue = [&](long long pr, int it_done) -> bool {
+      if (!mbar_wait(done, it_done & 1, g, 3)) return false;
+      tc_fence_after();
+      const long long rsafe = pr < rows ? pr : 0;
+      float4* zrow = reinterpret_cast<float4*>(p.z) + rsafe * 32;
+      float4* drow = p.delta ? reinterpret_cast<float4*>(p.delta) + rsafe * 32 : zrow;
+      const bool residual = p.delta == nullptr;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float4 zc[8];
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4)
+          zc[v4] = (residual && pr < rows) ? zrow[cc * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float yv[32];
+        tmem_row32(tmem + C::kAcc, warp, cc * 32, yv);
+        if (pr < rows) {
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            float4 o = zc[v4];
+            o.x += yv[4 * v4];
+            o.y += yv[4 * v4 + 1];
+            o.z += yv[4 * v4 + 2];
+            o.w += yv[4 * v4 + 3];
+            drow[cc * 8 + v4] = o;
+          }
+        }
+      }
+      tc_fence_before();  // acc read before the next tile's GEMM 2 writes it
+      return true;
+    };
+    bool ok = true;
+    int it = 0;
+    long long pprev = 0;
+    // persistent: tiles blockIdx.x, + gridDim.x, ... Per tile: LayerNorm into
+    // A (free once GEMM 1 of the previous tile's last chunk has retired, which
+    // this thread has waited for), the previous tile's epilogue (while GEMM 1
+    // of this tile runs), then the SwiGLU chunks
+#pragma unroll 1
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+    const long long pr = (long long)tile * 128 + t;
     {
       // ---- A = LN(z row t) into TMEM: one row per thread, all loads first
       float x[128];
@@ -197,11 +237,15 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(a_full);
     }
-    bool ok = true;
+    if (it > 0 && !epilogue(pprev, it - 1)) {
+      ok = false;
+      break;
+    }
 #pragma unroll 1
     for (int c = 0; c < C::NCH && ok; ++c) {
-      const int b = c % C::G1_BUFS;
-      if (!mbar_wait(&g1_full[b], (c / C::G1_BUFS) & 1, g, 31)) {
+      const int cg = it * C::NCH + c;  // chunk index over this CTA's tiles
+      const int b = cg % C::G1_BUFS;
+      if (!mbar_wait(&g1_full[b], (cg / C::G1_BUFS) & 1, g, 31)) {
         ok = false;
         break;
       }
@@ -218,9 +262,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&g1_free[b]);
       // H buffer hb was read by GEMM 2 of chunk c - H_BUFS
-      const int hb = c % C::H_BUFS;
-      if (c >= C::H_BUFS &&
-          !mbar_wait(&h_free[hb], ((c - C::H_BUFS) / C::H_BUFS) & 1, g, 32)) {
+      const int hb = cg % C::H_BUFS;
+      if (cg >= C::H_BUFS &&
+          !mbar_wait(&h_free[hb], ((cg - C::H_BUFS) / C::H_BUFS) & 1, g, 32)) {
         ok = false;
         break;
       }
@@ -250,33 +294,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&h_full[hb]);
     }
-    if (ok && mbar_wait(done, 0, g, 3)) {
-      tc_fence_after();
-      const long long rsafe = pr < rows ? pr : 0;
-      float4* zrow = reinterpret_cast<float4*>(p.z) + rsafe * 32;
-      float4* drow = p.delta ? reinterpret_cast<float4*>(p.delta) + rsafe * 32 : zrow;
-      const bool residual = p.delta == nullptr;
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        float4 zc[8];
-#pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4)
-          zc[v4] = (residual && pr < rows) ? zrow[cc * 8 + v4] : make_float4(0.f, 0.f, 0.f, 0.f);
-        float yv[32];
-        tmem_row32(tmem + C::kAcc, warp, cc * 32, yv);
-        if (pr < rows) {
-#pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4) {
-            float4 o = zc[v4];
-            o.x += yv[4 * v4];
-            o.y += yv[4 * v4 + 1];
-            o.z += yv[4 * v4 + 2];
-            o.w += yv[4 * v4 + 3];
-            drow[cc * 8 + v4] = o;
-          }
-        }
-      }
-    }
+      pprev = pr;
+    }  // tiles
+    if (ok && it > 0) (void)epilogue(pprev, it - 1);
   } else if (warp == 4) {
     if (lane == 0) {
       int seq = 0;
@@ -300,11 +320,13 @@ __global__ void __launch_bounds__(192, 1)
         ++seq;
         return true;
       };
-      for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, 0, a);
-      for (int c = 0; c < C::NCH && ok; ++c) {
-        if (c + 1 < C::NCH)
-          for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, c + 1, a);
-        for (int a = 0; a < C::NHA && ok; ++a) ok = push(true, c, a);
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, 0, a);
+        for (int c = 0; c < C::NCH && ok; ++c) {
+          if (c + 1 < C::NCH)
+            for (int a = 0; a < R::NKA && ok; ++a) ok = push(false, c + 1, a);
+          for (int a = 0; a < C::NHA && ok; ++a) ok = push(true, c, a);
+        }
       }
       if (g.aborted()) {
         for (int q = (seq > C::STAGES ? seq - C::STAGES : 0); q < seq; ++q)
@@ -357,13 +379,17 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(&g1_full[b]);
         return true;
       };
-      bool ok = mbar_wait(a_full, 0, g, 36);
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int cb = it * C::NCH;  // first chunk index of this tile
+      ok = mbar_wait(a_full, it & 1, g, 36);
       if (ok) tc_fence_after();
-      if (ok) ok = gemm1(0);
+      if (ok) ok = gemm1(cb);
       for (int c = 0; c < C::NCH && ok; ++c) {
-        if (c + 1 < C::NCH && !(ok = gemm1(c + 1))) break;
-        const int hb = c % C::H_BUFS;
-        if (!mbar_wait(&h_full[hb], (c / C::H_BUFS) & 1, g, 37)) {
+        if (c + 1 < C::NCH && !(ok = gemm1(cb + c + 1))) break;
+        const int hb = (cb + c) % C::H_BUFS;
+        if (!mbar_wait(&h_full[hb], ((cb + c) / C::H_BUFS) & 1, g, 37)) {
           ok = false;
           break;
         }
@@ -382,9 +408,9 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
         umma_commit(&h_free[hb]);
       }
-      if (ok) {
-        umma_commit(done);
-      } else {
+      if (ok) umma_commit(done);
+      }  // tiles
+      if (!ok) {
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
       }
@@ -507,16 +533,17 @@ extern "C" int fpb_transition(float* z, float* delta_out, long long rows, int c_
   if (!ok) return kErrArg;
   TransArgs ta{z, delta_out, (int)rows, eps, ln_w, ln_b, static_cast<int*>(workspace)};
   const unsigned tiles = (unsigned)((rows + 127) / 128);
+  const unsigned grid = tiles < (unsigned)sm_count() ? tiles : (unsigned)sm_count();
   if (strict) {
     auto k = transition_kernel<true>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
     FPB_LAUNCH("transition", stream,
-               k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
+               k<<<grid, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   } else {
     auto k = transition_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
     FPB_LAUNCH("transition", stream,
-               k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
+               k<<<grid, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   }
   return launch_status();
 }
@@ -610,14 +637,15 @@ extern "C" int fpb_transition_noalloc(float* z, float* delta_out, long long rows
   if (!ok) return kErrArg;
   TransArgs ta{z, delta_out, (int)rows, eps, ln_w, ln_b, static_cast<int*>(scratch)};
   const unsigned tiles = (unsigned)((rows + 127) / 128);
+  const unsigned grid = tiles < (unsigned)sm_count() ? tiles : (unsigned)sm_count();
   if (strict) {
     auto k = transition_kernel<true>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
-    k<<<tiles, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+    k<<<grid, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
   } else {
     auto k = transition_kernel<false>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
-    k<<<tiles, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
+    k<<<grid, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
   }
   if ((st = launch_status())) return st;
   if (status_out) {

@@ -120,6 +120,13 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // ---------------------------------------------------------------- TMA
+// Bring `bytes` (a multiple of 128) starting at p into L2, one line per
+// instruction; no registers are held for the data.
+__device__ __forceinline__ void prefetch_l2(const void* p, int bytes) {
+  const char* c = static_cast<const char*>(p);
+  for (int o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -1065,6 +1065,12 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll 1
     for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
       const int r = tile / njb, s0 = (tile % njb) * 128;
+      // this row's o into L2 now: its chunks are read one at a time after
+      // GEMM 1, each a dependent global load
+      if (s0 + t < n)
+        prefetch_l2(static_cast<const uint8_t*>(p.o) +
+                        ((long long)r * n + s0 + t) * 128 * (kStrict ? 4 : 2),
+                    128 * (kStrict ? 4 : 2));
       // A is free once GEMM 2 of the previous tile has read it
       if (it > 0 && !mbar_wait(g2_done, (it - 1) & 1, g, 5)) break;
       if constexpr (kStrict) {
@@ -1164,6 +1170,7 @@ __global__ void __launch_bounds__(320, 1)
           kTrans ? (long long)(valid ? s0 + t : 0) * n + r : (long long)r * n + (valid ? s0 + t : 0);
       float4* zrow = reinterpret_cast<float4*>(p.z) + zrow_idx * 32;
       float4* drow = residual ? zrow : reinterpret_cast<float4*>(p.delta) + zrow_idx * 32;
+      if (valid && residual) prefetch_l2(zrow, 512);  // the residual row, read chunk by chunk
       float4 zc[8];
 #pragma unroll
       for (int v4 = 0; v4 < 8; ++v4)

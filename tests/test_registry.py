@@ -125,7 +125,8 @@ def test_process_registry_is_shared():
     assert get_registry() is get_registry()
 
 
-REFERENCE = Path(os.environ.get("FIREPROT_REFERENCE", "/root/reference")) / "python"
+REFERENCE = Path(os.environ.get("FIREPROT_REFERENCE",
+                                Path(__file__).resolve().parents[1].parent / "reference")) / "python"
 
 
 @pytest.mark.skipif(not (REFERENCE / "fireprot/ops/registry.py").exists(),

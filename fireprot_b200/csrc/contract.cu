@@ -279,17 +279,17 @@ int launch_contract(const ContractOperands& op, const ContractArgs& args_in, cud
   if (strict) {
     auto k = contract_kernel<true, float>;
     const int smem = ContractCfg<true>::SMEM_BYTES;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (int smem_st = set_max_smem(k, smem)) return smem_st;
     FPB_LAUNCH("contract_strict", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
   } else {
     const int smem = ContractCfg<false>::SMEM_BYTES;
     if (args.out_bf16) {
       auto k = contract_kernel<false, __nv_bfloat16>;
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (int smem_st = set_max_smem(k, smem)) return smem_st;
       FPB_LAUNCH("contract_fast", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
     } else {
       auto k = contract_kernel<false, float>;
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (int smem_st = set_max_smem(k, smem)) return smem_st;
       FPB_LAUNCH("contract_fast", stream, k<<<grid, 192, smem, stream>>>(mah, mal, mbh, mbl, args));
     }
   }

@@ -112,4 +112,17 @@ inline int launch_status() {
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
+// Opt a kernel in to `bytes` of dynamic shared memory; a refusal is returned
+// as kErrCuda (with the CUDA error cleared) instead of surfacing later as a
+// less specific launch failure.
+template <class Kernel>
+inline int set_max_smem(Kernel k, int bytes) {
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return kErrCuda;
+  }
+  return kOk;
+}
+
 }  // namespace fpb

@@ -502,8 +502,7 @@ extern "C" int fpb_single_block(float* s, const float* z_loc, const float* mask,
   {
     const long long blocks = (long long)n * ((rows + kPBRows - 1) / kPBRows);
     if (blocks > 0x7fffffffll) return kErrShape;
-    cudaFuncSetAttribute(single_pair_bias_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kPBSmem);
+    if (int smem_st = set_max_smem(single_pair_bias_kernel, kPBSmem)) return smem_st;
     FPB_LAUNCH("single_pair_bias", stream,
                (single_pair_bias_kernel<<<(unsigned)blocks, kPBThreads, kPBSmem, stream>>>(
                    z_loc, mask, n, rows, r0, pl.wfold, eps, pl.biasT)));

@@ -536,12 +536,12 @@ extern "C" int fpb_transition(float* z, float* delta_out, long long rows, int c_
   const unsigned grid = tiles < (unsigned)sm_count() ? tiles : (unsigned)sm_count();
   if (strict) {
     auto k = transition_kernel<true>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
+    if (int smem_st = set_max_smem(k, TransCfg<true>::SMEM)) return smem_st;
     FPB_LAUNCH("transition", stream,
                k<<<grid, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   } else {
     auto k = transition_kernel<false>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
+    if (int smem_st = set_max_smem(k, TransCfg<false>::SMEM)) return smem_st;
     FPB_LAUNCH("transition", stream,
                k<<<grid, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta));
   }
@@ -564,26 +564,19 @@ constexpr size_t kTransitionScratchBytes = FPB_TRANSITION_SCRATCH_BYTES;
 // it on its own stream before its first kernel.
 static __device__ __align__(256) unsigned char g_transition_scratch[kTransitionScratchBytes];
 
-constexpr int kMaxScratchDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxScratchDevices];  // device address of the array, per device
-
-// Device address of this device's scratch, looked up once per device with
-// that device current (the first call per device does the lookup).
+// Device address of the array in the current device's current context. The
+// name g_transition_scratch is a host-side stand-in in host code, so the
+// address is looked up, and it is looked up on every call: a cached value
+// would outlive a cudaDeviceReset or belong to another context made current
+// on the same device. The lookup is a host-side query (no stream work); the
+// first one on a device may load this library's device code there.
 int transition_scratch(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
-  if (dev < 0 || dev >= kMaxScratchDevices) return kErrArg;
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_transition_scratch) != cudaSuccess || p == nullptr) {
-      cudaGetLastError();
-      return kErrCuda;
-    }
-    g_scratch_ptr[dev] = p;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_transition_scratch) != cudaSuccess || p == nullptr) {
+    cudaGetLastError();
+    return kErrCuda;
   }
-  *out = g_scratch_ptr[dev];
+  *out = p;
   return kOk;
 }
 
@@ -603,6 +596,15 @@ extern "C" int fpb_transition_noalloc(float* z, float* delta_out, long long rows
   const size_t need = fpb_transition_workspace_size(c_z, expansion, precision);
   if (need == 0) return kErrShape;
   if (need > kTransitionScratchBytes) return kErrScratch;
+  if (status_out) {
+    // reporting the status waits for the stream, which a capture forbids
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+      cudaGetLastError();
+      return kErrCuda;
+    }
+    if (cap != cudaStreamCaptureStatusNone) return kErrArg;
+  }
   void* scratch = nullptr;
   int st = transition_scratch(&scratch);
   if (st) return st;
@@ -640,11 +642,11 @@ extern "C" int fpb_transition_noalloc(float* z, float* delta_out, long long rows
   const unsigned grid = tiles < (unsigned)sm_count() ? tiles : (unsigned)sm_count();
   if (strict) {
     auto k = transition_kernel<true>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<true>::SMEM);
+    if (int smem_st = set_max_smem(k, TransCfg<true>::SMEM)) return smem_st;
     k<<<grid, 192, TransCfg<true>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
   } else {
     auto k = transition_kernel<false>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TransCfg<false>::SMEM);
+    if (int smem_st = set_max_smem(k, TransCfg<false>::SMEM)) return smem_st;
     k<<<grid, 192, TransCfg<false>::SMEM, stream>>>(m1h, m1l, m2h, m2l, ta);
   }
   if ((st = launch_status())) return st;

@@ -941,13 +941,13 @@ int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const
   dim3 grid((n + 127) / 128, kHeads, rows);
   if (strict) {
     auto k = attn_core_kernel<true>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<true>::SMEM);
+    if (int smem_st = set_max_smem(k, AttnCfg<true>::SMEM)) return smem_st;
     FPB_LAUNCH("triattn_core", stream,
                k<<<grid, AttnCfg<true>::THREADS, AttnCfg<true>::SMEM, stream>>>(
                    mqh, mql, mkh, mkl, mvh, mvl, args));
   } else {
     auto k = attn_core_kernel<false>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg<false>::SMEM);
+    if (int smem_st = set_max_smem(k, AttnCfg<false>::SMEM)) return smem_st;
     FPB_LAUNCH("triattn_core", stream,
                k<<<grid, AttnCfg<false>::THREADS, AttnCfg<false>::SMEM, stream>>>(
                    mqh, mql, mkh, mkl, mvh, mvl, args));
@@ -1338,7 +1338,7 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
   const int smem = strict ? attn_proj_smem_bytes<true>() : attn_proj_smem_bytes<false>();
   auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
                   : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (int smem_st = set_max_smem(k, smem)) return smem_st;
   FPB_LAUNCH("triattn_proj", stream, k<<<grid, 320, smem, stream>>>(mph, mpl, zm, pa));
   return launch_status();
 }
@@ -1379,7 +1379,7 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
   const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
   auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
                   : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (int smem_st = set_max_smem(k, smem)) return smem_st;
   FPB_LAUNCH("triattn_out", stream, k<<<grid, 320, smem, stream>>>(moh, mol, zm, oa));
   return launch_status();
 }

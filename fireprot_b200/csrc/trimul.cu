@@ -637,7 +637,7 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
                   : (transposed ? trimul_proj_kernel<false, true>
                                 : trimul_proj_kernel<false, false>);
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (int smem_st = set_max_smem(k, smem)) return smem_st;
   FPB_LAUNCH("trimul_proj", stream,
              k<<<grid, 320, smem, stream>>>(mph, mpl, zm, pa));
   return launch_status();
@@ -658,7 +658,7 @@ int trimul_finish_run(float* z_loc, int n, int rows, const void* x_blocked, cons
                    add ? 1 : 0, status, out_tiles};
   const int smem = strict ? out_smem_bytes<true>() : out_smem_bytes<false>();
   auto k = strict ? trimul_out_kernel<true> : trimul_out_kernel<false>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (int smem_st = set_max_smem(k, smem)) return smem_st;
   const unsigned grid = (unsigned)min(out_tiles, sm_count());
   FPB_LAUNCH("trimul_out", stream, k<<<grid, 192, smem, stream>>>(moh, mol, oa));
   return launch_status();

@@ -1,3 +1,31 @@
+# Portions of this file (the source-pinned scope `attention_scope`, the
+# dispatcher call contract in `contract_ok` and `AttentionDispatcher.__call__`)
+# follow FireProt's OpenFold3 adapter, python/fireprot/adapters/openfold3/
+# attention.py, which carries this notice:
+#
+#   Copyright 2026 AlQuraishi Laboratory
+#   Copyright 2026 Outpace Bio, Inc.
+#   Copyright 2026 Advanced Micro Devices, Inc.
+#   Copyright 2025 NVIDIA Corporation
+#   Copyright 2021 DeepMind Technologies Limited
+#
+#   Licensed under the Apache License, Version 2.0 (the "License");
+#   you may not use this file except in compliance with the License.
+#   You may obtain a copy of the License at
+#
+#       http://www.apache.org/licenses/LICENSE-2.0
+#
+#   Unless required by applicable law or agreed to in writing, software
+#   distributed under the License is distributed on an "AS IS" BASIS,
+#   WITHOUT WARRANTIES OR CONDITIONS OF ANY KIND, either express or implied.
+#   See the License for the specific language governing permissions and
+#   limitations under the License.
+#
+# Modified here: the scope dispatches to the B200 attention core
+# (fpb_attention_core) instead of a HIP softmax, the installation is an
+# object with explicit arm/disarm, and the device contract accepts any N.
+# This file, including these modifications, is Apache-2.0.
+
 """OpenFold3 ``_attention`` scope for the B200 backend.
 
 The reference's OpenFold3 ``hip_fused`` worker replaces

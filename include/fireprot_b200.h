@@ -120,16 +120,23 @@ int fpb_transition(float* z, float* delta_out, long long rows, int c_z, int expa
  * The scratch (packed weights plus the 256-byte status word) is a static
  * device array of this library, FPB_TRANSITION_SCRATCH_BYTES per device; a
  * request needing more is rejected with status 8. Nothing else is allocated.
- *  - The first call on each device, with that device current, looks up the
- *    array's device address; make that first call before any stream
- *    capture that would include this function.
+ *  - Every call looks up the array's device address in the current device's
+ *    current context (the address is per context, so it is never cached).
+ *    The first call on a device may load the library's device code there:
+ *    make that first call before any stream capture that would include
+ *    this function.
  *  - Each call zeroes the status word on `stream` before its kernels (the
  *    only part that must start at zero) and overwrites the packed weights.
  *  - Calls on one device share the array: calls that can overlap (several
  *    streams or threads on one device) race and must be serialised by the
  *    caller, e.g. by issuing them on one stream.
  *  - status_out (nullable host pointer): when given, the call waits for
- *    `stream` and stores the device status word (0 = every wait completed).
+ *    `stream` and stores the device status word (0 = every wait completed,
+ *    else 6000 + site of a device-side wait that timed out). Waiting is
+ *    illegal while `stream` is being captured, so a non-null status_out on a
+ *    capturing stream is rejected with status 4. With status_out null the
+ *    call never reports a device-side timeout: the word stays in the static
+ *    array, which the caller cannot read through this API.
  * Arguments otherwise as fpb_transition; z, the weights and `stream` belong
  * to the current device. */
 #define FPB_TRANSITION_SCRATCH_BYTES (2u << 20)

@@ -113,3 +113,67 @@ def test_noalloc_rejects_bad_requests(cuda_device):
     assert lib.fpb_transition_noalloc(z.data_ptr(), 0, ROWS, 128, 4, *_ptrs(w), 1e-5, 7,
                                       ctypes.byref(st), stream) == 4
     assert lib.fpb_status_string(8).decode() == "request exceeds the static scratch capacity"
+    # a null input or weight -> invalid argument (4)
+    assert lib.fpb_transition_noalloc(0, 0, ROWS, 128, 4, *_ptrs(w), 1e-5, 0,
+                                      ctypes.byref(st), stream) == 4
+    bad = _ptrs(w)
+    bad[2] = 0
+    assert lib.fpb_transition_noalloc(z.data_ptr(), 0, ROWS, 128, 4, *bad, 1e-5, 0,
+                                      ctypes.byref(st), stream) == 4
+    # z or delta_out off a 16-byte boundary -> misaligned (3)
+    assert lib.fpb_transition_noalloc(z.data_ptr() + 4, 0, ROWS - 1, 128, 4, *_ptrs(w), 1e-5,
+                                      0, ctypes.byref(st), stream) == 3
+    d = torch.zeros(ROWS, 128, device=cuda_device)
+    assert lib.fpb_transition_noalloc(z.data_ptr(), d.data_ptr() + 4, ROWS - 1, 128, 4,
+                                      *_ptrs(w), 1e-5, 0, ctypes.byref(st), stream) == 3
+    # no rows -> unsupported shape (2)
+    assert lib.fpb_transition_noalloc(z.data_ptr(), 0, 0, 128, 4, *_ptrs(w), 1e-5, 0,
+                                      ctypes.byref(st), stream) == 2
+    torch.cuda.synchronize(cuda_device)
+    assert torch.count_nonzero(z).item() == 0 and torch.count_nonzero(d).item() == 0
+
+
+def test_noalloc_status_out_refused_while_capturing(cuda_device):
+    """Reporting the status waits for the stream, which a capture forbids:
+    the call is refused before it enqueues anything."""
+    lib = _lib.load()
+    z = torch.zeros(ROWS, 128, device=cuda_device)
+    w = _weights(2, cuda_device)
+    x = torch.zeros(4, device=cuda_device)
+    side = torch.cuda.Stream(cuda_device)
+    graph = torch.cuda.CUDAGraph()
+    st = ctypes.c_int(-1)
+    rcs = []
+    torch.cuda.synchronize(cuda_device)
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        x.add_(1.0)
+        rcs.append(lib.fpb_transition_noalloc(z.data_ptr(), 0, ROWS, 128, 4, *_ptrs(w), 1e-5, 0,
+                                              ctypes.byref(st), side.cuda_stream))
+        graph.capture_end()
+    assert rcs == [4]
+    assert st.value == -1
+    graph.replay()
+    torch.cuda.synchronize(cuda_device)
+    assert x.tolist() == [1.0] * 4
+    assert torch.count_nonzero(z).item() == 0
+    del graph
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs a second GPU")
+def test_noalloc_second_device():
+    """Each device has its own array; a call on device 1 after one on device
+    0 uses device 1's copy and matches the workspace entry point there."""
+    lib = _lib.load()
+    for dev_index in (0, 1):
+        dev = torch.device("cuda", dev_index)
+        with torch.cuda.device(dev):
+            g = torch.Generator().manual_seed(40 + dev_index)
+            z = torch.randn(ROWS, 128, generator=g).to(dev)
+            w = _weights(30 + dev_index, dev)
+            ref = z.clone()
+            _reference(lib, ref, None, w, 0, dev)
+            out = z.clone()
+            _noalloc(lib, out, None, w, 0, dev)
+            assert _rel(out, ref) <= TOL

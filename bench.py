@@ -79,8 +79,49 @@ def kernel_flops(name: str, n: int) -> float:
     }.get(name, 0.0)
 
 
+_TF32 = {}
+
+
+def measure_tf32_tflops(device) -> float | None:
+    """Dense TF32 tensor-core rate of this GPU, measured once: cuBLAS
+    (torch.matmul with TF32 allowed) on 8192^3 FP32 operands, best of 10
+    launches timed with CUDA events after 3 warm-up launches (2 N^3 FLOPs
+    each). MEASURED_PEAKS.json holds the BF16 figure only."""
+    key = str(device)
+    if key in _TF32:
+        return _TF32[key]
+    val = None
+    try:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        n = 8192
+        a = torch.randn(n, n, device=device)
+        b = torch.randn(n, n, device=device)
+        c = torch.empty(n, n, device=device)
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        val = 2.0 * n ** 3 / (best / 1e3) / 1e12
+        del a, b, c
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    except Exception:
+        val = None
+    _TF32[key] = val
+    return val
+
+
 def peaks(precision: str):
-    """Tensor peak (TFLOP/s) and HBM (GB/s) used as roofline denominators."""
+    """Tensor peak (TFLOP/s) and HBM (GB/s) used as roofline denominators:
+    strict (3xTF32, three TF32 MMAs per product) = the TF32 rate measured
+    live on this GPU / 3; fast = the BF16 burst figure of
+    MEASURED_PEAKS.json."""
     src = "MEASURED_PEAKS.json"
     try:
         mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -88,8 +129,11 @@ def peaks(precision: str):
     except Exception:
         bf16, hbm, src = 1590.0, 6650.0, "fallback"
     if precision == "strict":
-        # tf32 = bf16 / 2 (not measured); 3xTF32 issues three tf32 MMAs per product
-        return bf16 / 6.0, hbm, f"{src} bf16 {bf16} / 2 (tf32) / 3 (3xTF32), of measured"
+        tf32 = next(iter(_TF32.values()), None)
+        if tf32:
+            return tf32 / 3.0, hbm, (f"tf32 {tf32:.1f} TFLOP/s measured live (cuBLAS 8192^3, "
+                                     f"best of 10) / 3 (3xTF32), of measured")
+        return bf16 / 6.0, hbm, f"{src} bf16 {bf16} / 2 (tf32, assumed) / 3 (3xTF32)"
     return bf16, hbm, f"{src} bf16 {bf16}, of measured"
 
 
@@ -188,25 +232,48 @@ def max_over_ranks(x: float, world: int, device) -> float:
 # reference arm: the native math on host cores (oracle port)
 # ---------------------------------------------------------------------------
 def run_reference(args, world, rank):
+    """The native math on the host cores: exactly ONE whole block at the
+    bench's size, every stage in full (no sampling, no scaling), its ordered
+    work items split over the K timed steps; value = 1 block / the summed
+    step times. The W warm-up steps each run a whole small block (N=96)."""
     if rank != 0:
         return None
-    from oracle.cpu_baseline import sampled_block_seconds
-    secs = []
-    sample = threads = None
-    for i in range(args.warmup + args.steps):
-        tot, _, sample, threads = sampled_block_seconds(args.n, args.valid, row_sample=8,
-                                                        chan_sample=4, seed=i)
-        if i >= args.warmup:
-            secs.append(tot)
-    mean = statistics.mean(secs)
-    value = 1.0 / mean
+    from oracle.cpu_baseline import FullBlock
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            warm = FullBlock(96, 90)
+            for _, _, fn in warm.items:
+                fn()
+        fb = FullBlock(args.n, args.valid)
+        step_s, stage_s = [], {}
+        for group in fb.steps(max(1, args.steps)):
+            t0 = time.perf_counter()
+            for label, _, fn in group:
+                t1 = time.perf_counter()
+                fn()
+                key = label.split("[")[0]
+                stage_s[key] = stage_s.get(key, 0.0) + time.perf_counter() - t1
+            step_s.append(time.perf_counter() - t0)
+        if not torch.isfinite(fb.z).all() or not torch.isfinite(fb.s).all():
+            raise RuntimeError("non-finite CPU block result")
+    block_s = sum(step_s)
+    value = 1.0 / block_s
+    sample = (f"one whole Pairformer block at N={args.n} (pair and single stacks, valid "
+              f"{args.valid}), every stage in full (no sampling or scaling), its ordered work "
+              f"items split over the {len(step_s)} timed steps; torch fp32 on {threads} host "
+              f"threads")
     return {
         "metric": METRIC, "value": value, "unit": "blocks/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": block_s / len(step_s) * 1e3,
         "higher_is_better": True,
         "scaling": "strong" if args.gpus > 1 and args.mode == "sharded" else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": _config(args),
+        "seconds_per_block": round(block_s, 3),
+        "stage_seconds": {k: round(v, 3) for k, v in stage_s.items()},
         "cpu_baseline": {"value": value, "unit": "blocks/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "blocks/s", "h2d_bytes_per_step": 0,
@@ -238,6 +305,58 @@ def _trimul_scheme(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def _kernel_table(kernels: dict, n: int, rows_frac: float) -> dict:
+    """Per-kernel launches, average device ms, share of the summed kernel
+    time and achieved TFLOP/s (algorithmic FLOPs of a launch / its average)."""
+    total = max(1e-9, sum(r["total_ms"] for r in kernels.values()))
+    out = {}
+    for name, rec in kernels.items():
+        avg = rec["total_ms"] / rec["launches"]
+        fl = kernel_flops(name, n) * rows_frac
+        out[name] = {"launches": rec["launches"], "avg_ms": round(avg, 4),
+                     "share": round(rec["total_ms"] / total, 4),
+                     "tflops": round(fl / (avg / 1e3) / 1e12, 2) if fl else None}
+    return out
+
+
+def block_parity(block, z_host, s_host, mask_host, valid, precision, dev):
+    """Line-sampled parity of one block at the bench's size (CPU leg): the
+    block from the bench's initial inputs runs one operator at a time on the
+    GPU (the timed kernels), and the oracle recomputes 16+ lines of every
+    operator's result from the GPU's own input to it. Returns the largest
+    output-scale relative errors per operator."""
+    from oracle import block_check as BC
+    from oracle import pairformer_oracle as O
+    pair = {name: getattr(block.pair, name).weight_dict() for name in BC.PAIR_OPERATORS}
+    p, ps = BC.params_from_weights(pair, block.single.weight_dict())
+    n = z_host.shape[0]
+    lines = O.sample_lines(n, count=12, seed=7, valid=valid)
+    z_in = z_host.float().clone()
+    s_in = s_host.float().clone()
+    mask = mask_host.float()
+    zd, sd = z_in.to(dev), s_in.to(dev)
+    errs = {}
+    with torch.no_grad():
+        for name, t in block.forward_by_operator(sd, zd, mask.to(dev), precision=precision):
+            if name == "single":
+                errs[name] = BC.check_single(s_in, t.cpu(), z_in, mask, ps, lines)
+            else:
+                z_out = t.cpu()
+                errs[name] = BC.check_pair_operator(name, z_in, z_out, mask, p, lines)
+                z_in = z_out
+    del zd, sd
+    tol = O.STRICT_TOL if precision == "strict" else O.FAST_TOL
+    worst = max(e["out"] for e in errs.values())
+    return {"lines": len(lines), "max_rel_err": worst,
+            "max_rel_err_update": max(e["update"] for e in errs.values()),
+            "tolerance": tol, "pass": bool(worst <= tol),
+            "per_operator": {k: {kk: float(f"{vv:.3g}") for kk, vv in v.items()}
+                             for k, v in errs.items()},
+            "how": ("one block from the bench's initial z and s, one operator at a time on "
+                    "the GPU; 16+ lines (rows; columns for the ending node) of each "
+                    "operator's result recomputed by the CPU oracle from the GPU's input to "
+                    "it; error = max|gpu - oracle| / max|oracle|")}
+
 def run_ours(args, world, rank, local):
     from fireprot_b200 import ops
     from fireprot_b200.modules import PairformerBlock
@@ -309,6 +428,9 @@ def run_ours(args, world, rank, local):
 
     def step(zz):
         step_fn(zz, s_dev, mask)
+
+    if args.precision == "strict":
+        measure_tf32_tflops(dev)
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -410,18 +532,23 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize(dev)
         fast_check()
         barrier(world)
+        torch.cuda.synchronize(dev)
+        ops.timing_enable(True)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         for _ in range(args.steps):
             fast_step(zf, sf, mask)
         g1.record(stream)
         torch.cuda.synchronize(dev)
+        fast_kernels = ops.timing_collect()
+        ops.timing_enable(False)
         fms = max_over_ranks(g0.elapsed_time(g1), world, dev) / args.steps
         pf, _, _ = peaks("fast")
         side = {"precision": "fast", "value": blocks_per_step * 1e3 / fms, "unit": "blocks/s",
                 "ms_per_step": fms,
                 "tc_frac_block": blocks_per_step * block_flops(n) / (fms / 1e3) / 1e12
-                / (pf * world)}
+                / (pf * world),
+                "kernels": _kernel_table(fast_kernels, n, rows_frac)}
         del zf, sf
 
     if rank != 0:
@@ -429,14 +556,7 @@ def run_ours(args, world, rank, local):
 
     # ---- roofline of the dominant kernel (live CUDA-event durations)
     peak_tc, peak_hbm, peak_src = peaks(args.precision)
-    per_kernel = {}
-    for name, rec in kernels.items():
-        avg = rec["total_ms"] / rec["launches"]
-        fl = kernel_flops(name, n) * rows_frac
-        per_kernel[name] = {"launches": rec["launches"], "avg_ms": round(avg, 4),
-                            "share": round(rec["total_ms"] / max(1e-9, sum(
-                                r["total_ms"] for r in kernels.values())), 4),
-                            "tflops": round(fl / (avg / 1e3) / 1e12, 2) if fl else None}
+    per_kernel = _kernel_table(kernels, n, rows_frac)
     dom = max(kernels, key=lambda k: kernels[k]["total_ms"])
     dom_avg_s = kernels[dom]["total_ms"] / kernels[dom]["launches"] / 1e3
     achieved = kernel_flops(dom, n) * rows_frac / dom_avg_s / 1e12
@@ -450,9 +570,12 @@ def run_ours(args, world, rank, local):
             traffic = None
     launches = sum(r["launches"] for r in kernels.values())
 
-    # ---- CPU baseline (rank 0, N=1 only): bounded sample of the same workload
+    # ---- CPU leg (rank 0, N=1 only): the oracle checks the timed kernels on
+    # sampled lines of one block, then times a bounded sample of the workload
     cpu = None
+    parity = None
     if world == 1 and not args.no_cpu:
+        parity = block_parity(block, z_host, s_host, mask_host, args.valid, args.precision, dev)
         from oracle.cpu_baseline import sampled_block_seconds
         tot, parts, sample, threads = sampled_block_seconds(n, args.valid, row_sample=8,
                                                             chan_sample=4)
@@ -481,6 +604,7 @@ def run_ours(args, world, rank, local):
                      "peak_source": peak_src},
         "kernels": per_kernel,
         "cpu_baseline": cpu,
+        "parity": parity,
         "clocks": clk,
         "side": side,
     }

@@ -61,6 +61,9 @@ SIGNATURES = {
     "fpb_attention_core": (c_int, [c_void_p, c_void_p] * 3 + [c_int] * 4
                            + [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                               c_size_t, c_void_p]),
+    "fpb_attention_core_ex": (c_int, [c_void_p, c_void_p] * 3 + [c_int] * 4
+                              + [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                 c_void_p, c_size_t, c_void_p]),
     "fpb_trimul_shard_workspace_size": (c_size_t, [c_int]),
     "fpb_trimul_plane_ld": (c_size_t, [c_int, c_int]),
     "fpb_trimul_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]

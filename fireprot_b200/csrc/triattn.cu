@@ -382,6 +382,7 @@ struct AttnCoreArgs {
   int* status;
   int o_f32;           // write fp32 output in fast mode too
   int q_plain;         // strict: q unsplit (FP32) in q_hi, split while staged into TMEM
+  int empty_nan;       // a row whose every logit is -inf: NaN (softmax) or 0 (SDPA)
 };
 
 template <bool kStrict>
@@ -777,11 +778,14 @@ __global__ void __launch_bounds__(192, 2)
       const float m_new = move ? mx : m_ref;
       const float alpha = move ? ex2_approx((m_ref - m_new) * kLog2e) : 1.0f;
       m_ref = m_new;
+      // while every logit so far is -inf the reference is -inf: exponentiate
+      // against 0 instead, so those entries give exp(-inf) = 0 and not NaN
+      const float m_sub = m_ref == -INFINITY ? 0.0f : m_ref;
       // P(t) over S(t) (A operand of P V), 16 keys at a time; strict P_lo
       // waits in registers until P V(t-1) has read the shared P_lo region
       float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t plo[kStrict ? C::BKV : 1];
-      const float2 neg_m = make_float2(-m_ref, -m_ref);
+      const float2 neg_m = make_float2(-m_sub, -m_sub);
       const float2 l2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
       for (int c = 0; c < C::BKV / 16; ++c) {
@@ -860,7 +864,10 @@ __global__ void __launch_bounds__(192, 2)
     }
     if (ok && mbar_wait(pv_done, (nt - 1) & 1, g, 28)) {
       tc_fence_after();
+      // l_run is 0 only when every logit of the row was -inf
+      const bool empty = l_run == 0.0f;
       const float inv = 1.0f / l_run;
+      const float fill = p.empty_nan ? __uint_as_float(0x7fc00000u) : 0.0f;
       float o[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -868,7 +875,7 @@ __global__ void __launch_bounds__(192, 2)
         tmem_ld16(tb + C::kO + c * 16, ov);
         tmem_ld_wait();
 #pragma unroll
-        for (int d = 0; d < 16; ++d) o[c * 16 + d] = __uint_as_float(ov[d]) * inv;
+        for (int d = 0; d < 16; ++d) o[c * 16 + d] = empty ? fill : __uint_as_float(ov[d]) * inv;
       }
       if (jvalid) {
         const size_t orow = (size_t)i * n + j;
@@ -1616,13 +1623,15 @@ extern "C" size_t fpb_attention_core_workspace_size(int batch, int n, int heads,
   return cnt.used;
 }
 
-extern "C" int fpb_attention_core(const float* q, const long long* q_strides, const float* k,
-                                  const long long* k_strides, const float* v,
-                                  const long long* v_strides, int batch, int n, int heads,
-                                  int head_dim, const float* tri_bias,
-                                  const long long* tri_bias_strides, const float* mask_bias,
-                                  const long long* mask_bias_strides, float* out, int precision,
-                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+extern "C" int fpb_attention_core_ex(const float* q, const long long* q_strides,
+                                     const float* k, const long long* k_strides, const float* v,
+                                     const long long* v_strides, int batch, int n, int heads,
+                                     int head_dim, const float* tri_bias,
+                                     const long long* tri_bias_strides, const float* mask_bias,
+                                     const long long* mask_bias_strides, float* out,
+                                     int precision, int empty_rows_nan, void* workspace,
+                                     size_t workspace_bytes, cudaStream_t stream) {
+  if (empty_rows_nan != 0 && empty_rows_nan != 1) return kErrArg;
   if (!q || !k || !v || !q_strides || !k_strides || !v_strides || !tri_bias ||
       !tri_bias_strides || !out || !workspace || (mask_bias && !mask_bias_strides))
     return kErrArg;
@@ -1675,7 +1684,20 @@ extern "C" int fpb_attention_core(const float* q, const long long* q_strides, co
                                                         pl.bias, pl.mbias));
   if ((st = launch_status())) return st;
   // this boundary returns FP32 [B, N, H, D] in both precision modes
-  AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1};
+  AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1, 0,
+                  empty_rows_nan};
   return launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, batch, pl.ldv,
                           ca, strict, stream);
+}
+
+extern "C" int fpb_attention_core(const float* q, const long long* q_strides, const float* k,
+                                  const long long* k_strides, const float* v,
+                                  const long long* v_strides, int batch, int n, int heads,
+                                  int head_dim, const float* tri_bias,
+                                  const long long* tri_bias_strides, const float* mask_bias,
+                                  const long long* mask_bias_strides, float* out, int precision,
+                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return fpb_attention_core_ex(q, q_strides, k, k_strides, v, v_strides, batch, n, heads,
+                               head_dim, tri_bias, tri_bias_strides, mask_bias, mask_bias_strides,
+                               out, precision, 0, workspace, workspace_bytes, stream);
 }

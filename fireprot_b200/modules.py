@@ -304,3 +304,34 @@ class PairformerBlock(nn.Module):
         self.pair(z, mask, precision=precision, workspace=workspace)
         self.single(s, z, mask, precision=precision, workspace=single_workspace)
         return s, z
+
+    OPERATORS = ("tri_mul_out", "tri_mul_in", "tri_att_start", "tri_att_end",
+                 "pair_transition", "single")
+
+    @torch.no_grad()
+    def forward_by_operator(self, s, z, mask=None, *, precision="strict"):
+        """The same block one operator at a time, for inspection: yields
+        ``(name, tensor)`` after each operator has updated ``z`` (or, for the
+        final ``"single"``, ``s``) in place, in ``OPERATORS`` order, with the
+        stream synchronised. Same kernels as ``forward``; each operator gets
+        its own workspace and its device status is checked."""
+        pair = self.pair
+        for name in self.OPERATORS[:5]:
+            mod = getattr(pair, name)
+            if name == "pair_transition":
+                _, ws = ops.transition(z, mod.weight_dict(), precision=precision,
+                                       return_workspace=True)
+            elif name.startswith("tri_mul"):
+                _, ws = ops.trimul(z, mask, mod.weight_dict(), outgoing=mod._outgoing,
+                                   precision=precision, return_workspace=True)
+            else:
+                _, ws = ops.triattn(z, mask, mod.weight_dict(), starting=mod.starting,
+                                    precision=precision, return_workspace=True)
+            if ops.workspace_status(ws) != 0:
+                raise RuntimeError(f"{name}: device status {ops.workspace_status(ws)}")
+            yield name, z
+        _, ws = ops.single_block(s, z, mask, self.single.c_weights(), precision=precision,
+                                 return_workspace=True)
+        if ops.workspace_status(ws) != 0:
+            raise RuntimeError(f"single: device status {ops.workspace_status(ws)}")
+        yield "single", s

@@ -166,7 +166,10 @@ class AttentionCoreKernel:
         if not self.supports(query, key, value, biases):
             raise ValueError("Unsupported attention tensors or device")
         with torch.cuda.device(self.device):
-            out = ops.attention_core(query, key, value, list(biases), precision=precision)
+            # a row with no finite logit is NaN, as upstream's softmax and the
+            # reference's kernel give it (fireprot_softmax_fp32.cpp:61-62)
+            out = ops.attention_core(query, key, value, list(biases), precision=precision,
+                                     empty_rows="nan")
         self.launches_submitted += 1
         return out.transpose(1, 2)  # [B, N, 4, 32] storage, [B, 4, N, 32] view
 

@@ -189,7 +189,8 @@ def transition(z: torch.Tensor, w: dict, *, precision="strict", eps: float = 1e-
 
 
 def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
-                   precision="strict", return_workspace: bool = False):
+                   precision="strict", empty_rows: str = "zero",
+                   return_workspace: bool = False):
     """``softmax(q k^T + sum(biases)) v`` at the reference's dispatch boundary.
 
     q (pre-scaled), k, v: ``[B, 4, N, 32]`` float32, any strides; ``biases``
@@ -197,7 +198,15 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
     ``mask_bias [B, 1, 1, N]`` (or ``[1, 1, 1, N]``, shared by every batch
     entry) and ``triangle_bias [1, 4, N, N]``, any non-negative strides. Returns
     ``[B, N, 4, 32]`` (``triangle_attention.py:129``).
+
+    ``empty_rows``: the result of a query row whose every logit is -inf:
+    ``"zero"`` as torch's scaled_dot_product_attention (the Protenix
+    dispatch, ``triangle_attention.py:83-129``), ``"nan"`` as a softmax
+    whose row sum is zero (the OpenFold3 contract,
+    ``fireprot_softmax_fp32.cpp:61-62``).
     """
+    if empty_rows not in ("zero", "nan"):
+        raise ValueError(f"empty_rows must be 'zero' or 'nan', got {empty_rows!r}")
     _require_cuda(q, k, v, *biases)
     if q.ndim != 4 or q.shape[1] != 4 or q.shape[3] != 32 or q.shape != k.shape \
             or q.shape != v.shape:
@@ -237,10 +246,11 @@ def attention_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, biases, *,
     qs, ks, vs, ts = strides(q), strides(k), strides(v), strides(tri)
     ms = (strides(mask_bias, broadcast_batch=mask_bias.shape[0] == 1)
           if mask_bias is not None else None)
-    _lib.check(lib.fpb_attention_core(
+    _lib.check(lib.fpb_attention_core_ex(
         q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, batch, n, 4, 32, tri.data_ptr(), ts,
-        0 if mask_bias is None else mask_bias.data_ptr(), ms, out.data_ptr(), p, ws.data_ptr(),
-        ws.numel(), _stream_ptr(q.device)), "fpb_attention_core")
+        0 if mask_bias is None else mask_bias.data_ptr(), ms, out.data_ptr(), p,
+        int(empty_rows == "nan"), ws.data_ptr(), ws.numel(), _stream_ptr(q.device)),
+        "fpb_attention_core_ex")
     return (out, ws) if return_workspace else out
 
 

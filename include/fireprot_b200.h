@@ -152,7 +152,11 @@ int fpb_transition_noalloc(float* z, float* delta_out, long long rows, int c_z, 
  *                                     + tri_bias[0,h,j,k]) v[b,h,k,:]
  * q (already scaled), k, v: [batch, 4, n, 32] FP32 with element strides
  * (4 entries each); tri_bias [1, 4, n, n], mask_bias [batch, 1, 1, n] or null,
- * any strides; out [batch, n, 4, 32] contiguous FP32 (both precisions). */
+ * any strides; out [batch, n, 4, 32] contiguous FP32 (both precisions).
+ * -inf biases are exact: such keys get weight 0. A query row whose every
+ * logit is -inf gives 0, as the torch scaled_dot_product_attention the
+ * reference's dispatch checks against (triangle_attention.py:83-129, tested
+ * with a -inf bias row at tests/operators/test_ck_attention.py:69-81). */
 size_t fpb_attention_core_workspace_size(int batch, int n, int heads, int head_dim,
                                          int precision, int with_mask);
 int fpb_attention_core(const float* q, const long long* q_strides, const float* k,
@@ -161,6 +165,18 @@ int fpb_attention_core(const float* q, const long long* q_strides, const float* 
                        const long long* tri_bias_strides, const float* mask_bias,
                        const long long* mask_bias_strides, float* out, int precision,
                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* fpb_attention_core with the result of an all -inf row chosen:
+ * empty_rows_nan = 0 gives 0 (as fpb_attention_core), 1 gives NaN, the
+ * contract of the OpenFold3 mask + bias softmax that a zero row sum is NaN
+ * (kernels/amd/fireprot_softmax_fp32.cpp:61-62, followed by upstream's P V
+ * einsum; python/fireprot/adapters/openfold3/attention.py:135-148). */
+int fpb_attention_core_ex(const float* q, const long long* q_strides, const float* k,
+                          const long long* k_strides, const float* v,
+                          const long long* v_strides, int batch, int n, int heads, int head_dim,
+                          const float* tri_bias, const long long* tri_bias_strides,
+                          const float* mask_bias, const long long* mask_bias_strides, float* out,
+                          int precision, int empty_rows_nan, void* workspace,
+                          size_t workspace_bytes, cudaStream_t stream);
 
 /* Operator policy registry (host only), the counterpart of the reference's
  * Rust core crates/fireprot-core/src/registry.rs:95-268 behind its bridge

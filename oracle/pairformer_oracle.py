@@ -210,19 +210,34 @@ def layer_norm(x, w, b, eps=LN_EPS):
     return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
 
 
-def attention_core(q, k, v, biases):
+def attention_core(q, k, v, biases, empty_rows="nan"):
     """The upstream ``_attention``: ``softmax(q @ k^T + sum(biases)) @ v``.
 
     q, k, v: ``[*, H, Q, D]``; biases broadcast to ``[*, H, Q, K]`` and are
     added in list order (mask bias first). Q is pre-scaled by the caller.
     Returns ``[*, H, Q, D]`` (the reference's dispatch transposes it to
     ``[*, Q, H, D]``; ``triangle_attention.py:129``).
+
+    ``empty_rows`` is the result of a query row whose every logit is -inf:
+    ``"nan"`` as torch's softmax (upstream ``_attention``, and the OpenFold3
+    kernel's zero-row-sum contract, ``fireprot_softmax_fp32.cpp:61-62``),
+    ``"zero"`` as torch's ``scaled_dot_product_attention``, which the
+    Protenix dispatch checks its kernels against (``triangle_attention.py:
+    83-129``; ``tests/operators/test_ck_attention.py:69-81``).
     """
     a = torch.matmul(q, k.transpose(-1, -2))
     for b in biases:
         a = a + b
+    empty = None
+    if empty_rows == "zero":
+        empty = torch.isneginf(a.amax(dim=-1, keepdim=True))
+    elif empty_rows != "nan":
+        raise ValueError(empty_rows)
     a = torch.softmax(a, dim=-1)
-    return torch.matmul(a, v)
+    out = torch.matmul(a, v)
+    if empty is not None:
+        out = out.masked_fill(empty, 0.0)
+    return out
 
 
 # --------------------------------------------------------------------------
@@ -313,6 +328,114 @@ def pair_block(z, mask, p: PairBlockParams, *, attn_chunk: int = 64):
     z = z + triangle_attention(z, mask, p.tri_att_end, starting=False, chunk=attn_chunk)
     z = z + pair_transition(z, p.transition)
     return z
+
+
+# --------------------------------------------------------------------------
+# row-sampled forms (full-size parity: the same math on a few rows)
+# --------------------------------------------------------------------------
+# Each function returns selected rows (or, for the ending node, columns) of
+# the corresponding full operator above, computing only what those rows
+# depend on: the terms that couple rows (TriMul's b over every pair, the
+# pair bias of TriAttn over every pair) in full, the rest for the selected
+# rows. Used to check CUDA results at sizes where the full CPU restatement
+# would take minutes (N = 1000, 1536, 3072).
+def _idx(rows):
+    return torch.as_tensor(rows, dtype=torch.long)
+
+
+def trimul_rows(z, mask, p: TriMulParams, rows, *, outgoing: bool, add: bool = True):
+    """Rows ``rows`` of ``triangle_multiplication(z, mask, p, ...)``
+    (``[len(rows), N, c_z]``). Outgoing row i needs a[i, :] and all of b;
+    incoming row i needs a[:, i] and all of b."""
+    r = _idx(rows)
+    zn = layer_norm(z, p.ln_in_w, p.ln_in_b)
+    b = torch.sigmoid(zn @ p.w_b_g.T) * (zn @ p.w_b_p.T)
+    if mask is not None:
+        b = b * mask[..., None]
+    za = zn[r] if outgoing else zn[:, r]          # [r, k, c] or [k, r, c]
+    a = torch.sigmoid(za @ p.w_a_g.T) * (za @ p.w_a_p.T)
+    if mask is not None:
+        a = a * (mask[r] if outgoing else mask[:, r])[..., None]
+    a_cf = a.permute(2, 0, 1) if outgoing else a.permute(2, 1, 0)  # [c, r, k]
+    b_cf = b.permute(2, 0, 1)                                      # [c, N, N]
+    if outgoing:
+        x = torch.matmul(a_cf, b_cf.transpose(-1, -2))  # sum_k a[c,i,k] b[c,j,k]
+    else:
+        x = torch.matmul(a_cf, b_cf)                    # sum_k a[c,k,i] b[c,k,j]
+    x = layer_norm(x.permute(1, 2, 0), p.ln_out_w, p.ln_out_b) @ p.w_z.T
+    delta = torch.sigmoid(zn[r] @ p.w_g.T) * x
+    return z[r] + delta if add else delta
+
+
+def triattn_lines(z, mask, p: TriAttnParams, lines, *, starting: bool = True, chunk: int = 8):
+    """Lines of the triangle attention update (no residual), as
+    ``[len(lines), N, c_z]``: starting node, rows ``delta[l, :]``; ending
+    node, columns ``delta[:, l]`` (row l of the starting-node form on z^T).
+    Each line needs its own pair line of z and the pair bias of every pair."""
+    x = z if starting else z.transpose(0, 1)
+    m = None if mask is None else (mask if starting else mask.transpose(0, 1))
+    r = _idx(lines)
+    n = x.shape[0]
+    H, d = p.heads, p.head_dim
+    tri_bias = (layer_norm(x, p.ln_w, p.ln_b) @ p.w_bias.T).permute(2, 0, 1).unsqueeze(0)
+    outs = []
+    for s in range(0, len(r), chunk):
+        rr = r[s:s + chunk]
+        xn = layer_norm(x[rr], p.ln_w, p.ln_b)                         # [c, N, C]
+        q = (xn @ p.w_q.T).reshape(len(rr), n, H, d).permute(0, 2, 1, 3) / math.sqrt(d)
+        k = (xn @ p.w_k.T).reshape(len(rr), n, H, d).permute(0, 2, 1, 3)
+        v = (xn @ p.w_v.T).reshape(len(rr), n, H, d).permute(0, 2, 1, 3)
+        biases = []
+        if m is not None:
+            biases.append((MASK_INF * (m[rr] - 1.0))[:, None, None, :])
+        biases.append(tri_bias)
+        o = attention_core(q, k, v, biases).permute(0, 2, 1, 3).reshape(len(rr), n, H * d)
+        gate = xn @ p.w_g.T
+        if p.b_g is not None:
+            gate = gate + p.b_g
+        out = (torch.sigmoid(gate) * o) @ p.w_o.T
+        if p.b_o is not None:
+            out = out + p.b_o
+        outs.append(out)
+    return torch.cat(outs, 0)
+
+
+def transition_rows(z, p: TransitionParams, rows):
+    """Rows of ``z + pair_transition(z, p)`` (the transition is row-local)."""
+    zr = z[_idx(rows)]
+    return zr + pair_transition(zr, p)
+
+
+def single_block_rows(s, z, mask, p: "SingleBlockParams", rows):
+    """Rows of ``single_block(s, z, mask, p)``: query row i needs its own
+    pair row z[i] (the pair bias of its keys) and every row of s (keys and
+    values); the transition is row-local."""
+    r = _idx(rows)
+    n = s.shape[0]
+    h, d = p.heads, p.head_dim
+    a = layer_norm(s, p.ln_a_w, p.ln_a_b)
+    q = ((a[r] @ p.w_q.T + p.b_q) / math.sqrt(d)).view(len(r), h, d).transpose(0, 1)
+    k = (a @ p.w_k.T).view(n, h, d).transpose(0, 1)
+    v = (a @ p.w_v.T).view(n, h, d).transpose(0, 1)
+    bias = (layer_norm(z[r], p.ln_z_w, p.ln_z_b) @ p.w_z.T).permute(2, 0, 1)  # [H, r, N]
+    biases = [bias]
+    if mask is not None:
+        biases = [(MASK_INF * (mask[r] - 1.0)).to(s.dtype)[None], bias]
+    o = attention_core(q, k, v, biases).transpose(0, 1).reshape(len(r), h * d)
+    s1 = s[r] + (torch.sigmoid(a[r] @ p.w_g.T) * o) @ p.w_o.T
+    return s1 + pair_transition(s1, p.transition)
+
+
+def sample_lines(n: int, count: int = 12, seed: int = 0, valid=None):
+    """Sorted distinct line indices: the first and last line, the last valid
+    line and the first padded one (when ``valid`` < n), and ``count`` seeded
+    random others."""
+    g = torch.Generator().manual_seed(seed)
+    pick = {0, n - 1}
+    if valid is not None and 0 < valid < n:
+        pick |= {valid - 1, valid}
+    extra = torch.randperm(n, generator=g)[:count].tolist()
+    return sorted(pick | set(extra))
 
 
 # --------------------------------------------------------------------------

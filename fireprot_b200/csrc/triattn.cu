@@ -383,20 +383,61 @@ struct AttnCoreArgs {
   int o_f32;           // write fp32 output in fast mode too
   int q_plain;         // strict: q unsplit (FP32) in q_hi, split while staged into TMEM
   int empty_nan;       // a row whose every logit is -inf: NaN (softmax) or 0 (SDPA)
+  const int* kend;     // [rows] keys to visit per row (key_extent_kernel), or null: all n
 };
+
+// Keys of pair row i that the attention core must visit: 1 + the last key
+// whose mask bias is not exactly -1e9 (mask exactly 0), when the row has a
+// key with mask bias exactly 0 (mask 1); otherwise (a fully masked row, or
+// fractional masks only) every key, n. Exactness of the skip: in such a row
+// the running reference max is at least that unmasked key's logit minus 8 in
+// log2 units, so each skipped key's logit, about -1e9 below it, gives
+// exp2(<= -1e9) = +0 exactly: P = 0, P V adds 0 to O and 0 to the row sum,
+// and a tile whose every key is skipped never moves the reference. The
+// result is bit-identical to visiting every key. One warp per row.
+__global__ void key_extent_kernel(const float* __restrict__ mbias, int ldb, int rows, int n,
+                                  int* __restrict__ kend) {
+  const int row = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* m = mbias + (size_t)row * ldb;
+  int last = -1;
+  bool live = false;
+  for (int k = lane; k < n; k += 32) {
+    const float v = __ldg(m + k);
+    if (v != -kMaskInf) last = k;
+    if (v == 0.0f) live = true;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+  live = __any_sync(0xffffffffu, live);
+  if (lane == 0) kend[row] = live ? last + 1 : n;
+}
+
+// Fast-mode shape of the attention core: keys per tile and resident CTAs
+// per SM (the strict shape is fixed at 48 keys, two CTAs). Three CTAs need
+// 32-key tiles to fit their TMEM share (128 columns) and registers.
+#ifndef FPB_ATTN_BKV_FAST
+#define FPB_ATTN_BKV_FAST 48
+#endif
+#ifndef FPB_ATTN_CTAS_FAST
+#define FPB_ATTN_CTAS_FAST 2
+#endif
 
 template <bool kStrict>
 struct AttnCfg {
   static constexpr int BQ = 128;                       // queries per CTA
-  static constexpr int BKV = 48;                       // keys per tile
+  static constexpr int BKV = kStrict ? 48 : FPB_ATTN_BKV_FAST;  // keys per tile
+  static constexpr int CTAS = kStrict ? 2 : FPB_ATTN_CTAS_FAST;  // resident per SM
   static constexpr int ESZ = kStrict ? 4 : 2;
   static constexpr int NSPLIT = kStrict ? 2 : 1;
   static constexpr int QK_ROW = 32 * ESZ;              // bytes per q/k row (128 / 64)
   static constexpr int Q_BYTES = BQ * QK_ROW;          // per split
   static constexpr int K_BYTES = BKV * QK_ROW;         // per split
   // V^T atoms: 64-byte rows of 16 fp32 keys (strict, 3 per tile) or
-  // 128-byte rows of 64 bf16 keys (fast, 1 per tile), 32 rows (d) each
-  static constexpr int V_ROW = kStrict ? 64 : 128;
+  // 128-byte rows of 64 bf16 keys (fast, 1 per tile; 64-byte rows of 32
+  // keys for 32-key tiles), 32 rows (d) each
+  static constexpr int V_ROW = (kStrict || BKV <= 32) ? 64 : 128;
   static constexpr int V_ATOM_KEYS = V_ROW / ESZ;
   static constexpr int V_ATOMS = (BKV + V_ATOM_KEYS - 1) / V_ATOM_KEYS;
   static constexpr int V_ATOM_BYTES = 32 * V_ROW;
@@ -418,8 +459,9 @@ struct AttnCfg {
   static constexpr uint32_t kQ = kO + 32;
   static constexpr uint32_t kQL = kQ + 32;  // strict only
   static constexpr int Q_COLS = kStrict ? 64 : 16;
-  static constexpr int TMEM_COLS = 256;
+  static constexpr int TMEM_COLS = CTAS >= 3 ? 128 : 256;
   static_assert(kQ + Q_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(CTAS * TMEM_COLS <= 512, "TMEM per SM");
   static_assert(BKV % KSTEP_KEYS == 0 && BKV % 16 == 0, "key tile shape");
   static_assert(KV_STAGE % 1024 == 0 && (NSPLIT * K_BYTES) % 1024 == 0, "stage alignment");
   static constexpr int THREADS = 192;  // 4 softmax warps, TMA warp, MMA warp
@@ -451,7 +493,7 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
 // S(t+2) reuses buffer t%2 once P V(t) has retired, so the softmax of
 // tile t+1 never waits on the tensor pipe.
 template <bool kStrict>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
     attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
                      const __grid_constant__ CUtensorMap mq_lo,
                      const __grid_constant__ CUtensorMap mk_hi,
@@ -480,7 +522,10 @@ __global__ void __launch_bounds__(192, 2)
   const int n = p.n;
   const int jt = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
   const int ih = i * kHeads + h;
-  const int nt = (n + C::BKV - 1) / C::BKV;
+  // key tiles of this row: the trailing tiles past its key extent hold only
+  // keys whose weight is exactly 0 (key_extent_kernel) and are not visited
+  const int nt = p.kend ? max(1, (min(__ldg(p.kend + i), n) + C::BKV - 1) / C::BKV)
+                        : (n + C::BKV - 1) / C::BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -587,7 +632,9 @@ __global__ void __launch_bounds__(192, 2)
             umma_tf32_ts(d_o, pa + kk * 8, dvl, id_o, 1u);              // P_hi V_lo
             umma_tf32_ts(d_o, tmem + C::kPLO + kk * 8, dvh, id_o, 1u);  // P_lo V_hi
           } else {
-            umma_bf16_ts(d_o, pa + kk * 8, umma_desc_sw128(vst + vo), id_o, acc);
+            const uint64_t dv =
+                C::V_ROW == 64 ? umma_desc_sw64(vst + vo) : umma_desc_sw128(vst + vo);
+            umma_bf16_ts(d_o, pa + kk * 8, dv, id_o, acc);
           }
         }
         umma_commit(pv_done);
@@ -640,7 +687,7 @@ __global__ void __launch_bounds__(192, 2)
     const float* brow = p.bias + bias_index(jvalid ? j : 0, h, 0, p.ldb);
     const float* mrow = p.mbias ? p.mbias + (size_t)i * p.ldb : nullptr;
     constexpr float kLog2e = 1.4426950408889634f;
-    constexpr float kRescale = 8.0f / kLog2e;  // move the reference max past 2^8
+    constexpr float kRescale = 8.0f;  // log2 units: move the reference past P = 2^8
     const uint64_t pol_bias = policy_evict_last();
     // Additive terms of key tile t, loaded in one batch a tile ahead: the
     // pair bias (a different row per thread) plus the mask bias row (the
@@ -682,7 +729,11 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
     };
-    float m_ref = -INFINITY, l_run = 0.f;
+    // reference max in log2 units (mL = fl(m log2e)); every P of the row is
+    // exp2(fl(s log2e - mL)) against the current mL, and O and the row sum
+    // are rescaled by exp2(mL_old - mL_new) whenever it moves, so numerator
+    // and denominator always share one reference
+    float mL = -INFINITY, l_run = 0.f;
     float2 cb[NP];
     load_bias(0, cb);
     // this thread's query row of Q (hi and lo) -> TMEM, the A operands of
@@ -774,25 +825,27 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int e = 0; e < NP; ++e) mx4[e & 3] = fmax3f(mx4[e & 3], sv[e].x, sv[e].y);
       const float mx = fmax3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
-      const bool move = mx > m_ref + kRescale;  // always on the first tile
-      const float m_new = move ? mx : m_ref;
-      const float alpha = move ? ex2_approx((m_ref - m_new) * kLog2e) : 1.0f;
-      m_ref = m_new;
+      const float mxL = mx * kLog2e;
+      const bool move = mxL > mL + kRescale;  // always on the first finite tile
+      const float mL_new = move ? mxL : mL;
+      const float alpha = move ? ex2_approx(mL - mL_new) : 1.0f;
+      mL = mL_new;
       // while every logit so far is -inf the reference is -inf: exponentiate
-      // against 0 instead, so those entries give exp(-inf) = 0 and not NaN
-      const float m_sub = m_ref == -INFINITY ? 0.0f : m_ref;
+      // against 0 instead, so those entries give exp2(-inf) = 0 and not NaN
+      const float m_sub = mL == -INFINITY ? 0.0f : mL;
       // P(t) over S(t) (A operand of P V), 16 keys at a time; strict P_lo
       // waits in registers until P V(t-1) has read the shared P_lo region
       float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t plo[kStrict ? C::BKV : 1];
-      const float2 neg_m = make_float2(-m_sub, -m_sub);
+      // exponent s log2e - mL, one fused multiply-add per key
+      const float2 neg_ml = make_float2(-m_sub, -m_sub);
       const float2 l2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
       for (int c = 0; c < C::BKV / 16; ++c) {
         float2 pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float2 a = __fmul2_rn(__fadd2_rn(sv[c * 8 + e], neg_m), l2e);
+          const float2 a = __ffma2_rn(sv[c * 8 + e], l2e, neg_ml);
           pv[e] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
           ls2[e & 1] = __fadd2_rn(ls2[e & 1], pv[e]);
         }
@@ -923,7 +976,8 @@ int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const
   const uint64_t nh = (uint64_t)rows * kHeads;
   const uint32_t bkv = strict ? AttnCfg<true>::BKV : AttnCfg<false>::BKV;
   const uint32_t vkeys = strict ? AttnCfg<true>::V_ATOM_KEYS : AttnCfg<false>::V_ATOM_KEYS;
-  const CUtensorMapSwizzle vsw = strict ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const int vrow = strict ? AttnCfg<true>::V_ROW : AttnCfg<false>::V_ROW;
+  const CUtensorMapSwizzle vsw = vrow == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
   bool ok = make_map_3d(&mqh, q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
             make_map_3d(&mkh, k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
@@ -1308,9 +1362,13 @@ struct TriAttnPlan {
     if (strict) v_lo = take(vc);
     ldb = padded_ld(n, 4);
     if (own_bias) bias = al.template take<float>(bias_elems(n, ldb));
-    if (with_mask) mbias = al.template take<float>((size_t)rows * ldb);
+    if (with_mask) {
+      mbias = al.template take<float>((size_t)rows * ldb);
+      kend = al.template take<int>((size_t)rows);
+    }
     o = take((size_t)rows * n * 128);
   }
+  int* kend = nullptr;
 };
 
 // phase 1: LN + q/k/v projection of the call's rows, pair bias of those rows
@@ -1364,7 +1422,13 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
   CUtensorMap moh, mol;
   if (!make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol)) return kErrArg;
   {
-    AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0};
+    if (pl.kend) {
+      FPB_LAUNCH("key_extent", stream,
+                 key_extent_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(pl.mbias, pl.ldb, rows, n,
+                                                                      pl.kend));
+      if ((st = launch_status())) return st;
+    }
+    AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0, 0, 0, pl.kend};
     if ((st = launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, rows,
                                pl.ldv, ca, strict, stream)))
       return st;

@@ -82,11 +82,10 @@ SIGNATURES = {
                                 + [c_float, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_triattn_bias_ld": (c_size_t, [c_int]),
     "fpb_triattn_shard_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
-    "fpb_triattn_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int] + [c_void_p] * 6
+    "fpb_triattn_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int] + [c_void_p] * 8
                                + [c_float, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_triattn_shard_finish": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
-                                 + [c_void_p] * 6
-                                 + [c_float, c_int, c_void_p, c_size_t, c_void_p]),
+                                 + [c_void_p] * 2 + [c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_registry_new": (c_void_p, []),
     "fpb_registry_free": (None, [c_void_p]),
     "fpb_registry_register": (c_int, [c_void_p, c_char_p, CAPABILITY_FN, c_void_p]),

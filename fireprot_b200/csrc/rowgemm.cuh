@@ -136,6 +136,30 @@ __device__ __forceinline__ void ln_smem_rows_to_a(uint8_t* A, int row0, float4 l
   }
 }
 
+// Strict-mode A operand from raw FP32 rows already in shared memory (copied
+// by TMA into the lo half of A, as for ln_smem_rows_to_a): the kRows rows
+// [row0, row0 + kRows) are split in place into tf32 hi and lo, no other
+// arithmetic. Lane l handles channels 4l..4l+3 of each row.
+template <int kRows>
+__device__ __forceinline__ void split_smem_rows_to_a(uint8_t* A, int row0) {
+  using C = RowCfg<true>;
+  constexpr int kBatch = 8;
+  static_assert(kRows % kBatch == 0, "batch must divide the rows");
+  const int lane = threadIdx.x & 31;
+  const int atom = lane / 8, byte = (lane % 8) * 16;
+  const uint8_t* raw = A + C::A_SPLIT_BYTES + atom * C::ATOM_BYTES;
+#pragma unroll 1
+  for (int b0 = 0; b0 < kRows; b0 += kBatch) {
+    float4 x[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      x[u] = *reinterpret_cast<const float4*>(raw + sw128_offset(row0 + b0 + u, byte));
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      a_store4<true>(A, row0 + b0 + u, lane * 4, x[u].x, x[u].y, x[u].z, x[u].w);
+  }
+}
+
 struct NoRowHook {
   __device__ __forceinline__ void operator()(int, float4) const {}
 };

@@ -10,15 +10,15 @@
 //
 // Three launches per call, all in "y" coordinates (y = z, or z^T for the
 // ending node, addressed through transposed reads; nothing is copied):
-//  1. proj: LN + [Wq;Wk;Wv] GEMM (tcgen05, 128 x 384 per tile) + the 4-head
-//     pair bias on CUDA cores in FP32; writes q,k as [i][h][j][d], v as
-//     [i][h][d][k] (K-major for PV), bias [h][j][k], mask bias [i][k].
-//  2. attn: one CTA per (128 queries, head, row i); key tiles of 64 stream by
-//     TMA; S = Q K^T in TMEM (double-buffered), online softmax by the 128
-//     row threads (FP32, SFU exp2), P -> shared memory, P V on tcgen05 into
-//     TMEM, rescaled accumulation in registers.
-//  3. out: LN(z) Wg^T (GEMM 1) -> gate; A2 = sigmoid(.) * o -> W_o (GEMM 2),
-//     + bias, residual add in place.
+//  1. proj: LN + [Wq;Wk;Wv;Wg] GEMM (tcgen05, 128 x 512 per tile) + the
+//     4-head pair bias on CUDA cores in FP32; writes q,k as [i][h][j][d], v
+//     as [i][h][d][k] (K-major for PV), the gate sigmoid(x Wg^T + b_g) as
+//     [i][j][128], bias [h][j][k], mask bias [i][k].
+//  2. attn: one CTA per (128 queries, head, row i); key tiles stream by TMA;
+//     S = Q K^T in TMEM (double-buffered), online softmax by the 128 row
+//     threads (FP32, SFU exp2), P V on tcgen05 into TMEM; the epilogue
+//     multiplies o by the gate.
+//  3. out: (gate * o) W_o^T (one GEMM) + b_o, residual add in place.
 #include "kernels.h"
 #include "rowgemm.cuh"
 
@@ -57,16 +57,17 @@ struct AttnProjArgs {
   const float* ln_b;
   const float* w_bias;  // [4][128]
   float q_scale;
-  void* q_hi;
-  void* q_lo;
-  void* k_hi;
-  void* k_lo;
-  void* v_hi;
-  void* v_lo;
+  void* q;          // [yrows*4 + h][n][32] FP32 (strict) / BF16 (fast), pre-scaled
+  void* k_hi;       // [yrows*4 + h][n][32] tf32 hi (strict) / BF16 (fast)
+  void* k_lo;       // strict: tf32 lo of k
+  void* v_hi;       // v^T [(yrows*4 + h)*32 + d][ldv], tf32 hi (strict) / BF16 (fast)
+  void* v_lo;       // strict: tf32 lo of v^T
   int ldv;          // keys pitch of v^T
   float* bias;      // j-blocked pair bias (bias_index), global rows
   int ldb;
   float* mbias;     // [yrows][ldb] or null
+  void* gate;       // [yrows * n][128]: sigmoid(x Wg^T + b_g), fp32 (strict) / bf16 (fast)
+  const float* b_g;  // [128] or null
   int* status;
 };
 
@@ -79,22 +80,23 @@ template <bool kStrict>
 constexpr int attn_proj_smem_bytes() {
   using C = RowCfg<kStrict>;
   return tmem_safe_smem(
-      C::A_BYTES + kAttnProjWStages * C::WSTAGE_BYTES + 1024 + 256 + 2 * 4 * 128 * 4, 512);
+      C::A_BYTES + kAttnProjWStages * C::WSTAGE_BYTES + 1024 + 256 + 3 * 4 * 128 * 4, 512);
 }
 
 // Persistent, warp-specialised: CTA b takes tiles b, b + gridDim.x, ...
 //   LN warps (0-3):       LayerNorm of the tile into A once the previous
 //                         tile's MMAs have read it, the 4-head pair bias on
 //                         the CUDA cores, the pair / mask bias rows;
-//   epilogue warps (4-7): q, k and v^T parts from TMEM to global memory,
-//                         each part released as soon as it is read, so the
-//                         next tile's MMAs of that part overlap the rest;
+//   epilogue warps (4-7): q, k, v^T and gate parts from TMEM to global
+//                         memory, each part released as soon as it is read,
+//                         so the next tile's MMAs of that part overlap the rest;
 //   TMA warp (8):         the weight ring, continuous across tiles;
-//   MMA warp (9):         part q, part k, part v of each tile.
+//   MMA warp (9):         parts q, k, v, gate of each tile (TMEM columns
+//                         [0, 512), 128 each).
 // Outputs (plain layouts, written by coalesced stores): q / k
 // [row*4 + h][j][32] (one thread = one j: 128 contiguous bytes per head),
 // v^T [(row*4 + h)*32 + d][key] (a warp's stores to one d are 32
-// consecutive keys).
+// consecutive keys), gate [row * n + j][128] (one thread = one j).
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(320, 1)
     attn_proj_kernel(const __grid_constant__ CUtensorMap w_hi,
@@ -109,13 +111,14 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* W = smem + C::A_BYTES;
   float* bias_tile = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // [4][128]
   float* wb = bias_tile + 4 * 128;                                              // [4][128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wb + 4 * 128);
+  float* bg = wb + 4 * 128;                                                     // [128] (+pad)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bg + 4 * 128);
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
   uint64_t* a_full = bars + 2 * WSTAGES;
-  uint64_t* done = a_full + 1;  // [3]: part q, k, v accumulated
-  uint64_t* freed = done + 3;   // [3]: part read by the epilogue
-  uint64_t* z_full = freed + 3; // strict: raw z rows of the tile in A (TMA)
+  uint64_t* done = a_full + 1;  // [4]: part q, k, v, gate accumulated
+  uint64_t* freed = done + 4;   // [4]: part read by the epilogue
+  uint64_t* z_full = freed + 4; // strict: raw z rows of the tile in A (TMA)
   uint64_t* drain = z_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
@@ -132,7 +135,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&wempty[s], 1);
     }
     mbar_init(a_full, 128);
-    for (int q = 0; q < 3; ++q) {
+    for (int q = 0; q < 4; ++q) {
       mbar_init(&done[q], 1);
       mbar_init(&freed[q], 128);
     }
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(320, 1)
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) wb[i] = p.w_bias[i];
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) bg[i] = p.b_g ? p.b_g[i] : 0.0f;
   if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -152,7 +156,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_slot;
   const Guard g{p.status, abort_flag};
   const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
-  constexpr int NLOADS = 3 * C::NKA;
+  constexpr int NLOADS = 4 * C::NKA;
 
   if (warp < 4) {
     const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll 1
     for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
       const int r = tile / njb, s0 = (tile % njb) * 128;
-      if (it > 0 && !mbar_wait(&done[2], (it - 1) & 1, g, 5)) break;
+      if (it > 0 && !mbar_wait(&done[3], (it - 1) & 1, g, 5)) break;
       auto src = [&](int row) -> const float4* {
         const int s = s0 + row;
         if (s >= n) return nullptr;
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(320, 1)
       const bool valid = j < n;
       bool ok = true;
 #pragma unroll 1
-      for (int part = 0; part < 3; ++part) {
+      for (int part = 0; part < 4; ++part) {
         if (!mbar_wait(&done[part], it & 1, g, 3)) {
           ok = false;
           break;
@@ -247,13 +251,12 @@ __global__ void __launch_bounds__(320, 1)
             const size_t ih = (size_t)r * kHeads + 2 * hp + u;
             if (part < 2) {
               const float sc = part == 0 ? p.q_scale : 1.0f;
-              void* dh = part == 0 ? p.q_hi : p.k_hi;
-              void* dl = part == 0 ? p.q_lo : p.k_lo;
+              void* dh = part == 0 ? p.q : p.k_hi;
               const size_t row = (ih * n + j) * 32;
               if constexpr (kStrict) {
                 float4* oh = reinterpret_cast<float4*>(static_cast<float*>(dh) + row);
-                if (dl == nullptr) {
-                  // q unsplit: the attention core splits it when staging Q
+                if (part == 0) {
+                  // q as FP32: the attention core splits it when staging Q
 #pragma unroll
                   for (int e = 0; e < 8; ++e)
                     oh[e] = make_float4(__uint_as_float(vr[u][4 * e]) * sc,
@@ -262,14 +265,15 @@ __global__ void __launch_bounds__(320, 1)
                                         __uint_as_float(vr[u][4 * e + 3]) * sc);
                   continue;
                 }
-                float4* ol = reinterpret_cast<float4*>(static_cast<float*>(dl) + row);
+                // k as tf32 hi / lo: the B operand of the core's S MMAs
+                float4* ol = reinterpret_cast<float4*>(static_cast<float*>(p.k_lo) + row);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                   float h0, l0, h1, l1, h2, l2, h3, l3;
-                  split_tf32(__uint_as_float(vr[u][4 * e]) * sc, h0, l0);
-                  split_tf32(__uint_as_float(vr[u][4 * e + 1]) * sc, h1, l1);
-                  split_tf32(__uint_as_float(vr[u][4 * e + 2]) * sc, h2, l2);
-                  split_tf32(__uint_as_float(vr[u][4 * e + 3]) * sc, h3, l3);
+                  split_tf32(__uint_as_float(vr[u][4 * e]), h0, l0);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 1]), h1, l1);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 2]), h2, l2);
+                  split_tf32(__uint_as_float(vr[u][4 * e + 3]), h3, l3);
                   oh[e] = make_float4(h0, h1, h2, h3);
                   ol[e] = make_float4(l0, l1, l2, l3);
                 }
@@ -286,6 +290,37 @@ __global__ void __launch_bounds__(320, 1)
                     w4[q] = *reinterpret_cast<uint32_t*>(&b2);
                   }
                   oh[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+              }
+            } else if (part == 3) {
+              // gate: channels (2 hp + u) * 32 + e of pair (r, j)
+              const int c0 = (2 * hp + u) * 32;
+              const size_t row = ((size_t)r * n + j) * 128 + c0;
+              if constexpr (kStrict) {
+                float4* og = reinterpret_cast<float4*>(static_cast<float*>(p.gate) + row);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  og[e] = make_float4(sigmoidf_(__uint_as_float(vr[u][4 * e]) + bg[c0 + 4 * e]),
+                                      sigmoidf_(__uint_as_float(vr[u][4 * e + 1]) +
+                                                bg[c0 + 4 * e + 1]),
+                                      sigmoidf_(__uint_as_float(vr[u][4 * e + 2]) +
+                                                bg[c0 + 4 * e + 2]),
+                                      sigmoidf_(__uint_as_float(vr[u][4 * e + 3]) +
+                                                bg[c0 + 4 * e + 3]));
+              } else {
+                uint4* og = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.gate) + row);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  uint32_t w4[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const int c = 8 * e + 2 * q;
+                    __nv_bfloat162 b2 = __floats2bfloat162_rn(
+                        sigmoidf_(__uint_as_float(vr[u][c]) + bg[c0 + c]),
+                        sigmoidf_(__uint_as_float(vr[u][c + 1]) + bg[c0 + c + 1]));
+                    w4[q] = *reinterpret_cast<uint32_t*>(&b2);
+                  }
+                  og[e] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                 }
               }
             } else {
@@ -336,7 +371,7 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        for (int nc = 0; nc < 3 && ok; ++nc) {
+        for (int nc = 0; nc < 4 && ok; ++nc) {
           if (it > 0 && !mbar_wait(&freed[nc], (it - 1) & 1, g, 6)) {
             ok = false;
             break;
@@ -381,9 +416,9 @@ struct AttnCoreArgs {
   void* o;             // [rows*n][128] fp32 (strict or o_f32) / bf16 (fast)
   int* status;
   int o_f32;           // write fp32 output in fast mode too
-  int q_plain;         // strict: q unsplit (FP32) in q_hi, split while staged into TMEM
   int empty_nan;       // a row whose every logit is -inf: NaN (softmax) or 0 (SDPA)
   const int* kend;     // [rows] keys to visit per row (key_extent_kernel), or null: all n
+  const void* gate;    // [rows*n][128] multiplied into o (fp32 strict / bf16 fast), or null
 };
 
 // Keys of pair row i that the attention core must visit: 1 + the last key
@@ -432,7 +467,7 @@ struct AttnCfg {
   static constexpr int ESZ = kStrict ? 4 : 2;
   static constexpr int NSPLIT = kStrict ? 2 : 1;
   static constexpr int QK_ROW = 32 * ESZ;              // bytes per q/k row (128 / 64)
-  static constexpr int Q_BYTES = BQ * QK_ROW;          // per split
+  static constexpr int Q_BYTES = BQ * QK_ROW;          // FP32 (strict) or BF16 (fast)
   static constexpr int K_BYTES = BKV * QK_ROW;         // per split
   // V^T atoms: 64-byte rows of 16 fp32 keys (strict, 3 per tile) or
   // 128-byte rows of 64 bf16 keys (fast, 1 per tile; 64-byte rows of 32
@@ -466,7 +501,7 @@ struct AttnCfg {
   static_assert(KV_STAGE % 1024 == 0 && (NSPLIT * K_BYTES) % 1024 == 0, "stage alignment");
   static constexpr int THREADS = 192;  // 4 softmax warps, TMA warp, MMA warp
   static constexpr int SMEM =
-      tmem_safe_smem(NSPLIT * Q_BYTES + KV_STAGES * KV_STAGE + 1024 + 256, TMEM_COLS);
+      tmem_safe_smem(Q_BYTES + KV_STAGES * KV_STAGE + 1024 + 256, TMEM_COLS);
 };
 
 template <bool kStrict>
@@ -494,8 +529,7 @@ __device__ __forceinline__ uint64_t qk_desc(uint32_t addr) {
 // tile t+1 never waits on the tensor pipe.
 template <bool kStrict>
 __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
-    attn_core_kernel(const __grid_constant__ CUtensorMap mq_hi,
-                     const __grid_constant__ CUtensorMap mq_lo,
+    attn_core_kernel(const __grid_constant__ CUtensorMap mq,
                      const __grid_constant__ CUtensorMap mk_hi,
                      const __grid_constant__ CUtensorMap mk_lo,
                      const __grid_constant__ CUtensorMap mv_hi,
@@ -505,7 +539,7 @@ __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* Q = smem;                                   // [split][BQ x QK_ROW]
-  uint8_t* KV = Q + C::NSPLIT * C::Q_BYTES;            // stages
+  uint8_t* KV = Q + C::Q_BYTES;                        // stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(KV + C::KV_STAGES * C::KV_STAGE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;
@@ -555,13 +589,19 @@ __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA
+    // the gate rows of this CTA's queries are read once the key loop is
+    // done: into L2 now, one 128-byte (strict) / 64-byte (fast) row per query
+    if (p.gate) {
+      for (int r = lane; r < C::BQ && jt * C::BQ + r < n; r += 32)
+        prefetch_l2(static_cast<const uint8_t*>(p.gate) +
+                        (((size_t)i * n + jt * C::BQ + r) * 128 + h * 32) * C::ESZ,
+                    32 * C::ESZ);
+    }
     if (lane == 0) {
       // the Q tile is read by this CTA only; keep L2 for the pair bias
       const uint64_t pol_q = policy_evict_first();
-      const bool q_split = kStrict && !p.q_plain;
-      mbar_arrive_expect_tx(q_full, (q_split ? 2 : 1) * C::Q_BYTES);
-      tma_load_3d_hint(Q, &mq_hi, q_full, 0, jt * C::BQ, ih, pol_q);
-      if (q_split) tma_load_3d_hint(Q + C::Q_BYTES, &mq_lo, q_full, 0, jt * C::BQ, ih, pol_q);
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      tma_load_3d_hint(Q, &mq, q_full, 0, jt * C::BQ, ih, pol_q);
       int issued = 0;
       for (int t = 0; t < nt; ++t) {
         const int s = t % C::KV_STAGES;
@@ -741,40 +781,22 @@ __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
     bool ok = mbar_wait(q_full, 0, g, 20);
     if (ok) {
       if constexpr (kStrict) {
-        if (p.q_plain) {
-          // unsplit q row: split here (hi = tf32 truncation, lo = rest)
-          uint32_t qh[32], ql[32];
+        // FP32 q row: split here (hi = tf32 truncation, lo = rest)
+        uint32_t qh[32], ql[32];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float4 v =
-                *reinterpret_cast<const float4*>(Q + sw128_offset(t_row, e * 16));
-            const float f[4] = {v.x, v.y, v.z, v.w};
+        for (int e = 0; e < 8; ++e) {
+          const float4 v = *reinterpret_cast<const float4*>(Q + sw128_offset(t_row, e * 16));
+          const float f[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float h, l;
-              split_tf32(f[u], h, l);
-              qh[4 * e + u] = __float_as_uint(h);
-              ql[4 * e + u] = __float_as_uint(l);
-            }
-          }
-          tmem_st32(tb + C::kQ, qh);
-          tmem_st32(tb + C::kQL, ql);
-        } else {
-#pragma unroll
-          for (int part = 0; part < 2; ++part) {
-            uint32_t qr[32];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const uint4 v = *reinterpret_cast<const uint4*>(Q + part * C::Q_BYTES +
-                                                              sw128_offset(t_row, e * 16));
-              qr[4 * e] = v.x;
-              qr[4 * e + 1] = v.y;
-              qr[4 * e + 2] = v.z;
-              qr[4 * e + 3] = v.w;
-            }
-            tmem_st32(tb + (part == 0 ? C::kQ : C::kQL), qr);
+          for (int u = 0; u < 4; ++u) {
+            float h, l;
+            split_tf32(f[u], h, l);
+            qh[4 * e + u] = __float_as_uint(h);
+            ql[4 * e + u] = __float_as_uint(l);
           }
         }
+        tmem_st32(tb + C::kQ, qh);
+        tmem_st32(tb + C::kQL, ql);
       } else {
         uint32_t qr[16];
 #pragma unroll
@@ -932,16 +954,39 @@ __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
       }
       if (jvalid) {
         const size_t orow = (size_t)i * n + j;
+        // the attention gate of this (pair, head), when given (the fused
+        // operator): o <- sigmoid(x Wg^T + b_g) * o, FP32 (strict) / BF16 (fast)
+        const size_t gofs = orow * 128 + h * 32;
         if (kStrict || p.o_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + orow * 128 + h * 32);
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            dst[e] = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+          for (int e = 0; e < 8; ++e) {
+            float4 v = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+            if constexpr (kStrict) {
+              if (p.gate) {
+                const float4 gv =
+                    __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.gate) + gofs) + e);
+                v = make_float4(v.x * gv.x, v.y * gv.y, v.z * gv.z, v.w * gv.w);
+              }
+            }
+            dst[e] = v;
+          }
         } else {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow * 128 +
                                                 h * 32);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
+            if (p.gate) {
+              const uint4 gv = __ldg(reinterpret_cast<const uint4*>(
+                                         static_cast<const __nv_bfloat16*>(p.gate) + gofs) + e);
+              const uint32_t g4[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&g4[q]);
+                o[8 * e + 2 * q] *= __bfloat162float(b2.x);
+                o[8 * e + 2 * q + 1] *= __bfloat162float(b2.y);
+              }
+            }
             uint32_t w4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -964,10 +1009,12 @@ __global__ void __launch_bounds__(192, AttnCfg<kStrict>::CTAS)
 }
 
 // Tensor maps and launch of the attention core over nh = rows x 4 (row,
-// head) pairs: q, k [nh][n][32] (hi/lo or bf16), v^T [nh][32][ldv].
-int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const void* k_lo,
-                     const void* v_hi, const void* v_lo, int n, int rows, int ldv,
-                     const AttnCoreArgs& ca, bool strict, cudaStream_t stream) {
+// head) pairs: q [nh][n][32] (FP32 strict, split by the core; BF16 fast),
+// k [nh][n][32] and v^T [nh][32][ldv] (tf32 hi / lo strict; BF16 fast, lo
+// unused).
+int launch_attn_core(const void* q, const void* k_hi, const void* k_lo, const void* v_hi,
+                     const void* v_lo, int n, int rows, int ldv, const AttnCoreArgs& ca,
+                     bool strict, cudaStream_t stream) {
   const int esz = strict ? 4 : 2;
   const CUtensorMapDataType dt =
       strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -978,58 +1025,46 @@ int launch_attn_core(const void* q_hi, const void* q_lo, const void* k_hi, const
   const uint32_t vkeys = strict ? AttnCfg<true>::V_ATOM_KEYS : AttnCfg<false>::V_ATOM_KEYS;
   const int vrow = strict ? AttnCfg<true>::V_ROW : AttnCfg<false>::V_ROW;
   const CUtensorMapSwizzle vsw = vrow == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
-  bool ok = make_map_3d(&mqh, q_hi, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
+  CUtensorMap mq, mkh, mkl, mvh, mvl;
+  bool ok = make_map_3d(&mq, q, dt, 32, n, nh, rowb, rowb * n, 32, 128, 1, qsw) &&
             make_map_3d(&mkh, k_hi, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
-            make_map_3d(&mvh, v_hi, dt, n, 32, nh, (uint64_t)ldv * esz,
-                        (uint64_t)ldv * esz * 32, vkeys, 32, 1, vsw);
-  // strict with no q_lo: q arrives unsplit and the core splits it
-  AttnCoreArgs args = ca;
-  args.q_plain = (strict && q_lo == nullptr) ? 1 : 0;
+            make_map_3d(&mvh, v_hi, dt, n, 32, nh, (uint64_t)ldv * esz, (uint64_t)ldv * esz * 32,
+                        vkeys, 32, 1, vsw);
   if (strict)
-    ok = ok &&
-         make_map_3d(&mql, args.q_plain ? q_hi : q_lo, dt, 32, n, nh, rowb, rowb * n, 32, 128,
-                     1, qsw) &&
-         make_map_3d(&mkl, k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
+    ok = ok && make_map_3d(&mkl, k_lo, dt, 32, n, nh, rowb, rowb * n, 32, bkv, 1, qsw) &&
          make_map_3d(&mvl, v_lo, dt, n, 32, nh, (uint64_t)ldv * esz, (uint64_t)ldv * esz * 32,
                      vkeys, 32, 1, vsw);
   else {
-    mql = mqh;
     mkl = mkh;
     mvl = mvh;
   }
   if (!ok) return kErrArg;
   dim3 grid((n + 127) / 128, kHeads, rows);
   if (strict) {
-    auto k = attn_core_kernel<true>;
-    if (int smem_st = set_max_smem(k, AttnCfg<true>::SMEM)) return smem_st;
+    auto kern = attn_core_kernel<true>;
+    if (int smem_st = set_max_smem(kern, AttnCfg<true>::SMEM)) return smem_st;
     FPB_LAUNCH("triattn_core", stream,
-               k<<<grid, AttnCfg<true>::THREADS, AttnCfg<true>::SMEM, stream>>>(
-                   mqh, mql, mkh, mkl, mvh, mvl, args));
+               kern<<<grid, AttnCfg<true>::THREADS, AttnCfg<true>::SMEM, stream>>>(
+                   mq, mkh, mkl, mvh, mvl, ca));
   } else {
-    auto k = attn_core_kernel<false>;
-    if (int smem_st = set_max_smem(k, AttnCfg<false>::SMEM)) return smem_st;
+    auto kern = attn_core_kernel<false>;
+    if (int smem_st = set_max_smem(kern, AttnCfg<false>::SMEM)) return smem_st;
     FPB_LAUNCH("triattn_core", stream,
-               k<<<grid, AttnCfg<false>::THREADS, AttnCfg<false>::SMEM, stream>>>(
-                   mqh, mql, mkh, mkl, mvh, mvl, args));
+               kern<<<grid, AttnCfg<false>::THREADS, AttnCfg<false>::SMEM, stream>>>(
+                   mq, mkh, mkl, mvh, mvl, ca));
   }
   return launch_status();
 }
 
 // ============================================================================
-// 3. gate + output projection + residual
+// 3. output projection + residual
 // ============================================================================
 struct AttnOutArgs {
   float* z;
   float* delta;  // when non-null: write the update here and leave z unchanged
   int n;
   int rows;      // pair rows of y owned by this call (n unsharded)
-  float eps;
-  const float* ln_w;
-  const float* ln_b;
-  const float* b_g;  // [128] or null
   const float* b_o;  // [128] or null
-  const void* o;     // [n*n][128] y coordinates
   int* status;
 };
 
@@ -1039,27 +1074,25 @@ constexpr int attn_out_smem_bytes() {
   return tmem_safe_smem(C::A_BYTES + 2 * C::WSTAGE_BYTES + 1024 + 256 + 1024, 256);
 }
 
-// Gate, output projection and residual over tiles of 128 pair rows of y
-// (y row r, columns s0..), persistent and warp-specialised:
-//   A warps (0-3):        strict: the tile's z rows by TMA into A, LayerNorm
-//                         in place (fast: LayerNorm from global rows); after
-//                         GEMM 1: A = sigmoid(gate + b_g) * o (o from
-//                         global, one 32-channel chunk ahead);
-//   epilogue warps (4-7): y = GEMM 2 + b_o from TMEM, released to the next
-//                         GEMM 2 after its last read, residual added, rows
-//                         stored to z (or delta) while the next tile runs;
-//   TMA warp (8):         the weight ring [W_g; W_o], continuous across tiles;
-//   MMA warp (9):         GEMM 1 (gate) into TMEM columns [0, 128), GEMM 2
-//                         into [128, 256) once the epilogue has read the
-//                         previous y (which keeps every barrier in lockstep:
-//                         none can complete two phases ahead of a waiter).
+// Output projection and residual over tiles of 128 pair rows of y (y row r,
+// columns s0..), persistent and warp-specialised. The gated attention output
+// g * o (the attention core applied the gate) is the A operand as it is:
+//   A warps (0-3):        the tile's g * o rows by TMA into A once the
+//                         previous tile's MMAs have read it (fast: BF16 rows
+//                         straight into the operand layout; strict: FP32 rows
+//                         into the lo half, split into tf32 hi / lo in place);
+//   epilogue warps (4-7): y = (g * o) W_o^T + b_o from TMEM (two buffers, so
+//                         the next tile's MMAs run during this epilogue),
+//                         residual added, rows stored to z (or delta);
+//   TMA warp (8):         the W_o ring, continuous across tiles;
+//   MMA warp (9):         one GEMM per tile into TMEM buffer tile % 2.
 // z rows read and written by a tile are its own (row r * n + s, or s * n + r
 // transposed), so tiles in flight never touch each other's rows.
 template <bool kStrict, bool kTrans>
 __global__ void __launch_bounds__(320, 1)
     attn_out_kernel(const __grid_constant__ CUtensorMap w_hi,
                     const __grid_constant__ CUtensorMap w_lo,
-                    const __grid_constant__ CUtensorMap zmap, AttnOutArgs p) {
+                    const __grid_constant__ CUtensorMap omap, AttnOutArgs p) {
   using C = RowCfg<kStrict>;
   constexpr int WSTAGES = 2;
   extern __shared__ uint8_t smem_raw[];
@@ -1067,17 +1100,16 @@ __global__ void __launch_bounds__(320, 1)
                                              ~uintptr_t(1023));
   uint8_t* A = smem;
   uint8_t* W = smem + C::A_BYTES;
-  float* bvec = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // b_g, b_o
+  float* bvec = reinterpret_cast<float*>(W + WSTAGES * C::WSTAGE_BYTES);  // b_o
   uint64_t* bars = reinterpret_cast<uint64_t*>(bvec + 256);
   uint64_t* wfull = bars;
   uint64_t* wempty = bars + WSTAGES;
-  uint64_t* a1_full = bars + 2 * WSTAGES;  // LN(z) in A
-  uint64_t* g1_done = a1_full + 1;         // gate in TMEM, A free for gate * o
-  uint64_t* a2_full = g1_done + 1;         // gate * o in A
-  uint64_t* g2_done = a2_full + 1;         // y in TMEM, A free for the next tile
-  uint64_t* y_free = g2_done + 1;          // y read by the epilogue
-  uint64_t* z_full = y_free + 1;           // strict: raw z rows in A (TMA)
-  uint64_t* drain = z_full + 1;
+  uint64_t* o_full = bars + 2 * WSTAGES;  // g * o rows in A (TMA)
+  uint64_t* a_full = o_full + 1;          // A ready for the MMAs
+  uint64_t* a_free = a_full + 1;          // the tile's MMAs have read A
+  uint64_t* y_full = a_free + 1;          // [2] y of the tile in TMEM buffer b
+  uint64_t* y_free = y_full + 2;          // [2] buffer b read by the epilogue
+  uint64_t* drain = y_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -1091,20 +1123,18 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&wfull[s], 1);
       mbar_init(&wempty[s], 1);
     }
-    mbar_init(a1_full, 128);
-    mbar_init(g1_done, 1);
-    mbar_init(a2_full, 128);
-    mbar_init(g2_done, 1);
-    mbar_init(y_free, 128);
-    mbar_init(z_full, 1);
+    mbar_init(o_full, 1);
+    mbar_init(a_full, 128);
+    mbar_init(a_free, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&y_full[b], 1);
+      mbar_init(&y_free[b], 128);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x < 128) {
-    bvec[threadIdx.x] = p.b_g ? p.b_g[threadIdx.x] : 0.f;
-    bvec[128 + threadIdx.x] = p.b_o ? p.b_o[threadIdx.x] : 0.f;
-  }
+  if (threadIdx.x < 128) bvec[threadIdx.x] = p.b_o ? p.b_o[threadIdx.x] : 0.f;
   if (warp == 9) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -1115,108 +1145,27 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_slot;
   const Guard g{p.status, abort_flag};
   const WRing ring{W, wfull, wempty, WSTAGES, C::WSTAGE_BYTES};
-  constexpr int NLOADS = 2 * C::NKA;
 
   if (warp < 4) {
     // ---------------------------------------------------------------- A warps
-    const float4 lw = reinterpret_cast<const float4*>(p.ln_w)[lane];
-    const float4 lb = reinterpret_cast<const float4*>(p.ln_b)[lane];
-    const float4* z4 = reinterpret_cast<const float4*>(p.z);
-    const int t = warp * 32 + lane;
 #pragma unroll 1
     for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
       const int r = tile / njb, s0 = (tile % njb) * 128;
-      // this row's o into L2 now: its chunks are read one at a time after
-      // GEMM 1, each a dependent global load
-      if (s0 + t < n)
-        prefetch_l2(static_cast<const uint8_t*>(p.o) +
-                        ((long long)r * n + s0 + t) * 128 * (kStrict ? 4 : 2),
-                    128 * (kStrict ? 4 : 2));
-      // A is free once GEMM 2 of the previous tile has read it
-      if (it > 0 && !mbar_wait(g2_done, (it - 1) & 1, g, 5)) break;
-      if constexpr (kStrict) {
-        if (threadIdx.x == 0) {
-          mbar_arrive_expect_tx(z_full, C::A_SPLIT_BYTES);
+      // A is free once the previous tile's MMAs have read it
+      if (it > 0 && !mbar_wait(a_free, (it - 1) & 1, g, 5)) break;
+      if (threadIdx.x == 0) {
+        // rows s0.. of y row r; rows past n are zero-filled
+        mbar_arrive_expect_tx(o_full, C::A_SPLIT_BYTES);
+        uint8_t* dst = kStrict ? A + C::A_SPLIT_BYTES : A;
 #pragma unroll
-          for (int a = 0; a < C::NKA; ++a)
-            tma_load_3d(A + C::A_SPLIT_BYTES + a * C::ATOM_BYTES, &zmap, z_full, a * C::KATOM,
-                        kTrans ? r : s0, kTrans ? s0 : r);
-        }
-        if (!mbar_wait(z_full, it & 1, g, 7)) break;
-        ln_smem_rows_to_a<32>(A, warp * 32, lw, lb, p.eps, NoRowHook{});
-      } else {
-        auto src = [&](int row) -> const float4* {
-          const int s = s0 + row;
-          if (s >= n) return nullptr;
-          return z4 + (kTrans ? ((long long)s * n + r) : ((long long)r * n + s)) * 32;
-        };
-        ln_rows_to_a<kStrict, 16, false>(A, warp * 32, src, lw, lb, p.eps, NoRowHook{});
+        for (int a = 0; a < C::NKA; ++a)
+          tma_load_3d(dst + a * C::ATOM_BYTES, &omap, o_full, a * C::KATOM, s0, r);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(a1_full);
-
-      // gate * o of this thread's row into A once GEMM 1 is done
-      const bool valid = s0 + t < n;
-      const long long pr = (long long)r * n + (valid ? s0 + t : 0);  // y pair (o row)
-      auto load_o = [&](int cc, float (&ov)[32]) {
-        if (!valid) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
-          return;
-        }
-        if constexpr (kStrict) {
-          const float4* src =
-              reinterpret_cast<const float4*>(static_cast<const float*>(p.o) + pr * 128 + cc * 32);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float4 v = __ldg(src + e);
-            ov[4 * e] = v.x;
-            ov[4 * e + 1] = v.y;
-            ov[4 * e + 2] = v.z;
-            ov[4 * e + 3] = v.w;
-          }
-        } else {
-          const uint4* src = reinterpret_cast<const uint4*>(
-              static_cast<const __nv_bfloat16*>(p.o) + pr * 128 + cc * 32);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint4 v = __ldg(src + e);
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-              ov[8 * e + 2 * u] = __bfloat162float(b2.x);
-              ov[8 * e + 2 * u + 1] = __bfloat162float(b2.y);
-            }
-          }
-        }
-      };
-      float ocur[32];
-      load_o(0, ocur);
-      if (!mbar_wait(g1_done, it & 1, g, 8)) break;
-      tc_fence_after();
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        float onext[32];
-        if (cc < 3) load_o(cc + 1, onext);
-        float gv[32];
-        tmem_row32(tmem, warp, cc * 32, gv);
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const int c = cc * 32 + e;
-          a_store4<kStrict>(A, t, c, sigmoidf_(gv[e] + bvec[c]) * ocur[e],
-                            sigmoidf_(gv[e + 1] + bvec[c + 1]) * ocur[e + 1],
-                            sigmoidf_(gv[e + 2] + bvec[c + 2]) * ocur[e + 2],
-                            sigmoidf_(gv[e + 3] + bvec[c + 3]) * ocur[e + 3]);
-        }
-        if (cc < 3) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ocur[e] = onext[e];
-        }
-      }
+      if (!mbar_wait(o_full, it & 1, g, 7)) break;
+      if constexpr (kStrict) split_smem_rows_to_a<32>(A, warp * 32);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(a2_full);
+      mbar_arrive(a_full);
     }
   } else if (warp < 8) {
     // ---------------------------------------------------------------- epilogue
@@ -1226,6 +1175,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll 1
     for (int it = 0, tile = blockIdx.x; tile < ntiles; ++it, tile += gridDim.x) {
       const int r = tile / njb, s0 = (tile % njb) * 128;
+      const int b = it & 1;
       const bool valid = s0 + t < n;
       const long long zrow_idx =
           kTrans ? (long long)(valid ? s0 + t : 0) * n + r : (long long)r * n + (valid ? s0 + t : 0);
@@ -1236,9 +1186,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int v4 = 0; v4 < 8; ++v4)
         zc[v4] = (valid && residual) ? zrow[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (!mbar_wait(g2_done, it & 1, g, 3)) break;
+      if (!mbar_wait(&y_full[b], (it >> 1) & 1, g, 3)) break;
       tc_fence_after();
-      const uint32_t ycol = 128;
+      const uint32_t ycol = b * 128;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         float4 zn[8];
@@ -1251,17 +1201,17 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld_wait();
         if (cc == 3) {
           tc_fence_before();
-          mbar_arrive(y_free);  // GEMM 2 of the next tile may overwrite y
+          mbar_arrive(&y_free[b]);  // the MMAs of tile it + 2 may overwrite this buffer
         }
         if (valid) {
 #pragma unroll
           for (int v4 = 0; v4 < 8; ++v4) {
             float4 o = zc[v4];
             const int c = cc * 32 + 4 * v4;
-            o.x += __uint_as_float(yr[4 * v4]) + bvec[128 + c];
-            o.y += __uint_as_float(yr[4 * v4 + 1]) + bvec[129 + c];
-            o.z += __uint_as_float(yr[4 * v4 + 2]) + bvec[130 + c];
-            o.w += __uint_as_float(yr[4 * v4 + 3]) + bvec[131 + c];
+            o.x += __uint_as_float(yr[4 * v4]) + bvec[c];
+            o.y += __uint_as_float(yr[4 * v4 + 1]) + bvec[c + 1];
+            o.z += __uint_as_float(yr[4 * v4 + 2]) + bvec[c + 2];
+            o.w += __uint_as_float(yr[4 * v4 + 3]) + bvec[c + 3];
             drow[cc * 8 + v4] = o;
           }
         }
@@ -1274,9 +1224,8 @@ __global__ void __launch_bounds__(320, 1)
       int seq = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        for (int q = 0; q < NLOADS; ++q, ++seq) {
-          const int nc = q / C::NKA, ka = q % C::NKA;
-          if (!wring_push<kStrict>(ring, seq, &w_hi, &w_lo, ka * C::KATOM, nc * 128, g)) {
+        for (int ka = 0; ka < C::NKA; ++ka, ++seq) {
+          if (!wring_push<kStrict>(ring, seq, &w_hi, &w_lo, ka * C::KATOM, 0, g)) {
             ok = false;
             break;
           }
@@ -1291,30 +1240,30 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       int seq = 0;
       for (int it = 0, tile = blockIdx.x; tile < ntiles && ok; ++it, tile += gridDim.x) {
-        for (int gemm = 0; gemm < 2 && ok; ++gemm) {
-          if (!mbar_wait(gemm ? a2_full : a1_full, it & 1, g, 4)) {
-            ok = false;
-            break;
-          }
-          // GEMM 2 overwrites y once the epilogue has read the previous one
-          if (gemm == 1 && it >= 1 && !mbar_wait(y_free, (it - 1) & 1, g, 6)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + (gemm ? 128 : 0);
-          for (int ka = 0; ka < C::NKA; ++ka, ++seq) {
-            const uint32_t w = wring_wait(ring, seq, g);
-            if (!w) {
-              ok = false;
-              break;
-            }
-            mma_k_atom<kStrict>(d, a_hi + ka * C::ATOM_BYTES, a_lo + ka * C::ATOM_BYTES, w,
-                                w + C::ATOM_BYTES, idesc, ka == 0);
-            wring_release(ring, seq);
-          }
-          if (ok) umma_commit(gemm ? g2_done : g1_done);
+        const int b = it & 1;
+        if (!mbar_wait(a_full, it & 1, g, 4)) {
+          ok = false;
+          break;
         }
+        // buffer b is overwritten once the epilogue has read tile it - 2
+        if (it >= 2 && !mbar_wait(&y_free[b], ((it >> 1) - 1) & 1, g, 6)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int ka = 0; ka < C::NKA; ++ka, ++seq) {
+          const uint32_t w = wring_wait(ring, seq, g);
+          if (!w) {
+            ok = false;
+            break;
+          }
+          mma_k_atom<kStrict>(tmem + b * 128, a_hi + ka * C::ATOM_BYTES,
+                              a_lo + ka * C::ATOM_BYTES, w, w + C::ATOM_BYTES, idesc, ka == 0);
+          wring_release(ring, seq);
+        }
+        if (!ok) break;
+        umma_commit(a_free);
+        umma_commit(&y_full[b]);
       }
       if (!ok) {
         umma_commit(drain);
@@ -1334,26 +1283,28 @@ __global__ void __launch_bounds__(320, 1)
 // ============================================================================
 // host
 // ============================================================================
-// Workspace of one call: packed weights, q/k/v^T, mask bias, attention
-// output, and (unsharded calls only) the pair bias. `rows` = pair rows of y
-// owned by the call (n when unsharded).
+// Workspace of one call: packed weights, q/k/v^T, gate, mask bias, gated
+// attention output, and (unsharded calls only) the pair bias. `rows` = pair
+// rows of y owned by the call (n when unsharded).
 template <class Alloc>
 struct TriAttnPlan {
   void *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
-  void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr;
-  void *v_hi = nullptr, *v_lo = nullptr, *o = nullptr;
+  void *q = nullptr, *k_hi = nullptr, *k_lo = nullptr, *v_hi = nullptr, *v_lo = nullptr;
+  void *o = nullptr, *gate = nullptr;
   float *bias = nullptr, *mbias = nullptr;
   int ldv = 0, ldb = 0;
   void plan(Alloc& al, int n, int rows, bool strict, bool with_mask, bool own_bias) {
     auto take = [&](size_t c) -> void* {
       return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
     };
-    wp_hi = take(384 * 128);
-    if (strict) wp_lo = take(384 * 128);
-    wo_hi = take(256 * 128);
-    if (strict) wo_lo = take(256 * 128);
+    wp_hi = take(512 * 128);  // [Wq; Wk; Wv; Wg]
+    if (strict) wp_lo = take(512 * 128);
+    wo_hi = take(128 * 128);
+    if (strict) wo_lo = take(128 * 128);
     const size_t qk = (size_t)rows * n * 128;
-    q_hi = take(qk);  // strict: unsplit, split by the attention core
+    // q: FP32 (strict: split by the attention core while staging Q) or
+    // BF16; k, v^T: tf32 hi / lo (strict) or BF16
+    q = take(qk);
     k_hi = take(qk);
     if (strict) k_lo = take(qk);
     ldv = padded_ld(n, strict ? 4 : 2);
@@ -1367,23 +1318,25 @@ struct TriAttnPlan {
       kend = al.template take<int>((size_t)rows);
     }
     o = take((size_t)rows * n * 128);
+    gate = take((size_t)rows * n * 128);
   }
   int* kend = nullptr;
 };
 
-// phase 1: LN + q/k/v projection of the call's rows, pair bias of those rows
-// (written at their global rows of `bias`), mask bias
+// phase 1: LN + q/k/v/gate projection of the call's rows, pair bias of
+// those rows (written at their global rows of `bias`), mask bias
 template <class Plan>
 int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int n, int rows,
                      int r0, bool trans, const float* ln_w, const float* ln_b, const float* w_q,
-                     const float* w_k, const float* w_v, const float* w_bias, float eps,
-                     float* bias, bool strict, int* status, cudaStream_t stream) {
+                     const float* w_k, const float* w_v, const float* w_bias, const float* w_g,
+                     const float* b_g, float eps, float* bias, bool strict, int* status,
+                     cudaStream_t stream) {
   int st;
-  if ((st = pack_weights(PackSrc{{w_q, w_k, w_v, nullptr}, 3, 128}, pl.wp_hi, pl.wp_lo, strict,
+  if ((st = pack_weights(PackSrc{{w_q, w_k, w_v, w_g}, 4, 128}, pl.wp_hi, pl.wp_lo, strict,
                          stream)))
     return st;
   CUtensorMap mph, mpl;
-  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 384, strict, &mph, &mpl)) return kErrArg;
+  if (!make_weight_maps(pl.wp_hi, pl.wp_lo, 512, strict, &mph, &mpl)) return kErrArg;
   // raw z rows of a tile (strict): [128 rows][32 channels] boxes, rows past
   // n zero-filled; transposed: tile rows are rows of z at column r
   CUtensorMap zm{};
@@ -1398,8 +1351,8 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
   const int tiles = rows * ((n + 127) / 128);
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   AttnProjArgs pa{z_loc, mask, n, rows, r0, eps, ln_w, ln_b, w_bias,
-                  1.0f / sqrtf((float)kHeadDim), pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi,
-                  pl.v_lo, pl.ldv, bias, pl.ldb, pl.mbias, status};
+                  1.0f / sqrtf((float)kHeadDim), pl.q, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo,
+                  pl.ldv, bias, pl.ldb, pl.mbias, pl.gate, b_g, status};
   const int smem = strict ? attn_proj_smem_bytes<true>() : attn_proj_smem_bytes<false>();
   auto k = strict ? (trans ? attn_proj_kernel<true, true> : attn_proj_kernel<true, false>)
                   : (trans ? attn_proj_kernel<false, true> : attn_proj_kernel<false, false>);
@@ -1408,19 +1361,19 @@ int triattn_proj_run(const Plan& pl, const float* z_loc, const float* mask, int 
   return launch_status();
 }
 
-// phase 2: attention core over the call's rows (keys = all n) + gate, output
-// projection and residual (or delta) on those rows
+// phase 2: attention core over the call's rows (keys = all n; the gate is
+// applied to o in its epilogue) + output projection and residual (or delta)
+// on those rows
 template <class Plan>
 int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, int rows,
-                       bool trans, const float* bias, const float* ln_w, const float* ln_b,
-                       const float* w_g, const float* b_g, const float* w_o, const float* b_o,
-                       float eps, bool strict, int* status, cudaStream_t stream) {
+                       bool trans, const float* bias, const float* w_o, const float* b_o,
+                       bool strict, int* status, cudaStream_t stream) {
   int st;
-  if ((st = pack_weights(PackSrc{{w_g, w_o, nullptr, nullptr}, 2, 128}, pl.wo_hi, pl.wo_lo,
+  if ((st = pack_weights(PackSrc{{w_o, nullptr, nullptr, nullptr}, 1, 128}, pl.wo_hi, pl.wo_lo,
                          strict, stream)))
     return st;
   CUtensorMap moh, mol;
-  if (!make_weight_maps(pl.wo_hi, pl.wo_lo, 256, strict, &moh, &mol)) return kErrArg;
+  if (!make_weight_maps(pl.wo_hi, pl.wo_lo, 128, strict, &moh, &mol)) return kErrArg;
   {
     if (pl.kend) {
       FPB_LAUNCH("key_extent", stream,
@@ -1428,30 +1381,27 @@ int triattn_finish_run(const Plan& pl, float* z_loc, float* delta_out, int n, in
                                                                       pl.kend));
       if ((st = launch_status())) return st;
     }
-    AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0, 0, 0, pl.kend};
-    if ((st = launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, rows,
-                               pl.ldv, ca, strict, stream)))
+    AttnCoreArgs ca{n, bias, pl.mbias, pl.ldb, pl.o, status, 0, 0, pl.kend, pl.gate};
+    if ((st = launch_attn_core(pl.q, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, rows, pl.ldv, ca,
+                               strict, stream)))
       return st;
   }
-  AttnOutArgs oa{z_loc, delta_out, n, rows, eps, ln_w, ln_b, b_g, b_o, pl.o, status};
-  // raw z rows of a tile (strict LayerNorm by TMA): y row r = z row r, or
-  // z column r when transposed; rows past n zero-filled
-  CUtensorMap zm{};
-  if (strict) {
-    const uint64_t rowb = 128ull * 4, pitch = (uint64_t)n * rowb;
-    const bool zok = trans ? make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, rows,
-                                         n, rowb, pitch, 32, 1, 128)
-                           : make_map_3d(&zm, z_loc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, n,
-                                         rows, rowb, pitch, 32, 128, 1);
-    if (!zok) return kErrArg;
-  }
+  AttnOutArgs oa{z_loc, delta_out, n, rows, b_o, status};
+  // gated attention output, y coordinates [rows][n][128]: boxes of 128 rows
+  // x one 128-byte channel atom, rows past n zero-filled
+  const int esz = strict ? 4 : 2;
+  CUtensorMap om{};
+  if (!make_map_3d(&om, pl.o,
+                   strict ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 128,
+                   n, rows, 128ull * esz, 128ull * esz * n, 128 / esz, 128, 1))
+    return kErrArg;
   const int tiles = rows * ((n + 127) / 128);
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   const int smem = strict ? attn_out_smem_bytes<true>() : attn_out_smem_bytes<false>();
   auto k = strict ? (trans ? attn_out_kernel<true, true> : attn_out_kernel<true, false>)
                   : (trans ? attn_out_kernel<false, true> : attn_out_kernel<false, false>);
   if (int smem_st = set_max_smem(k, smem)) return smem_st;
-  FPB_LAUNCH("triattn_out", stream, k<<<grid, 320, smem, stream>>>(moh, mol, zm, oa));
+  FPB_LAUNCH("triattn_out", stream, k<<<grid, 320, smem, stream>>>(moh, mol, om, oa));
   return launch_status();
 }
 
@@ -1495,11 +1445,11 @@ extern "C" int fpb_triattn(float* z, float* delta_out, const float* mask, int n,
   int* status = static_cast<int*>(workspace);
   if (reset_status(workspace, stream)) return kErrCuda;
   const bool trans = !starting;
-  int st = triattn_proj_run(pl, z, mask, n, n, 0, trans, ln_w, ln_b, w_q, w_k, w_v, w_bias, eps,
-                            pl.bias, strict, status, stream);
+  int st = triattn_proj_run(pl, z, mask, n, n, 0, trans, ln_w, ln_b, w_q, w_k, w_v, w_bias, w_g,
+                            b_g, eps, pl.bias, strict, status, stream);
   if (st) return st;
-  return triattn_finish_run(pl, z, delta_out, n, n, trans, pl.bias, ln_w, ln_b, w_g, b_g, w_o,
-                            b_o, eps, strict, status, stream);
+  return triattn_finish_run(pl, z, delta_out, n, n, trans, pl.bias, w_o, b_o, strict, status,
+                            stream);
 }
 
 // ---------------------------------------------------------------- row-sharded phases
@@ -1520,10 +1470,12 @@ extern "C" size_t fpb_triattn_shard_workspace_size(int n, int rows, int precisio
 extern "C" int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int n, int rows,
                                       int r0, const float* ln_w, const float* ln_b,
                                       const float* w_q, const float* w_k, const float* w_v,
-                                      const float* w_bias, float eps, float* bias_full,
-                                      int precision, void* workspace, size_t workspace_bytes,
+                                      const float* w_bias, const float* w_g, const float* b_g,
+                                      float eps, float* bias_full, int precision,
+                                      void* workspace, size_t workspace_bytes,
                                       cudaStream_t stream) {
-  if (!z_loc || !bias_full || !workspace || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias)
+  if (!z_loc || !bias_full || !workspace || !ln_w || !ln_b || !w_q || !w_k || !w_v || !w_bias ||
+      !w_g)
     return kErrArg;
   if (precision != 0 && precision != 1) return kErrArg;
   if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
@@ -1538,20 +1490,17 @@ extern "C" int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int
   pl.plan(cur, n, rows, strict, with_mask, false);
   if (reset_status(workspace, stream)) return kErrCuda;
   return triattn_proj_run(pl, z_loc, mask, n, rows, r0, false, ln_w, ln_b, w_q, w_k, w_v, w_bias,
-                          eps, bias_full, strict, static_cast<int*>(workspace), stream);
+                          w_g, b_g, eps, bias_full, strict, static_cast<int*>(workspace), stream);
 }
 
 extern "C" int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, int rows,
-                                        int with_mask, const float* bias_full, const float* ln_w,
-                                        const float* ln_b, const float* w_g, const float* b_g,
-                                        const float* w_o, const float* b_o, float eps,
-                                        int precision, void* workspace, size_t workspace_bytes,
-                                        cudaStream_t stream) {
-  if (!z_loc || !bias_full || !workspace || !ln_w || !ln_b || !w_g || !w_o) return kErrArg;
+                                        int with_mask, const float* bias_full, const float* w_o,
+                                        const float* b_o, int precision, void* workspace,
+                                        size_t workspace_bytes, cudaStream_t stream) {
+  if (!z_loc || !bias_full || !workspace || !w_o) return kErrArg;
   if (precision != 0 && precision != 1) return kErrArg;
   if (n <= 0 || rows <= 0) return kErrShape;
-  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_w) || !aligned16(ln_b))
-    return kErrAlign;
+  if (!aligned16(z_loc) || !aligned16(workspace)) return kErrAlign;
   if (delta_out && !aligned16(delta_out)) return kErrAlign;
   const bool strict = precision == 0;
   if (workspace_bytes < fpb_triattn_shard_workspace_size(n, rows, precision, with_mask))
@@ -1559,8 +1508,8 @@ extern "C" int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, i
   WsCursor cur(workspace, workspace_bytes);
   TriAttnPlan<WsCursor> pl;
   pl.plan(cur, n, rows, strict, with_mask != 0, false);
-  return triattn_finish_run(pl, z_loc, delta_out, n, rows, false, bias_full, ln_w, ln_b, w_g, b_g,
-                            w_o, b_o, eps, strict, static_cast<int*>(workspace), stream);
+  return triattn_finish_run(pl, z_loc, delta_out, n, rows, false, bias_full, w_o, b_o, strict,
+                            static_cast<int*>(workspace), stream);
 }
 
 // ============================================================================
@@ -1568,10 +1517,12 @@ extern "C" int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, i
 // ============================================================================
 namespace fpb {
 
-// q or k [B, H, N, 32] (any strides) -> [(b*H + h)*N + j][32] split / bf16.
+// q or k [B, H, N, 32] (any strides) -> [(b*H + h)*N + j][32]: strict FP32
+// (lo == null: q, split by the core) or tf32 hi / lo (k); fast bf16.
 template <bool kStrict>
 __global__ void pack_qk_kernel(const float* __restrict__ src, long long s0, long long s1,
-                               long long s2, long long s3, int batch, int n, void* hi, void* lo) {
+                               long long s2, long long s3, int batch, int n, void* dst,
+                               void* lo) {
   const long long total = (long long)batch * kHeads * n * 32;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
        e += (long long)gridDim.x * blockDim.x) {
@@ -1583,20 +1534,25 @@ __global__ void pack_qk_kernel(const float* __restrict__ src, long long s0, long
     const long long b = bh / kHeads;
     const float v = src[b * s0 + h * s1 + j * s2 + d * s3];
     if constexpr (kStrict) {
-      float vh, vl;
-      split_tf32(v, vh, vl);
-      static_cast<float*>(hi)[e] = vh;
-      static_cast<float*>(lo)[e] = vl;
+      if (lo) {
+        float vh, vl;
+        split_tf32(v, vh, vl);
+        static_cast<float*>(dst)[e] = vh;
+        static_cast<float*>(lo)[e] = vl;
+      } else {
+        static_cast<float*>(dst)[e] = v;
+      }
     } else {
-      static_cast<__nv_bfloat16*>(hi)[e] = __float2bfloat16_rn(v);
+      static_cast<__nv_bfloat16*>(dst)[e] = __float2bfloat16_rn(v);
     }
   }
 }
 
-// v [B, H, N, 32] (any strides) -> v^T [(b*H + h)*32 + d][ldv], 32x32 tiles.
+// v [B, H, N, 32] (any strides) -> v^T [(b*H + h)*32 + d][ldv], 32x32 tiles,
+// tf32 hi / lo (strict) or bf16 (fast).
 template <bool kStrict>
 __global__ void pack_vt_kernel(const float* __restrict__ src, long long s0, long long s1,
-                               long long s2, long long s3, int n, int ldv, void* hi, void* lo) {
+                               long long s2, long long s3, int n, int ldv, void* dst, void* lo) {
   __shared__ float tile[32][33];
   const long long bh = blockIdx.y;
   const int k0 = blockIdx.x * 32;
@@ -1615,10 +1571,10 @@ __global__ void pack_vt_kernel(const float* __restrict__ src, long long s0, long
       if constexpr (kStrict) {
         float vh, vl;
         split_tf32(v, vh, vl);
-        static_cast<float*>(hi)[idx] = vh;
+        static_cast<float*>(dst)[idx] = vh;
         static_cast<float*>(lo)[idx] = vl;
       } else {
-        static_cast<__nv_bfloat16*>(hi)[idx] = __float2bfloat16_rn(v);
+        static_cast<__nv_bfloat16*>(dst)[idx] = __float2bfloat16_rn(v);
       }
     }
   }
@@ -1650,8 +1606,7 @@ __global__ void pack_bias_kernel(const float* __restrict__ tb, long long t1, lon
 
 template <class Alloc>
 struct CorePlan {
-  void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr, *v_hi = nullptr,
-       *v_lo = nullptr;
+  void *q = nullptr, *k_hi = nullptr, *k_lo = nullptr, *v_hi = nullptr, *v_lo = nullptr;
   float *bias = nullptr, *mbias = nullptr;
   int ldv = 0, ldb = 0;
   void plan(Alloc& al, int batch, int n, bool strict, bool with_mask) {
@@ -1659,12 +1614,9 @@ struct CorePlan {
       return strict ? (void*)al.template take<float>(c) : (void*)al.template take<__nv_bfloat16>(c);
     };
     const size_t qk = (size_t)batch * kHeads * n * 32;
-    q_hi = take(qk);
+    q = take(qk);
     k_hi = take(qk);
-    if (strict) {
-      q_lo = take(qk);
-      k_lo = take(qk);
-    }
+    if (strict) k_lo = take(qk);
     ldv = padded_ld(n, strict ? 4 : 2);
     const size_t vc = (size_t)batch * kHeads * 32 * ldv;
     v_hi = take(vc);
@@ -1719,25 +1671,25 @@ extern "C" int fpb_attention_core_ex(const float* q, const long long* q_strides,
   if (strict) {
     FPB_LAUNCH("pack_qkv", stream,
                pack_qk_kernel<true><<<1184, 256, 0, stream>>>(q, qs[0], qs[1], qs[2], qs[3], batch,
-                                                              n, pl.q_hi, pl.q_lo));
+                                                              n, pl.q, nullptr));
     FPB_LAUNCH("pack_qkv", stream,
                pack_qk_kernel<true><<<1184, 256, 0, stream>>>(k, ks[0], ks[1], ks[2], ks[3], batch,
                                                               n, pl.k_hi, pl.k_lo));
     FPB_LAUNCH("pack_qkv", stream,
                pack_vt_kernel<true><<<dim3((n + 31) / 32, batch * kHeads), dim3(32, 8), 0,
-                                      stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv,
-                                                pl.v_hi, pl.v_lo));
+                                      stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv, pl.v_hi,
+                                                pl.v_lo));
   } else {
     FPB_LAUNCH("pack_qkv", stream,
                pack_qk_kernel<false><<<1184, 256, 0, stream>>>(q, qs[0], qs[1], qs[2], qs[3],
-                                                               batch, n, pl.q_hi, nullptr));
+                                                               batch, n, pl.q, nullptr));
     FPB_LAUNCH("pack_qkv", stream,
                pack_qk_kernel<false><<<1184, 256, 0, stream>>>(k, ks[0], ks[1], ks[2], ks[3],
                                                                batch, n, pl.k_hi, nullptr));
     FPB_LAUNCH("pack_qkv", stream,
                pack_vt_kernel<false><<<dim3((n + 31) / 32, batch * kHeads), dim3(32, 8), 0,
-                                       stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv,
-                                                 pl.v_hi, nullptr));
+                                       stream>>>(v, vs[0], vs[1], vs[2], vs[3], n, pl.ldv, pl.v_hi,
+                                                 nullptr));
   }
   const long long* tb = tri_bias_strides;
   const long long* mbs = mask_bias_strides;
@@ -1748,10 +1700,10 @@ extern "C" int fpb_attention_core_ex(const float* q, const long long* q_strides,
                                                         pl.bias, pl.mbias));
   if ((st = launch_status())) return st;
   // this boundary returns FP32 [B, N, H, D] in both precision modes
-  AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1, 0,
+  AttnCoreArgs ca{n, pl.bias, pl.mbias, pl.ldb, out, static_cast<int*>(workspace), 1,
                   empty_rows_nan};
-  return launch_attn_core(pl.q_hi, pl.q_lo, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, batch, pl.ldv,
-                          ca, strict, stream);
+  return launch_attn_core(pl.q, pl.k_hi, pl.k_lo, pl.v_hi, pl.v_lo, n, batch, pl.ldv, ca, strict,
+                          stream);
 }
 
 extern "C" int fpb_attention_core(const float* q, const long long* q_strides, const float* k,

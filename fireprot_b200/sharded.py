@@ -275,10 +275,11 @@ class CudaPhases:
         dev = z_loc.device
         ws = self._ws_take("triattn", self.lib.fpb_triattn_shard_workspace_size(
             shard.n, shard.rows, self.p, int(mask is not None)), dev)
-        wt = [w[k].contiguous() for k in ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias")]
+        wt = [None if w.get(k) is None else w[k].contiguous()
+              for k in ("ln_w", "ln_b", "w_q", "w_k", "w_v", "w_bias", "w_g", "b_g")]
         _lib.check(self.lib.fpb_triattn_shard_proj(
             z_loc.data_ptr(), self._ptr(mask), shard.n, shard.rows, shard.r0,
-            *[t.data_ptr() for t in wt], self.eps, bias_full.data_ptr(), self.p, ws.data_ptr(),
+            *[self._ptr(t) for t in wt], self.eps, bias_full.data_ptr(), self.p, ws.data_ptr(),
             ws.numel(), ops._stream_ptr(dev)), "fpb_triattn_shard_proj")
         return ws
 
@@ -286,11 +287,10 @@ class CudaPhases:
         if shard.rows == 0:
             return
         ws = state
-        keep = [None if w.get(k) is None else w[k].contiguous()
-                for k in ("ln_w", "ln_b", "w_g", "b_g", "w_o", "b_o")]
+        keep = [None if w.get(k) is None else w[k].contiguous() for k in ("w_o", "b_o")]
         _lib.check(self.lib.fpb_triattn_shard_finish(
             z_loc.data_ptr(), 0, shard.n, shard.rows, int(bool(with_mask)), bias_full.data_ptr(),
-            *[self._ptr(t) for t in keep], self.eps, self.p, ws.data_ptr(), ws.numel(),
+            *[self._ptr(t) for t in keep], self.p, ws.data_ptr(), ws.numel(),
             ops._stream_ptr(z_loc.device)), "fpb_triattn_shard_finish")
 
     # ---------------------------------------------------------------- transition

@@ -260,11 +260,12 @@ int fpb_trimul_shard_finish(float* z_loc, int n, int rows, const void* x_blocked
                             float eps, int add, int precision, void* workspace,
                             size_t workspace_bytes, cudaStream_t stream);
 /* Triangle attention, starting-node form on the rank's rows: proj writes the
- * rank's rows of the pair bias; the caller all-gathers it; finish runs
- * attention + gate + output on the rows
- * (z_loc += delta, or delta_out = delta). The ending node is this form on the
- * transposed pair tensor (all-to-all transposes around it). proj and finish
- * share the workspace. The bias buffer is row-blocked: for ldb =
+ * rank's q/k/v and gate (LayerNorm and all four projections, so it takes
+ * w_g and b_g) and its rows of the pair bias; the caller all-gathers the
+ * bias; finish runs the attention core (gate applied to o) and the output
+ * projection on the rows (z_loc += delta, or delta_out = delta). The ending
+ * node is this form on the transposed pair tensor (all-to-all transposes
+ * around it). proj and finish share the workspace. The bias buffer is row-blocked: for ldb =
  * fpb_triattn_bias_ld(n), rows are grouped by 32, and rows [32q, 32q + 32m)
  * occupy the m*32*4*ldb floats starting at float q*32*4*ldb (so a rank whose
  * r0 and row chunk are multiples of 32 owns one contiguous range); the
@@ -273,14 +274,14 @@ size_t fpb_triattn_bias_ld(int n);
 size_t fpb_triattn_shard_workspace_size(int n, int rows, int precision, int with_mask);
 int fpb_triattn_shard_proj(const float* z_loc, const float* mask, int n, int rows, int r0,
                            const float* ln_w, const float* ln_b, const float* w_q,
-                           const float* w_k, const float* w_v, const float* w_bias, float eps,
-                           float* bias_full, int precision, void* workspace,
-                           size_t workspace_bytes, cudaStream_t stream);
+                           const float* w_k, const float* w_v, const float* w_bias,
+                           const float* w_g, const float* b_g, float eps, float* bias_full,
+                           int precision, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream);
 int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, int rows, int with_mask,
-                             const float* bias_full, const float* ln_w, const float* ln_b,
-                             const float* w_g, const float* b_g, const float* w_o,
-                             const float* b_o, float eps, int precision, void* workspace,
-                             size_t workspace_bytes, cudaStream_t stream);
+                             const float* bias_full, const float* w_o, const float* b_o,
+                             int precision, void* workspace, size_t workspace_bytes,
+                             cudaStream_t stream);
 
 /* Weights of the five pair operators of one block (torch Linear layouts). */
 typedef struct {

@@ -282,12 +282,23 @@ def run_reference(args, world, rank):
 
 
 def _config(args):
-    return {"workload": (f"one Pairformer block: pair stack (TriMul out/in, TriAttn start/end "
-                         f"H=4 d=32, pair transition) and single stack (attention with pair "
-                         f"bias H=16 d=24, single transition), N={args.n}, c_z=128, c_s=384, "
-                         f"{args.precision} precision, padding mask valid {args.valid}"),
+    if args.trunk > 1:
+        what = (f"{args.trunk}-block Pairformer trunk (distinct random-init blocks), each block a "
+                f"pair stack (TriMul out/in, TriAttn start/end H=4 d=32, pair transition) and "
+                f"single stack (attention with pair bias H=16 d=24, single transition)")
+    else:
+        what = ("one Pairformer block: pair stack (TriMul out/in, TriAttn start/end H=4 d=32, "
+                "pair transition) and single stack (attention with pair bias H=16 d=24, single "
+                "transition)")
+    masking = (f"padding mask with a per-sample valid length drawn uniformly from "
+               f"[{args.valid_range[0]}, {args.valid_range[1]}] (seeded, one sample per step)"
+               if args.valid_range else f"padding mask valid {args.valid}")
+    return {"workload": (f"{args.config}: {what}, N={args.n}, c_z=128, c_s=384, "
+                         f"{args.precision} precision, {masking}"),
+            "config": args.config,
             "n": args.n, "c_z": C, "c_s": CS, "precision": args.precision,
-            "valid_length": args.valid,
+            "valid_length": (list(args.valid_range) if args.valid_range else args.valid),
+            "blocks_per_step": args.trunk,
             "l2": "inputs larger than L2 (z alone is %.2f GB)" % (args.n ** 2 * C * 4 / 1e9),
             "parallelism": ("single GPU" if args.gpus == 1 else
                             f"rows of z sharded over {args.gpus} GPUs (NCCL all-gather, "
@@ -372,15 +383,40 @@ def run_ours(args, world, rank, local):
     s_host = torch.randn(n, CS, generator=gen).pin_memory()
     valid = torch.arange(n) < args.valid
     mask_host = (valid[:, None] & valid[None, :]).float().pin_memory()
-    block = PairformerBlock().init_random_(seed=1 + seed).to(dev)
+    blocks = [PairformerBlock().init_random_(seed=1 + seed + 7 * b).to(dev)
+              for b in range(args.trunk)]
+    block = blocks[0]
     mask = mask_host.to(dev)
+    # per-sample valid lengths (config 4): one sample per step, seeded
+    n_samples = args.warmup + args.steps + args.e2e_steps + 4
+    if args.valid_range:
+        lo, hi = args.valid_range
+        vgen = torch.Generator().manual_seed(4)
+        lengths = torch.randint(lo, hi + 1, (n_samples,), generator=vgen).tolist()
+    else:
+        lengths = [args.valid] * n_samples
+    mask_cache = {}
+    host_mask_cache = {}
+
+    def host_mask_for(k):
+        v = min(n, lengths[k % len(lengths)])
+        if v not in host_mask_cache:
+            keep = torch.arange(n) < v
+            host_mask_cache[v] = (keep[:, None] & keep[None, :]).float().pin_memory()
+        return host_mask_cache[v]
+
+    def mask_for(k):
+        v = min(n, lengths[k % len(lengths)])
+        if v not in mask_cache:
+            keep = torch.arange(n, device=dev) < v
+            mask_cache[v] = (keep[:, None] & keep[None, :]).float()
+        return mask_cache[v]
 
     if sharded:
         from fireprot_b200 import sharded as S
         shard = S.shard_plan(n, world, rank)
         comm = S.DistComm()
-        weights = S.block_weight_dicts(block.pair)
-        w_single = block.single.weight_dict()
+        weights = [(S.block_weight_dicts(b.pair), b.single.weight_dict()) for b in blocks]
         z_host = S.local_rows(z_full, shard).pin_memory()
         rows_frac = shard.rows / n
         scheme = _trimul_scheme(args)
@@ -390,15 +426,16 @@ def run_ours(args, world, rank, local):
 
             def step(zz, ss, mm):
                 # ss: [W * chunk, 384] all-gather buffer holding s in its first n rows
-                S.sharded_pair_block(zz, mm, weights, shard, comm, phases, scheme=scheme)
-                S.sharded_single_block(ss, zz, mm, w_single, shard, comm, phases)
+                for w_pair, w_single in weights:
+                    S.sharded_pair_block(zz, mm, w_pair, shard, comm, phases, scheme=scheme)
+                    S.sharded_single_block(ss, zz, mm, w_single, shard, comm, phases)
             return step, phases.check
 
         def s_device(src):
             return S.single_buffer(src.to(dev), shard)
     else:
         z_host = z_full.pin_memory()
-        cw, cw_single = block.pair.c_weights(), block.single.c_weights()
+        cws = [(b.pair.c_weights(), b.single.c_weights()) for b in blocks]
         rows_frac = 1.0
 
         def make_step(precision):
@@ -406,9 +443,10 @@ def run_ours(args, world, rank, local):
             ws_single = ops.single_block_workspace(n, n, dev)
 
             def step(zz, ss, mm):
-                ops.pair_block(zz, mm, cw, precision=precision, workspace=ws)
-                ops.single_block(ss, zz, mm, cw_single, precision=precision,
-                                 workspace=ws_single)
+                for cw, cw_single in cws:
+                    ops.pair_block(zz, mm, cw, precision=precision, workspace=ws)
+                    ops.single_block(ss, zz, mm, cw_single, precision=precision,
+                                     workspace=ws_single)
 
             def check():
                 for w in (ws, ws_single):
@@ -420,21 +458,24 @@ def run_ours(args, world, rank, local):
         def s_device(src):
             return src.to(dev)
     del z_full
-    blocks_per_step = 1 if sharded else world
+    blocks_per_step = args.trunk * (1 if sharded else world)
     z = z_host.to(dev)
     s_dev = s_device(s_host)
     stream = torch.cuda.current_stream(dev)
     step_fn, check = make_step(args.precision)
 
-    def step(zz):
-        step_fn(zz, s_dev, mask)
+    def step(zz, k):
+        step_fn(zz, s_dev, mask_for(k))
 
     if args.precision == "strict":
         measure_tf32_tflops(dev)
 
-    # ---- warm-up
-    for _ in range(args.warmup):
-        step(z)
+    # ---- warm-up (every sample's mask is built here, outside the timed region)
+    for k in range(n_samples):
+        mask_for(k)
+        host_mask_for(k)
+    for k in range(args.warmup):
+        step(z, k)
     torch.cuda.synchronize(dev)
     check()
 
@@ -454,8 +495,8 @@ def run_ours(args, world, rank, local):
     ops.timing_enable(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        step(z)
+    for k in range(args.steps):
+        step(z, args.warmup + k)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     kernels = ops.timing_collect()
@@ -497,7 +538,7 @@ def run_ours(args, world, rank, local):
                 h2d_s.wait_event(drained[b])
             zbuf[b].copy_(z_host, non_blocking=True)
             sbuf[b][:n].copy_(s_host, non_blocking=True)
-            mbuf[b].copy_(mask_host, non_blocking=True)
+            mbuf[b].copy_(host_mask_for(args.warmup + args.steps + k), non_blocking=True)
             loaded[b].record(h2d_s)
         stream.wait_event(loaded[b])
         step_fn(zbuf[b], sbuf[b], mbuf[b])
@@ -610,6 +651,17 @@ def run_ours(args, world, rank, local):
     }
 
 
+# BASELINE.json workloads. c3 (the metric's N=1536 strict block, padding
+# mask valid 1480) is the default; c1 (N=124 on CPU) is a parity case.
+CONFIGS = {
+    "c2": {"n": 1000, "valid": 1000, "precision": "strict"},
+    "c3": {"n": 1536, "valid": 1480, "precision": "strict"},
+    "c4": {"n": 1536, "valid": 1480, "precision": "fast", "trunk": 48,
+           "valid_range": [1400, 1536], "e2e_steps": 2},
+    "c5": {"n": 3072, "valid": 3072, "precision": "strict"},
+}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -627,7 +679,23 @@ def main():
                     help="N>1 sharded: TriMul exchange (auto: channels from 4 GPUs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3",
+                    help="BASELINE workload preset (c3, the metric's N=1536 strict block, is the "
+                         "default; the others set --n/--valid/--precision/--trunk as described "
+                         "in CONFIGS)")
+    ap.add_argument("--trunk", type=int, default=None,
+                    help="distinct blocks per step (a trunk pass); default from --config")
+    ap.add_argument("--valid-range", type=int, nargs=2, default=None, metavar=("LO", "HI"),
+                    help="per-sample valid length drawn from [LO, HI], one sample per step")
     args = ap.parse_args()
+    preset = CONFIGS[args.config]
+    explicit = {a.lstrip("-").split("=")[0].replace("-", "_") for a in sys.argv[1:]
+                if a.startswith("--")}
+    for key, val in preset.items():
+        if key not in explicit:
+            setattr(args, key, val)
+    if args.trunk is None:
+        args.trunk = 1
     world, rank, local = dist_setup()
     if world > 1 and args.gpus != world:
         args.gpus = world

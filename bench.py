@@ -301,11 +301,18 @@ def _config(args):
             "blocks_per_step": args.trunk,
             "l2": "inputs larger than L2 (z alone is %.2f GB)" % (args.n ** 2 * C * 4 / 1e9),
             "parallelism": ("single GPU" if args.gpus == 1 else
-                            f"rows of z sharded over {args.gpus} GPUs (NCCL all-gather, "
-                            f"reduce-scatter, all-to-all)" if args.mode == "sharded" else
+                            f"rows of z sharded over {args.gpus} GPUs ({_TRANSPORT[args.comm]})"
+                            if args.mode == "sharded" else
                             f"independent replicas x{args.gpus}"),
-            **({"trimul_exchange": _trimul_scheme(args)}
+            **({"trimul_exchange": _trimul_scheme(args), "transport": args.comm}
                if args.gpus > 1 and args.mode == "sharded" else {})}
+
+
+_TRANSPORT = {
+    "nccl": "NCCL all-gather, reduce-scatter, all-to-all",
+    "peer": "peer-memory copies and a fused transpose kernel over NVLink, NCCL barriers",
+}
+_TO_CLOSE = []  # peer transports to unmap before the process group goes
 
 
 def _trimul_scheme(args):
@@ -415,7 +422,9 @@ def run_ours(args, world, rank, local):
     if sharded:
         from fireprot_b200 import sharded as S
         shard = S.shard_plan(n, world, rank)
-        comm = S.DistComm()
+        comm = S.PeerComm() if args.comm == "peer" else S.DistComm()
+        if args.comm == "peer":
+            _TO_CLOSE.append(comm)
         weights = [(S.block_weight_dicts(b.pair), b.single.weight_dict()) for b in blocks]
         z_host = S.local_rows(z_full, shard).pin_memory()
         rows_frac = shard.rows / n
@@ -677,6 +686,8 @@ def main():
                     help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
     ap.add_argument("--trimul-scheme", choices=["auto", "rows", "channels"], default="auto",
                     help="N>1 sharded: TriMul exchange (auto: channels from 4 GPUs)")
+    ap.add_argument("--comm", choices=["nccl", "peer"], default="nccl",
+                    help="N>1 sharded: exchange transport (NCCL collectives or peer memory)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3",
@@ -709,6 +720,10 @@ def main():
     finally:
         if world > 1:
             import torch.distributed as dist
+            if _TO_CLOSE:
+                torch.cuda.synchronize()
+                for c in _TO_CLOSE:
+                    c.close()
             dist.destroy_process_group()
 
 

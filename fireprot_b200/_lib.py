@@ -86,6 +86,14 @@ SIGNATURES = {
                                + [c_float, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_triattn_shard_finish": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
                                  + [c_void_p] * 2 + [c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_ipc_handle_bytes": (c_size_t, []),
+    "fpb_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_size_t)]),
+    "fpb_ipc_import": (c_int, [c_void_p, c_size_t, ctypes.POINTER(c_void_p),
+                               ctypes.POINTER(c_void_p)]),
+    "fpb_ipc_close": (c_int, [c_void_p]),
+    "fpb_copy_async": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "fpb_peer_transpose_rows": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                        c_void_p]),
     "fpb_registry_new": (c_void_p, []),
     "fpb_registry_free": (None, [c_void_p]),
     "fpb_registry_register": (c_int, [c_void_p, c_char_p, CAPABILITY_FN, c_void_p]),

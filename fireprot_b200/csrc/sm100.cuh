@@ -127,6 +127,13 @@ __device__ __forceinline__ void prefetch_l2(const void* p, int bytes) {
   for (int o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
 }
 
+// One bulk L2 prefetch of a contiguous range (PTX cp.async.bulk.prefetch.L2):
+// p 16-byte aligned, bytes a multiple of 16. Issued by one thread; nothing
+// waits for it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

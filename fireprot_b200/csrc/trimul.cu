@@ -494,7 +494,20 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 4) {
     if (lane == 0) {
       int issued = 0;
+      // Bulk L2 prefetch of a tile's z rows and x block (each one contiguous
+      // range): the row warps then read them from L2 instead of DRAM, which
+      // their few loads in flight could not keep busy.
+      auto prefetch_tile = [&](int tile) {
+        const int jb = tile % p.njb;
+        const long long p0 = (long long)(tile / p.njb) * n + jb * 128;
+        bulk_prefetch_l2(static_cast<const float*>(p.z) + p0 * 128,
+                         (uint32_t)min(128, n - jb * 128) * 512u);
+        const size_t xb = (size_t)128 * 128 * C::ESZ;
+        bulk_prefetch_l2(static_cast<const uint8_t*>(p.x) + (size_t)tile * xb, (uint32_t)xb);
+      };
+      if (nmine > 0) prefetch_tile(blockIdx.x);
       for (int it = 0; it < nmine; ++it) {
+        if (it + 1 < nmine) prefetch_tile(blockIdx.x + (it + 1) * gridDim.x);
         bool pushed = true;
         for (int q = 0; q < NLOADS; ++q) {
           const int nc = q / C::NKA, ka = q % C::NKA;

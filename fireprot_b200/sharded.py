@@ -36,6 +36,7 @@ the three collectives so the orchestration is independent of the transport.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -103,6 +104,181 @@ class DistComm:
         self._dist.all_to_all_single(out.view(-1), inp.reshape(-1), group=self.group)
 
 
+class PeerComm:
+    """The exchanges over CUDA peer memory between the GPUs of one node.
+
+    Every rank registers the receive buffers once (an IPC handle per buffer,
+    swapped with ``all_gather_object``; the peers map them into their own
+    context), after which an all-to-all or all-gather is one copy per peer,
+    written straight into the peer's buffer over NVLink by the copy engines
+    (one stream per peer, so the copies run side by side), and the
+    transposed exchange of the ending-node operator is one kernel
+    (``fpb_peer_transpose_rows``) that stores each 512-byte channel vector
+    at its transposed place on its owner: no packing, staging or unpacking
+    pass. A one-element NCCL all-reduce on the current stream before the
+    copies (every peer is done with the buffer's previous contents) and
+    after them (every peer's copies into this rank have landed) orders the
+    transfers; the reduce-scatter of the row TriMul scheme stays on NCCL.
+
+    A buffer obtained from ``recv_buffer`` is filled in place; any other
+    destination is filled through a registered scratch buffer plus one local
+    copy. Registered buffers live as long as the object: ``close()`` unmaps
+    the peers' buffers (call it, after a device synchronise, before the
+    process group is destroyed)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self._dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nccl = DistComm(group)
+        self.lib = _lib.load()
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self._tick = torch.zeros(1, device=self.dev)
+        self._bufs: dict = {}     # tag -> (tensor, [device pointer per rank])
+        self._by_ptr: dict = {}   # data_ptr -> tag
+        self._opened: dict = {}   # handle bytes -> mapped base (peer segments)
+        self._retired: list = []  # replaced buffers: peers may still map them
+        self._streams = [torch.cuda.Stream(self.dev) for _ in range(self.world)]
+        self._hbytes = int(self.lib.fpb_ipc_handle_bytes())
+
+    # -- registration -----------------------------------------------------
+    def _register(self, tag, shape, dtype):
+        t = torch.zeros(shape, dtype=dtype, device=self.dev)
+        handle = ctypes.create_string_buffer(self._hbytes)
+        off = ctypes.c_size_t(0)
+        _lib.check(self.lib.fpb_ipc_export(ctypes.c_void_p(t.data_ptr()), handle,
+                                           ctypes.byref(off)), "fpb_ipc_export")
+        mine = (bytes(handle.raw), int(off.value), t.numel() * t.element_size())
+        got = [None] * self.world
+        self._dist.all_gather_object(got, mine, group=self.group)
+        ptrs = []
+        for r, (h, o, nbytes) in enumerate(got):
+            if nbytes != mine[2]:
+                raise RuntimeError(f"peer buffer {tag!r}: rank {r} registered {nbytes} bytes, "
+                                   f"rank {self.rank} {mine[2]}")
+            if r == self.rank:
+                ptrs.append(t.data_ptr())
+                continue
+            base = self._opened.get(h)
+            ptr = ctypes.c_void_p()
+            if base is None:
+                b = ctypes.c_void_p()
+                _lib.check(self.lib.fpb_ipc_import(h, o, ctypes.byref(b), ctypes.byref(ptr)),
+                           "fpb_ipc_import")
+                self._opened[h] = base = b.value
+            ptrs.append(base + o)
+        old = self._bufs.get(tag)
+        if old is not None:
+            self._by_ptr.pop(old[0].data_ptr(), None)
+            self._retired.append(old)
+        self._bufs[tag] = (t, ptrs)
+        self._by_ptr[t.data_ptr()] = tag
+        return t, ptrs
+
+    def _buffer(self, tag, shape, dtype):
+        ent = self._bufs.get(tag)
+        if ent is None or ent[0].dtype != dtype or tuple(ent[0].shape) != tuple(shape):
+            ent = self._register(tag, tuple(shape), dtype)
+        return ent
+
+    def recv_buffer(self, tag: str, like: torch.Tensor) -> torch.Tensor:
+        """Registered buffer shaped like ``like`` (collective on first use of
+        ``tag`` or a new shape); filled in place by the exchanges."""
+        return self._buffer(tag, like.shape, like.dtype)[0]
+
+    def _target(self, out):
+        tag = self._by_ptr.get(out.data_ptr())
+        if tag is not None and self._bufs[tag][0].numel() == out.numel():
+            return self._bufs[tag], False
+        return self._buffer(("scratch", out.numel(), out.dtype), (out.numel(),), out.dtype), True
+
+    # -- ordering ---------------------------------------------------------
+    def barrier(self) -> None:
+        """Stream-ordered barrier: work queued on every rank's current stream
+        before it is complete once it returns on any stream after it."""
+        self._dist.all_reduce(self._tick, group=self.group)
+
+    def _scatter(self, copies):
+        """``copies``: ``(peer, dst_ptr, src_ptr, nbytes)``; the peer's copies
+        go on its own stream, joined back into the current stream."""
+        cur = torch.cuda.current_stream(self.dev)
+        used = set()
+        for peer, dst, src, nbytes in copies:
+            if dst == src or nbytes == 0:
+                continue
+            s = cur if peer == self.rank else self._streams[peer]
+            if s is not cur and peer not in used:
+                s.wait_stream(cur)
+                used.add(peer)
+            _lib.check(self.lib.fpb_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src),
+                                               nbytes, ctypes.c_void_p(s.cuda_stream)),
+                       "fpb_copy_async")
+        for peer in used:
+            cur.wait_stream(self._streams[peer])
+
+    def _order(self):
+        return [(self.rank + k) % self.world for k in range(self.world)]
+
+    # -- collectives ------------------------------------------------------
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        (buf, ptrs), copy_back = self._target(out)
+        inp = inp.contiguous()
+        m = inp.numel() * inp.element_size() // self.world
+        self.barrier()
+        self._scatter([(d, ptrs[d] + self.rank * m, inp.data_ptr() + d * m, m)
+                       for d in self._order()])
+        self.barrier()
+        if copy_back:
+            out.view(-1).copy_(buf)
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        (buf, ptrs), copy_back = self._target(out)
+        inp = inp.contiguous()
+        m = inp.numel() * inp.element_size()
+        self.barrier()
+        self._scatter([(d, ptrs[d] + self.rank * m, inp.data_ptr(), m) for d in self._order()])
+        self.barrier()
+        if copy_back:
+            out.view(-1).copy_(buf)
+
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        self.nccl.reduce_scatter(out, inp)
+
+    def transpose_rows(self, z_loc, shard: RowShard, out=None, tag="transpose"):
+        """``transpose_rows`` in one kernel over peer memory (see there)."""
+        c, n, ch = shard.chunk, shard.n, z_loc.shape[-1]
+        if z_loc.dtype != torch.float32 or not z_loc.is_contiguous():
+            raise ValueError("peer transpose takes a contiguous float32 [chunk, n, c] tensor")
+        buf, ptrs = self._buffer(tag, (c, n, ch), torch.float32)
+        arr = (ctypes.c_void_p * self.world)(*ptrs)
+        self.barrier()
+        _lib.check(self.lib.fpb_peer_transpose_rows(
+            ctypes.c_void_p(z_loc.data_ptr()), n, c, ch, self.rank, self.world, arr,
+            ops._stream_ptr(self.dev)), "fpb_peer_transpose_rows")
+        self.barrier()
+        if out is None:
+            return buf
+        out[:shard.rows].copy_(buf[:shard.rows])
+        return out
+
+    def close(self) -> None:
+        """Unmap every peer buffer (after a device synchronise)."""
+        for base in self._opened.values():
+            self.lib.fpb_ipc_close(ctypes.c_void_p(base))
+        self._opened.clear()
+        self._bufs.clear()
+        self._by_ptr.clear()
+
+
+def _recv_like(comm, tag: str, like: torch.Tensor) -> torch.Tensor:
+    """Receive buffer of an exchange: the transport's registered buffer when
+    it has one (filled in place), else a fresh tensor."""
+    get = getattr(comm, "recv_buffer", None)
+    return torch.empty_like(like) if get is None else get(tag, like)
+
+
 def gather_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
     """Full ``[n, n, c]`` pair tensor on every rank (tests and checkpoints)."""
     full = z_loc.new_empty((shard.world * shard.chunk,) + tuple(z_loc.shape[1:]))
@@ -115,7 +291,13 @@ def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm, out=None) -> torc
     rank's ``i``. One all-to-all of ``[chunk, chunk, c]`` blocks, packed and
     unpacked in one pass each; padded columns travel as zeros and padded rows
     of the result are zero. ``out``: optional ``[chunk, n, c]`` destination
-    (may be ``z_loc`` itself: the send block is packed before it is written)."""
+    (may be ``z_loc`` itself: the send block is packed before it is written).
+    A transport with its own ``transpose_rows`` (``PeerComm``) does it in one
+    pass; its result without ``out`` is a registered buffer, valid until the
+    next transpose into it."""
+    peer = getattr(comm, "transpose_rows", None)
+    if peer is not None:
+        return peer(z_loc, shard, out=out, tag="transpose" if out is None else "transpose_out")
     w, c, n = shard.world, shard.chunk, shard.n
     ch = z_loc.shape[-1]
     send = z_loc.new_empty(w, c, c, ch)  # [dest][my i][dest j]
@@ -444,15 +626,15 @@ def trimul_scheme(world: int) -> str:
 
 def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
     a, b, ld = phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w)
-    ra = torch.empty_like(a)
+    ra = _recv_like(comm, "trimul_a", a)
     comm.all_to_all(ra, a)
     del a
-    rb = torch.empty_like(b)
+    rb = _recv_like(comm, "trimul_b", b)
     comm.all_to_all(rb, b)
     del b
     xg = phases.trimul_contract_groups(ra, rb, shard, outgoing, ld)
     del ra, rb
-    rx = torch.empty_like(xg)
+    rx = _recv_like(comm, "trimul_x", xg)
     comm.all_to_all(rx, xg)
     del xg
     phases.trimul_finish(z_loc, shard, phases.trimul_ungroup_x(rx, shard), w, add)
@@ -495,7 +677,7 @@ def sharded_triattn(z_loc, mask, w: dict, shard: RowShard, comm, phases, *,
         sharded_triattn(zt, mt, w, shard, comm, phases, starting=True)
         transpose_rows(zt, shard, comm, out=z_loc)
         return z_loc
-    bias_full = phases.triattn_bias_buffer(shard, z_loc.device)
+    bias_full = _recv_like(comm, "triattn_bias", phases.triattn_bias_buffer(shard, z_loc.device))
     state = phases.triattn_proj(z_loc, mask, shard, w, bias_full)
     own = bias_full[shard.rank * shard.chunk:(shard.rank + 1) * shard.chunk]
     comm.all_gather(bias_full, own.clone())

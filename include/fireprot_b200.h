@@ -283,6 +283,33 @@ int fpb_triattn_shard_finish(float* z_loc, float* delta_out, int n, int rows, in
                              int precision, void* workspace, size_t workspace_bytes,
                              cudaStream_t stream);
 
+/* Peer memory for the row-sharded phases on the GPUs of one node (one
+ * process per GPU). No reference counterpart (the reference has no sharded
+ * path). fpb_ipc_export turns a device pointer of the caller's into a CUDA
+ * IPC handle (fpb_ipc_handle_bytes bytes) of its allocation plus the
+ * pointer's offset in it; another process maps it into its current device's
+ * context with fpb_ipc_import (peer access enabled lazily; ptr_out = mapped
+ * base + offset) and unmaps it with fpb_ipc_close(base). fpb_copy_async
+ * enqueues one copy on `stream` (either pointer may be a mapped peer
+ * address). The caller orders the copies against the owner's use of the
+ * buffer (e.g. a collective on both sides). Nothing is allocated. */
+size_t fpb_ipc_handle_bytes(void);
+int fpb_ipc_export(const void* ptr, void* handle_out, size_t* offset_out);
+int fpb_ipc_import(const void* handle, size_t offset, void** base_out, void** ptr_out);
+int fpb_ipc_close(void* base);
+int fpb_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
+/* Transposed exchange of the row-sharded pair tensor: rank `rank` of `world`
+ * (world <= 16) owns rows [rank*chunk, rank*chunk + chunk) of z [n, n, ch]
+ * as z_loc [chunk][n][ch] (rows at or past n are padding and are not read).
+ * Every owned z[i, j, :] with j < n is stored at row j - d*chunk, column i
+ * of dst[d], d = j / chunk: dst[d] is rank d's [chunk][n][ch] buffer of the
+ * rows of z^T it owns (a peer mapping, or the caller's own buffer for
+ * d == rank). Rows of dst past n are not written. ch % 4 == 0, every pointer
+ * 16-byte aligned. One kernel; the stores to other ranks cross NVLink. */
+int fpb_peer_transpose_rows(const float* z_loc, int n, int chunk, int ch, int rank, int world,
+                            float* const* dst, cudaStream_t stream);
+
 /* Weights of the five pair operators of one block (torch Linear layouts). */
 typedef struct {
   const float *ln_in_w, *ln_in_b, *w_a_p, *w_a_g, *w_b_p, *w_b_g, *w_g, *ln_out_w, *ln_out_b,

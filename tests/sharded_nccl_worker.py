@@ -2,8 +2,9 @@
 NCCL process group, the whole Pairformer block on each rank's rows (the
 sharded pair stack, then the single stack on the rank's query rows and the
 all-gather of s), then rank 0 compares the all-gathered z and s with the CPU
-oracle and writes a JSON verdict to ``argv[1]``. Every rank runs the same
-collective sequence."""
+oracle and writes a JSON verdict to ``argv[1]``, over NCCL collectives and
+over the peer-memory transport. Every rank runs the same collective
+sequence."""
 import datetime
 import json
 import os
@@ -27,7 +28,8 @@ def main(out_path: str) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    comm = S.DistComm()
+    comms = {"nccl": S.DistComm(), "peer": S.PeerComm()}
+    comm = comms["nccl"]
     results = {}
     try:
         for n, mask_kind in ((150, "padding"), (96, "none")):
@@ -45,8 +47,14 @@ def main(out_path: str) -> None:
             s_ref = O.single_block(s, ref, mask, ps) if comm.rank == 0 else None
             # both TriMul exchange schemes at every world size (the channel
             # scheme is the default only from four ranks)
-            for precision, scheme in (("strict", "rows"), ("fast", "rows"),
-                                      ("strict", "channels"), ("fast", "channels")):
+            # and both transports (NCCL collectives, peer-memory copies)
+            for precision, scheme, kind in (("strict", "rows", "nccl"), ("fast", "rows", "nccl"),
+                                            ("strict", "channels", "nccl"),
+                                            ("fast", "channels", "nccl"),
+                                            ("strict", "rows", "peer"),
+                                            ("strict", "channels", "peer"),
+                                            ("fast", "channels", "peer")):
+                comm = comms[kind]
                 z_loc = S.local_rows(z.to(dev), sh)
                 s_buf = S.single_buffer(s.to(dev), sh)
                 ph = S.CudaPhases(precision)
@@ -59,11 +67,13 @@ def main(out_path: str) -> None:
                     tol = O.STRICT_TOL if precision == "strict" else O.FAST_TOL
                     err = O.rel_max_err(full, ref)
                     err_s = O.rel_max_err(s_buf[:n].cpu(), s_ref)
-                    results[f"n{n}_{mask_kind}_{precision}_{scheme}"] = {
+                    results[f"n{n}_{mask_kind}_{precision}_{scheme}_{kind}"] = {
                         "err": err, "err_s": err_s, "tol": tol,
                         "ok": err <= tol and err_s <= tol}
         dist.barrier()
+        torch.cuda.synchronize(dev)
     finally:
+        comms["peer"].close()
         dist.destroy_process_group()
     if comm.rank == 0:
         Path(out_path).write_text(json.dumps({"world": comm.world, "cases": results}))

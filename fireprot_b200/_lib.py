@@ -76,6 +76,10 @@ SIGNATURES = {
     "fpb_trimul_group_contract": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                           c_int, c_int, c_int, c_size_t, c_int, c_int, c_int,
                                           c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_group_contract_scatter": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p,
+                                                  c_void_p, c_int, c_int, c_int, c_size_t, c_int,
+                                                  c_int, c_int, c_void_p, c_int, c_int, c_int,
+                                                  c_int, c_void_p, c_size_t, c_void_p]),
     "fpb_trimul_group_gather": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                         c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "fpb_trimul_shard_finish": (c_int, [c_void_p, c_int, c_int, c_void_p] + [c_void_p] * 6
@@ -92,6 +96,7 @@ SIGNATURES = {
                                ctypes.POINTER(c_void_p)]),
     "fpb_ipc_close": (c_int, [c_void_p]),
     "fpb_copy_async": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "fpb_peer_scatter": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "fpb_peer_transpose_rows": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                         c_void_p]),
     "fpb_registry_new": (c_void_p, []),

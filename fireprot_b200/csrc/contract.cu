@@ -176,7 +176,13 @@ __global__ void __launch_bounds__(192, 1)
         // `out` points at column 0 of this (channel, row) run, so that
         // out + col0 addresses columns col0..col0+31 in either layout
         OutT* out;
-        if (args.blocked)
+        if (args.owners) {
+          const int d = min(row / args.owner_rows, args.owners - 1);
+          const size_t lr = (size_t)(row - d * args.owner_rows);
+          out = reinterpret_cast<OutT*>(args.outs[d]) +
+                (((lr * args.njb + (col0 >> 7)) * 128 + ch + args.ch_off) << 7) + (col0 & 127) -
+                col0;
+        } else if (args.blocked)
           out = reinterpret_cast<OutT*>(args.out) +
                 ((((size_t)row * args.njb + (col0 >> 7)) * (args.bchannels ? args.bchannels : 128) +
                    ch)

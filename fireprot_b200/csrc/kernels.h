@@ -42,6 +42,14 @@ struct ContractArgs {
   int blocked;
   int njb;
   int bchannels;  // channels per block of the blocked layout (0: 128)
+  // Owner scatter (blocked layout, owners > 0): output row r is stored in
+  // outs[r / owner_rows] at row r % owner_rows of a blocked layout of 128
+  // channels, channel ch + ch_off: every row goes straight to the x buffer
+  // of the rank that owns it (a peer address for the other ranks).
+  int owners;
+  int owner_rows;
+  int ch_off;
+  void* outs[16];
 };
 
 int launch_contract(const ContractOperands& op, const ContractArgs& args, cudaStream_t stream);

@@ -70,10 +70,60 @@ __global__ void __launch_bounds__(256) peer_transpose_kernel(const float4* __res
   }
 }
 
+struct CopySeg {
+  const float4* src;
+  float4* dst;
+  long long n4;
+};
+struct CopySegs {
+  CopySeg s[kMaxPeers];
+};
+
+// Block row y copies segment y; its blocks stride over the segment with
+// four independent 16-byte loads in flight per thread before the stores, so
+// every peer's NVLink port is written by SMs at once (the copy engines run
+// one transfer per engine, and a few engines cannot fill the fabric).
+__global__ void __launch_bounds__(256) peer_scatter_kernel(CopySegs segs) {
+  const CopySeg sg = segs.s[blockIdx.y];
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < sg.n4; i += 4 * stride) {
+    const float4 v0 = __ldcs(sg.src + i);
+    const float4 v1 = __ldcs(sg.src + i + stride);
+    const float4 v2 = __ldcs(sg.src + i + 2 * stride);
+    const float4 v3 = __ldcs(sg.src + i + 3 * stride);
+    sg.dst[i] = v0;
+    sg.dst[i + stride] = v1;
+    sg.dst[i + 2 * stride] = v2;
+    sg.dst[i + 3 * stride] = v3;
+  }
+  for (; i < sg.n4; i += stride) sg.dst[i] = __ldcs(sg.src + i);
+}
+
 }  // namespace
 }  // namespace fpb
 
 using namespace fpb;
+
+extern "C" int fpb_peer_scatter(const void* const* src, void* const* dst, const size_t* bytes,
+                                int count, cudaStream_t stream) {
+  if (count < 0 || count > kMaxPeers || (count && (!src || !dst || !bytes))) return kErrArg;
+  CopySegs segs{};
+  int used = 0;
+  for (int k = 0; k < count; ++k) {
+    if (!bytes[k]) continue;
+    if (!src[k] || !dst[k] || !aligned16(src[k]) || !aligned16(dst[k]) || (bytes[k] & 15))
+      return kErrArg;
+    segs.s[used++] = CopySeg{static_cast<const float4*>(src[k]), static_cast<float4*>(dst[k]),
+                             static_cast<long long>(bytes[k] / 16)};
+  }
+  if (!used) return kOk;
+  const int per = (sm_count() * 8 + used - 1) / used;  // 8 blocks of 256 per SM in all
+  FPB_LAUNCH("peer_scatter", stream,
+             peer_scatter_kernel<<<dim3(static_cast<unsigned>(per), static_cast<unsigned>(used)),
+                                   256, 0, stream>>>(segs));
+  return launch_status();
+}
 
 extern "C" int fpb_peer_transpose_rows(const float* z_loc, int n, int chunk, int ch, int rank,
                                        int world, float* const* dst, cudaStream_t stream) {

@@ -680,7 +680,9 @@ int trimul_finish_run(float* z_loc, int n, int rows, const void* x_blocked, cons
 int trimul_contract_run(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
                         const void* b_hi, const void* b_lo, int nn, int b_chunk_rows,
                         int b_chunks, size_t b_chunk_stride, int k, int ld, void* x_blocked,
-                        bool strict, int* status, cudaStream_t stream, int channels = 128) {
+                        bool strict, int* status, cudaStream_t stream, int channels = 128,
+                        void* const* x_owner = nullptr, int owners = 0, int owner_rows = 0,
+                        int ch_off = 0) {
   ContractOperands op{a_hi, a_lo, b_hi, b_lo, ld, (size_t)a_plane_rows * ld,
                       (size_t)b_chunk_rows * ld,
                       m, nn, k, b_chunk_rows, b_chunks, b_chunk_stride, channels, strict};
@@ -691,6 +693,10 @@ int trimul_contract_run(const void* a_hi, const void* a_lo, int m, int a_plane_r
   ca.blocked = 1;
   ca.njb = (nn + 127) / 128;
   ca.bchannels = channels;
+  ca.owners = owners;
+  ca.owner_rows = owner_rows;
+  ca.ch_off = ch_off;
+  for (int d = 0; d < owners; ++d) ca.outs[d] = x_owner[d];
   return launch_contract(op, ca, stream);
 }
 
@@ -837,6 +843,31 @@ extern "C" int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int
   return trimul_contract_run(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows, b_chunks,
                              b_chunk_stride, k, ld, x_blocked, strict,
                              static_cast<int*>(workspace), stream, channels);
+}
+
+extern "C" int fpb_trimul_group_contract_scatter(
+    const void* a_hi, const void* a_lo, int m, int a_plane_rows, const void* b_hi,
+    const void* b_lo, int nn, int b_chunk_rows, int b_chunks, size_t b_chunk_stride, int k, int ld,
+    int channels, void* const* x_owner, int owners, int owner_rows, int ch_off, int precision,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!a_hi || !b_hi || !x_owner || !workspace) return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (strict && (!a_lo || !b_lo)) return kErrArg;
+  if (m <= 0 || nn <= 0 || k <= 0 || b_chunk_rows <= 0 || b_chunks <= 0 || a_plane_rows < m ||
+      (long long)b_chunk_rows * b_chunks < nn || channels <= 0 || channels > 128)
+    return kErrShape;
+  if (owners <= 0 || owners > 16 || owner_rows <= 0 || (long long)owners * owner_rows < m ||
+      ch_off < 0 || ch_off + channels > 128)
+    return kErrShape;
+  for (int d = 0; d < owners; ++d)
+    if ((long long)d * owner_rows < m && (!x_owner[d] || !aligned16(x_owner[d]))) return kErrArg;
+  if (workspace_bytes < kWsHeader || !aligned16(workspace)) return kErrWorkspace;
+  if (reset_status(workspace, stream)) return kErrCuda;
+  return trimul_contract_run(a_hi, a_lo, m, a_plane_rows, b_hi, b_lo, nn, b_chunk_rows, b_chunks,
+                             b_chunk_stride, k, ld, x_owner[0], strict,
+                             static_cast<int*>(workspace), stream, channels, x_owner, owners,
+                             owner_rows, ch_off);
 }
 
 extern "C" int fpb_trimul_shard_contract(const void* a_hi, const void* a_lo, int m,

@@ -109,9 +109,9 @@ class PeerComm:
 
     Every rank registers the receive buffers once (an IPC handle per buffer,
     swapped with ``all_gather_object``; the peers map them into their own
-    context), after which an all-to-all or all-gather is one copy per peer,
-    written straight into the peer's buffer over NVLink by the copy engines
-    (one stream per peer, so the copies run side by side), and the
+    context), after which an all-to-all or all-gather is one kernel
+    (``fpb_peer_scatter``) whose SMs store every peer's block straight into
+    the peer's buffer over NVLink, all peers side by side, and the
     transposed exchange of the ending-node operator is one kernel
     (``fpb_peer_transpose_rows``) that stores each 512-byte channel vector
     at its transposed place on its owner: no packing, staging or unpacking
@@ -132,15 +132,15 @@ class PeerComm:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        if self.world > 16:
+            raise ValueError(f"the peer transport spans at most 16 ranks (world={self.world})")
         self.nccl = DistComm(group)
         self.lib = _lib.load()
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self._tick = torch.zeros(1, device=self.dev)
-        self._bufs: dict = {}     # tag -> (tensor, [device pointer per rank])
-        self._by_ptr: dict = {}   # data_ptr -> tag
+        self._bufs: dict = {}     # (tag, shape, dtype) -> (tensor, [device pointer per rank])
+        self._by_ptr: dict = {}   # data_ptr -> (tag, shape, dtype)
         self._opened: dict = {}   # handle bytes -> mapped base (peer segments)
-        self._retired: list = []  # replaced buffers: peers may still map them
-        self._streams = [torch.cuda.Stream(self.dev) for _ in range(self.world)]
         self._hbytes = int(self.lib.fpb_ipc_handle_bytes())
 
     # -- registration -----------------------------------------------------
@@ -169,19 +169,25 @@ class PeerComm:
                            "fpb_ipc_import")
                 self._opened[h] = base = b.value
             ptrs.append(base + o)
-        old = self._bufs.get(tag)
-        if old is not None:
-            self._by_ptr.pop(old[0].data_ptr(), None)
-            self._retired.append(old)
-        self._bufs[tag] = (t, ptrs)
-        self._by_ptr[t.data_ptr()] = tag
+        self._bufs[(tag, shape, dtype)] = (t, ptrs)
+        self._by_ptr[t.data_ptr()] = (tag, shape, dtype)
         return t, ptrs
 
     def _buffer(self, tag, shape, dtype):
-        ent = self._bufs.get(tag)
-        if ent is None or ent[0].dtype != dtype or tuple(ent[0].shape) != tuple(shape):
-            ent = self._register(tag, tuple(shape), dtype)
+        """The registered buffer of ``(tag, shape, dtype)``: one per distinct
+        shape, so operators whose exchanges differ in shape (the outgoing and
+        incoming TriMul) each keep theirs instead of re-registering."""
+        shape = tuple(int(d) for d in shape)
+        ent = self._bufs.get((tag, shape, dtype))
+        if ent is None:
+            ent = self._register(tag, shape, dtype)
         return ent
+
+    def owner_buffer(self, tag: str, shape, dtype):
+        """Registered buffer of this rank plus every rank's address of its
+        own (``(tensor, [pointer per rank])``), for kernels that store
+        straight at the owners."""
+        return self._buffer(tag, shape, dtype)
 
     def recv_buffer(self, tag: str, like: torch.Tensor) -> torch.Tensor:
         """Registered buffer shaped like ``like`` (collective on first use of
@@ -189,10 +195,10 @@ class PeerComm:
         return self._buffer(tag, like.shape, like.dtype)[0]
 
     def _target(self, out):
-        tag = self._by_ptr.get(out.data_ptr())
-        if tag is not None and self._bufs[tag][0].numel() == out.numel():
-            return self._bufs[tag], False
-        return self._buffer(("scratch", out.numel(), out.dtype), (out.numel(),), out.dtype), True
+        key = self._by_ptr.get(out.data_ptr())
+        if key is not None and self._bufs[key][0].numel() == out.numel():
+            return self._bufs[key], False
+        return self._buffer("scratch", (out.numel(),), out.dtype), True
 
     # -- ordering ---------------------------------------------------------
     def barrier(self) -> None:
@@ -201,43 +207,62 @@ class PeerComm:
         self._dist.all_reduce(self._tick, group=self.group)
 
     def _scatter(self, copies):
-        """``copies``: ``(peer, dst_ptr, src_ptr, nbytes)``; the peer's copies
-        go on its own stream, joined back into the current stream."""
-        cur = torch.cuda.current_stream(self.dev)
-        used = set()
-        for peer, dst, src, nbytes in copies:
-            if dst == src or nbytes == 0:
-                continue
-            s = cur if peer == self.rank else self._streams[peer]
-            if s is not cur and peer not in used:
-                s.wait_stream(cur)
-                used.add(peer)
-            _lib.check(self.lib.fpb_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src),
-                                               nbytes, ctypes.c_void_p(s.cuda_stream)),
+        """``copies``: ``(peer, dst_ptr, src_ptr, nbytes)``. One kernel on the
+        current stream (``fpb_peer_scatter``) writes every peer's block side
+        by side; a copy that is not 16-byte aligned goes through the copy
+        engine on the same stream instead."""
+        cur = ops._stream_ptr(self.dev)
+        fast = [(d, s, b) for _, d, s, b in copies
+                if b and d != s and not (d | s | b) & 15]
+        slow = [(d, s, b) for _, d, s, b in copies
+                if b and d != s and (d | s | b) & 15]
+        for i in range(0, len(fast), 16):
+            part = fast[i:i + 16]
+            k = len(part)
+            _lib.check(self.lib.fpb_peer_scatter(
+                (ctypes.c_void_p * k)(*[s for _, s, _ in part]),
+                (ctypes.c_void_p * k)(*[d for d, _, _ in part]),
+                (ctypes.c_size_t * k)(*[b for _, _, b in part]), k, cur), "fpb_peer_scatter")
+        for d, s, b in slow:
+            _lib.check(self.lib.fpb_copy_async(ctypes.c_void_p(d), ctypes.c_void_p(s), b, cur),
                        "fpb_copy_async")
-        for peer in used:
-            cur.wait_stream(self._streams[peer])
 
     def _order(self):
         return [(self.rank + k) % self.world for k in range(self.world)]
 
     # -- collectives ------------------------------------------------------
-    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor) -> None:
-        (buf, ptrs), copy_back = self._target(out)
-        inp = inp.contiguous()
-        m = inp.numel() * inp.element_size() // self.world
+    # ``fresh=True``: the caller's schedule guarantees that every rank's
+    # reads of the destination buffers' previous contents were queued before
+    # a barrier that has since been passed (typically the closing barrier of
+    # a later exchange), so the opening barrier is skipped. The closing
+    # barrier is always issued.
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor, *, fresh: bool = False) -> None:
+        self.all_to_all_many([(out, inp)], fresh=fresh)
+
+    def all_to_all_many(self, pairs, *, fresh: bool = False) -> None:
+        """Several all-to-alls ``(out, inp)`` in one kernel and one barrier."""
+        copies, backs = [], []
+        for out, inp in pairs:
+            (buf, ptrs), copy_back = self._target(out)
+            inp = inp.contiguous()
+            m = inp.numel() * inp.element_size() // self.world
+            copies += [(d, ptrs[d] + self.rank * m, inp.data_ptr() + d * m, m)
+                       for d in self._order()]
+            if copy_back:
+                backs.append((out, buf))
+        if not fresh:
+            self.barrier()
+        self._scatter(copies)
         self.barrier()
-        self._scatter([(d, ptrs[d] + self.rank * m, inp.data_ptr() + d * m, m)
-                       for d in self._order()])
-        self.barrier()
-        if copy_back:
+        for out, buf in backs:
             out.view(-1).copy_(buf)
 
-    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor, *, fresh: bool = False) -> None:
         (buf, ptrs), copy_back = self._target(out)
         inp = inp.contiguous()
         m = inp.numel() * inp.element_size()
-        self.barrier()
+        if not fresh:
+            self.barrier()
         self._scatter([(d, ptrs[d] + self.rank * m, inp.data_ptr(), m) for d in self._order()])
         self.barrier()
         if copy_back:
@@ -246,14 +271,16 @@ class PeerComm:
     def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
         self.nccl.reduce_scatter(out, inp)
 
-    def transpose_rows(self, z_loc, shard: RowShard, out=None, tag="transpose"):
+    def transpose_rows(self, z_loc, shard: RowShard, out=None, tag="transpose", *,
+                       fresh: bool = False):
         """``transpose_rows`` in one kernel over peer memory (see there)."""
         c, n, ch = shard.chunk, shard.n, z_loc.shape[-1]
         if z_loc.dtype != torch.float32 or not z_loc.is_contiguous():
             raise ValueError("peer transpose takes a contiguous float32 [chunk, n, c] tensor")
         buf, ptrs = self._buffer(tag, (c, n, ch), torch.float32)
         arr = (ctypes.c_void_p * self.world)(*ptrs)
-        self.barrier()
+        if not fresh:
+            self.barrier()
         _lib.check(self.lib.fpb_peer_transpose_rows(
             ctypes.c_void_p(z_loc.data_ptr()), n, c, ch, self.rank, self.world, arr,
             ops._stream_ptr(self.dev)), "fpb_peer_transpose_rows")
@@ -286,7 +313,8 @@ def gather_rows(z_loc: torch.Tensor, shard: RowShard, comm) -> torch.Tensor:
     return full[:shard.n]
 
 
-def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm, out=None) -> torch.Tensor:
+def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm, out=None, *,
+                   fresh: bool = False) -> torch.Tensor:
     """Rows of ``z^T`` owned by this rank: ``zt[i, j] = z[j, i]`` for the
     rank's ``i``. One all-to-all of ``[chunk, chunk, c]`` blocks, packed and
     unpacked in one pass each; padded columns travel as zeros and padded rows
@@ -294,10 +322,11 @@ def transpose_rows(z_loc: torch.Tensor, shard: RowShard, comm, out=None) -> torc
     (may be ``z_loc`` itself: the send block is packed before it is written).
     A transport with its own ``transpose_rows`` (``PeerComm``) does it in one
     pass; its result without ``out`` is a registered buffer, valid until the
-    next transpose into it."""
+    next transpose into it; ``fresh`` as for ``PeerComm`` exchanges."""
     peer = getattr(comm, "transpose_rows", None)
     if peer is not None:
-        return peer(z_loc, shard, out=out, tag="transpose" if out is None else "transpose_out")
+        return peer(z_loc, shard, out=out, tag="transpose" if out is None else "transpose_out",
+                    fresh=fresh)
     w, c, n = shard.world, shard.chunk, shard.n
     ch = z_loc.shape[-1]
     send = z_loc.new_empty(w, c, c, ch)  # [dest][my i][dest j]
@@ -548,11 +577,15 @@ class CudaPhases:
                                            ops._stream_ptr(t.device)), "fpb_split_tf32")
         return [t, lo]
 
-    def trimul_contract_groups(self, ra, rb, shard: RowShard, outgoing: bool, ld: int):
+    def trimul_contract_groups(self, ra, rb, shard: RowShard, outgoing: bool, ld: int,
+                               x_owner=None):
         """This rank's channel group contracted over the whole grid. ``ra``,
         ``rb``: the received ``[world][G][rows_p][ld]`` blocks. Returns x
         blocked ``[world * chunk][njb][G][128]``; rows ``[r * chunk, (r + 1) *
-        chunk)`` are rank ``r``'s (the send block of the return all-to-all)."""
+        chunk)`` are rank ``r``'s (the send block of the return all-to-all).
+        With ``x_owner`` (rank ``r``'s ``[chunk][njb][128][128]`` x buffer
+        address, for every rank) the rows are stored at their owners instead,
+        in this rank's channel group, and nothing is returned."""
         W, n, chunk = shard.world, shard.n, shard.chunk
         G = 128 // W
         dev = ra.device
@@ -580,8 +613,16 @@ class CudaPhases:
             b_op = gather(rb, n, chunk, 1, n, ldk)
             geo = dict(m=n, a_rows=n, nn=n, b_chunk_rows=n, b_chunks=1, b_chunk_stride=0,
                        k=W * chunk, ld=ldk)
-        x = torch.empty(W * chunk, (n + 127) // 128, G, 128, dtype=self._dtype(), device=dev)
         ws = self._ws_take("trimul_contract", 256, dev)
+        if x_owner is not None:
+            _lib.check(self.lib.fpb_trimul_group_contract_scatter(
+                *self._pair(a_op), geo["m"], geo["a_rows"], *self._pair(b_op), geo["nn"],
+                geo["b_chunk_rows"], geo["b_chunks"], geo["b_chunk_stride"], geo["k"], geo["ld"],
+                G, (ctypes.c_void_p * W)(*x_owner), W, chunk, shard.rank * G, self.p,
+                ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)),
+                "fpb_trimul_group_contract_scatter")
+            return None
+        x = torch.empty(W * chunk, (n + 127) // 128, G, 128, dtype=self._dtype(), device=dev)
         _lib.check(self.lib.fpb_trimul_group_contract(
             *self._pair(a_op), geo["m"], geo["a_rows"], *self._pair(b_op), geo["nn"],
             geo["b_chunk_rows"], geo["b_chunks"], geo["b_chunk_stride"], geo["k"], geo["ld"], G,
@@ -626,10 +667,28 @@ def trimul_scheme(world: int) -> str:
 
 def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
     a, b, ld = phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w)
+    a_dtype = a.dtype
     ra = _recv_like(comm, "trimul_a", a)
+    rb = _recv_like(comm, "trimul_b", b)
+    owners = getattr(comm, "owner_buffer", None)
+    if owners is not None:
+        # Peer transport. ra / rb were last read by the contraction of an
+        # earlier call of this direction, and the x buffers by the finish of
+        # an earlier call; every call closes its contraction with a barrier
+        # and issues one (the a / b exchange) after any earlier finish, so
+        # neither exchange needs an opening barrier.
+        comm.all_to_all_many([(ra, a), (rb, b)], fresh=True)
+        del a, b
+        njb = (shard.n + 127) // 128
+        x_loc, ptrs = owners("trimul_x", (shard.chunk, njb, 128, 128), a_dtype)
+        # the contraction stores each x row at its owner (fused return exchange)
+        phases.trimul_contract_groups(ra, rb, shard, outgoing, ld, x_owner=ptrs)
+        comm.barrier()
+        del ra, rb
+        phases.trimul_finish(z_loc, shard, x_loc, w, add)
+        return z_loc
     comm.all_to_all(ra, a)
     del a
-    rb = _recv_like(comm, "trimul_b", b)
     comm.all_to_all(rb, b)
     del b
     xg = phases.trimul_contract_groups(ra, rb, shard, outgoing, ld)
@@ -655,8 +714,8 @@ def sharded_trimul(z_loc, mask, w: dict, shard: RowShard, comm, phases, *, outgo
     a, b, ld = phases.trimul_proj(z_loc, mask, shard, outgoing, w)
     if outgoing:
         b_full = []
-        for t in b:
-            full = t.new_empty((shard.world,) + tuple(t.shape))
+        for i, t in enumerate(b):
+            full = _recv_like(comm, f"trimul_b_full{i}", t.new_empty((shard.world,) + tuple(t.shape)))
             comm.all_gather(full, t)
             b_full.append(full)
         x_loc = phases.trimul_contract_out(a, b_full, shard, ld)
@@ -672,10 +731,15 @@ def sharded_triattn(z_loc, mask, w: dict, shard: RowShard, comm, phases, *,
                     starting: bool = True):
     """Triangle attention update added to the rank's rows of ``z_loc``."""
     if not starting:
-        zt = transpose_rows(z_loc, shard, comm)
+        # Peer transport: the forward destination was last read by an
+        # earlier call's attention and backward transpose, the backward
+        # destination by an earlier call's copy out of it; the backward
+        # transpose and this call's forward transpose close with barriers
+        # after those reads, so neither transpose needs an opening barrier.
+        zt = transpose_rows(z_loc, shard, comm, fresh=True)
         mt = None if mask is None else mask.transpose(0, 1).contiguous()
         sharded_triattn(zt, mt, w, shard, comm, phases, starting=True)
-        transpose_rows(zt, shard, comm, out=z_loc)
+        transpose_rows(zt, shard, comm, out=z_loc, fresh=True)
         return z_loc
     bias_full = _recv_like(comm, "triattn_bias", phases.triattn_bias_buffer(shard, z_loc.device))
     state = phases.triattn_proj(z_loc, mask, shard, w, bias_full)

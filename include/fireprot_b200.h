@@ -242,6 +242,22 @@ int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m, int a_p
                               int b_chunks, size_t b_chunk_stride, int k, int ld, int channels,
                               void* x_blocked, int precision, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
+/* fpb_trimul_group_contract with the output rows stored straight at their
+ * owners: output row r goes to x_owner[r / owner_rows] (owners <= 16
+ * pointers, a peer mapping for the other ranks' buffers) at row
+ * r % owner_rows of the blocked [owner_rows][ceil(nn/128)][128][128]
+ * layout, channel c + ch_off. Rank g of the channel-sharded TriMul passes
+ * ch_off = g * channels, so every rank's buffer ends up holding all 128
+ * channels of its rows, the layout fpb_trimul_shard_finish reads, with no
+ * return exchange and no regrouping pass. The caller orders the stores
+ * against the owners' reads (a barrier before and after). */
+int fpb_trimul_group_contract_scatter(const void* a_hi, const void* a_lo, int m, int a_plane_rows,
+                                      const void* b_hi, const void* b_lo, int nn,
+                                      int b_chunk_rows, int b_chunks, size_t b_chunk_stride,
+                                      int k, int ld, int channels, void* const* x_owner,
+                                      int owners, int owner_rows, int ch_off, int precision,
+                                      void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream);
 /* Operand gather of the channel-group exchange: src is the all-to-all
  * receive buffer [world][channels][rows][src_ld] (FP32 unsplit in strict
  * mode, BF16 in fast mode); the call writes the contraction operand, split
@@ -307,6 +323,14 @@ int fpb_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream
  * rows of z^T it owns (a peer mapping, or the caller's own buffer for
  * d == rank). Rows of dst past n are not written. ch % 4 == 0, every pointer
  * 16-byte aligned. One kernel; the stores to other ranks cross NVLink. */
+/* Up to 16 copies in one kernel: bytes[k] from src[k] to dst[k] (either
+ * may be a mapped peer address), every pointer 16-byte aligned and every
+ * size a multiple of 16 (zero sizes are skipped). The SMs issue the loads and
+ * stores, so the copies to several peers cross NVLink side by side. The
+ * caller orders them against the owners' use of the buffers. */
+int fpb_peer_scatter(const void* const* src, void* const* dst, const size_t* bytes, int count,
+                     cudaStream_t stream);
+
 int fpb_peer_transpose_rows(const float* z_loc, int n, int chunk, int ch, int rank, int world,
                             float* const* dst, cudaStream_t stream);
 

@@ -60,3 +60,38 @@ def test_peer_transpose_rejects_bad_arguments():
     mis = (ctypes.c_void_p * 2)(z.data_ptr(), z.data_ptr() + 4)
     assert lib.fpb_peer_transpose_rows(zp, 64, 32, 128, 0, 2, mis, st) != 0
     torch.cuda.synchronize()
+
+
+def test_peer_scatter_copies_every_segment():
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    sizes = [0, 16, 4096, 1 << 20, (3 << 20) + 48, 7 * 16]
+    src = [torch.randint(0, 255, (max(b, 16),), dtype=torch.uint8, device=dev) for b in sizes]
+    dst = [torch.zeros(max(b, 16) + 32, dtype=torch.uint8, device=dev) for b in sizes]
+    k = len(sizes)
+    _lib.check(lib.fpb_peer_scatter(
+        (ctypes.c_void_p * k)(*[t.data_ptr() for t in src]),
+        (ctypes.c_void_p * k)(*[t.data_ptr() + 16 for t in dst]),
+        (ctypes.c_size_t * k)(*sizes), k, ops._stream_ptr(dev)), "fpb_peer_scatter")
+    torch.cuda.synchronize()
+    for b, s_, d_ in zip(sizes, src, dst):
+        assert torch.equal(d_[16:16 + b], s_[:b])
+        assert not d_[:16].any() and not d_[16 + b:].any()  # nothing outside the segment
+
+
+def test_peer_scatter_rejects_bad_arguments():
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    t = torch.zeros(1024, dtype=torch.uint8, device=dev)
+    st = ops._stream_ptr(dev)
+
+    def call(src_off, dst_off, nbytes, count=1):
+        return lib.fpb_peer_scatter((ctypes.c_void_p * 1)(t.data_ptr() + src_off),
+                                    (ctypes.c_void_p * 1)(t.data_ptr() + 512 + dst_off),
+                                    (ctypes.c_size_t * 1)(nbytes), count, st)
+    assert call(0, 0, 24) != 0     # size not a multiple of 16
+    assert call(8, 0, 32) != 0     # misaligned source
+    assert call(0, 4, 32) != 0     # misaligned destination
+    assert call(0, 0, 32, count=17) != 0
+    assert call(0, 0, 32, count=-1) != 0
+    torch.cuda.synchronize()

@@ -69,6 +69,10 @@ SIGNATURES = {
     "fpb_trimul_shard_proj": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]
                               + [c_void_p] * 6 + [c_float] + [c_void_p] * 4
                               + [c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fpb_trimul_shard_proj_scatter": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+                                      + [c_void_p] * 6 + [c_float] + [c_void_p] * 2
+                                      + [c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
+                                         c_void_p]),
     "fpb_split_tf32": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "fpb_trimul_shard_contract": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                           c_int, c_int, c_int, c_size_t, c_int, c_int, c_void_p,

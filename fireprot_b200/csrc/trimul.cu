@@ -42,6 +42,14 @@ struct TriMulProjArgs {
   int b_plain;  // strict: write b unsplit (FP32) into the b_hi planes
   int ntiles;   // yrows x ceil(ycols / 128) tiles, walked by a persistent grid
   int a_plain;  // strict: write a unsplit (FP32) into the a_hi planes
+  // Owner scatter (owners > 0; a and b unsplit): channel c goes to the
+  // receive buffer of rank c / gch, plane (rank * gch + c % gch) of its
+  // [owners][gch][plane_rows][ld] layout (peer addresses for other ranks).
+  int owners;
+  int gch;
+  int rank;
+  void* a_out[16];
+  void* b_out[16];
 };
 
 // Weight ring depth of the projection kernel: three 32 KB strict stages
@@ -187,6 +195,22 @@ __global__ void __launch_bounds__(320, 1)
             mbar_arrive(part ? free_b : free_a);
           }
           if (!valid) continue;
+          if (p.owners) {
+            // straight into the owners' receive buffers (one channel group
+            // per rank): the exchange rides on the epilogue's stores
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float v = sigmoidf_(__uint_as_float(gr[e])) * __uint_as_float(pr[e]) * m;
+              const int c = cc * 32 + e, grp = c / p.gch;
+              const size_t idx = (size_t)(p.rank * p.gch + c - grp * p.gch) * p.cs + pos;
+              void* dst = part ? p.b_out[grp] : p.a_out[grp];
+              if constexpr (kStrict)
+                static_cast<float*>(dst)[idx] = v;
+              else
+                static_cast<__nv_bfloat16*>(dst)[idx] = __float2bfloat16_rn(v);
+            }
+            continue;
+          }
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float v = sigmoidf_(__uint_as_float(gr[e])) * __uint_as_float(pr[e]) * m;
@@ -619,7 +643,8 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
                     const float* w_a_p, const float* w_a_g, const float* w_b_p,
                     const float* w_b_g, float eps, void* a_hi, void* a_lo, void* b_hi,
                     void* b_lo, int ld, int plane_rows, bool strict, void* wp_hi, void* wp_lo,
-                    int* status, cudaStream_t stream) {
+                    int* status, cudaStream_t stream, int owners = 0, int rank = 0,
+                    void* const* a_owner = nullptr, void* const* b_owner = nullptr) {
   int st = pack_weights(PackSrc{{w_a_p, w_a_g, w_b_p, w_b_g}, 4, 128}, wp_hi, wp_lo, strict,
                         stream);
   if (st) return st;
@@ -645,6 +670,13 @@ int trimul_proj_run(const float* z_loc, const float* mask, int yrows, int ycols,
   const int tiles = yrows * ((ycols + 127) / 128);
   TriMulProjArgs pa{z_loc, mask, yrows, ycols, zcols, r0,   eps,    ln_w,  ln_b,   a_hi,
                     a_lo,  b_hi, b_lo,  ld,    cs,    status, b_plain, tiles, a_plain};
+  pa.owners = owners;
+  pa.gch = owners ? 128 / owners : 0;
+  pa.rank = rank;
+  for (int d = 0; d < owners; ++d) {
+    pa.a_out[d] = a_owner[d];
+    pa.b_out[d] = b_owner[d];
+  }
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
   const int smem = strict ? proj_smem_bytes<true>() : proj_smem_bytes<false>();
   auto k = strict ? (transposed ? trimul_proj_kernel<true, true> : trimul_proj_kernel<true, false>)
@@ -823,6 +855,40 @@ extern "C" int fpb_trimul_shard_proj(const float* z_loc, const float* mask, int 
   return trimul_proj_run(z_loc, mask, yrows, ycols, n, r0, transposed != 0, ln_in_w, ln_in_b,
                          w_a_p, w_a_g, w_b_p, w_b_g, eps, a_hi, a_lo, b_hi, b_lo, ld, plane_rows,
                          strict, wh, wl, static_cast<int*>(workspace), stream);
+}
+
+extern "C" int fpb_trimul_shard_proj_scatter(
+    const float* z_loc, const float* mask, int n, int rows, int r0, int transposed,
+    const float* ln_in_w, const float* ln_in_b, const float* w_a_p, const float* w_a_g,
+    const float* w_b_p, const float* w_b_g, float eps, void* const* a_owner,
+    void* const* b_owner, int owners, int rank, int ld, int plane_rows, int precision,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!z_loc || !a_owner || !b_owner || !workspace || !ln_in_w || !ln_in_b || !w_a_p ||
+      !w_a_g || !w_b_p || !w_b_g)
+    return kErrArg;
+  if (precision != 0 && precision != 1) return kErrArg;
+  const bool strict = precision == 0;
+  if (owners <= 0 || owners > 16 || 128 % owners || rank < 0 || rank >= owners) return kErrShape;
+  for (int d = 0; d < owners; ++d)
+    if (!a_owner[d] || !b_owner[d] || !aligned16(a_owner[d]) || !aligned16(b_owner[d]))
+      return kErrArg;
+  if (n <= 0 || rows <= 0 || r0 < 0 || r0 + rows > n) return kErrShape;
+  const int yrows = transposed ? n : rows;
+  const int ycols = transposed ? rows : n;
+  if (plane_rows < yrows) return kErrShape;
+  if (ld < ycols || ld % (strict ? 32 : 64)) return kErrAlign;
+  if (!aligned16(z_loc) || !aligned16(workspace) || !aligned16(ln_in_w) || !aligned16(ln_in_b))
+    return kErrAlign;
+  if (workspace_bytes < fpb_trimul_shard_workspace_size(precision)) return kErrWorkspace;
+  WsCursor cur(workspace, workspace_bytes);
+  void *wh, *wl;
+  plan_weights(cur, strict, 512, &wh, &wl);
+  if (reset_status(workspace, stream)) return kErrCuda;
+  // a / b unsplit (the receivers split their operand while gathering it)
+  return trimul_proj_run(z_loc, mask, yrows, ycols, n, r0, transposed != 0, ln_in_w, ln_in_b,
+                         w_a_p, w_a_g, w_b_p, w_b_g, eps, a_owner[rank], nullptr, b_owner[rank],
+                         nullptr, ld, plane_rows, strict, wh, wl, static_cast<int*>(workspace),
+                         stream, owners, rank, a_owner, b_owner);
 }
 
 extern "C" int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m,

@@ -538,19 +538,42 @@ class CudaPhases:
                          eps=self.eps, workspace=ws)
 
     # ------------------------------------------------ TriMul, channel groups
-    def trimul_proj_groups(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict):
+    def trimul_group_plane(self, shard: RowShard, outgoing: bool):
+        """``(rows_p, ld)`` of the channel-group a/b planes (see
+        ``trimul_proj_groups``)."""
+        if outgoing:
+            return shard.chunk, int(self.lib.fpb_trimul_plane_ld(shard.n, self.p))
+        return shard.n, int(self.lib.fpb_trimul_plane_ld(shard.chunk, self.p))
+
+    def trimul_proj_groups(self, z_loc, mask, shard: RowShard, outgoing: bool, w: dict,
+                           a_owner=None, b_owner=None):
         """Gated, masked a/b planes of the rank's rows, unsplit (FP32 strict,
         BF16 fast) and channel-first ``[128][rows_p][ld]``, so that channel
         group ``g`` is the ``g``-th contiguous block of the all-to-all:
         outgoing ``rows_p = chunk``, ``ld = ld(n)``; incoming ``rows_p = n``,
         ``ld = ld(chunk)`` with the columns past the rank's rows zero (they
-        are terms of the concatenated contraction index)."""
+        are terms of the concatenated contraction index). With ``a_owner`` /
+        ``b_owner`` (every rank's ``[world][G][rows_p][ld]`` receive buffer,
+        zero where no rank writes) group ``g`` is stored straight into block
+        ``rank`` of rank ``g``'s buffers and ``(None, None, ld)`` returned."""
         n, rows, chunk = shard.n, shard.rows, shard.chunk
         dev = z_loc.device
-        if outgoing:
-            ld, plane_rows = int(self.lib.fpb_trimul_plane_ld(n, self.p)), chunk
-        else:
-            ld, plane_rows = int(self.lib.fpb_trimul_plane_ld(chunk, self.p)), n
+        plane_rows, ld = self.trimul_group_plane(shard, outgoing)
+        if a_owner is not None:
+            # stored straight into every rank's receive buffers
+            if rows:
+                ws = self._ws_take("trimul_proj",
+                                   self.lib.fpb_trimul_shard_workspace_size(self.p), dev)
+                keys = ("ln_in_w", "ln_in_b", "w_a_p", "w_a_g", "w_b_p", "w_b_g")
+                wt = [w[k].contiguous() for k in keys]
+                W = shard.world
+                _lib.check(self.lib.fpb_trimul_shard_proj_scatter(
+                    z_loc.data_ptr(), self._ptr(mask), n, rows, shard.r0, int(not outgoing),
+                    *[t.data_ptr() for t in wt], self.eps, (ctypes.c_void_p * W)(*a_owner),
+                    (ctypes.c_void_p * W)(*b_owner), W, shard.rank, ld, plane_rows, self.p,
+                    ws.data_ptr(), ws.numel(), ops._stream_ptr(dev)),
+                    "fpb_trimul_shard_proj_scatter")
+            return None, None, ld
         a = torch.empty(128, plane_rows, ld, dtype=self._dtype(), device=dev)
         b = torch.empty_like(a)
         if rows:
@@ -666,27 +689,30 @@ def trimul_scheme(world: int) -> str:
 
 
 def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
-    a, b, ld = phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w)
-    a_dtype = a.dtype
-    ra = _recv_like(comm, "trimul_a", a)
-    rb = _recv_like(comm, "trimul_b", b)
     owners = getattr(comm, "owner_buffer", None)
     if owners is not None:
-        # Peer transport. ra / rb were last read by the contraction of an
-        # earlier call of this direction, and the x buffers by the finish of
-        # an earlier call; every call closes its contraction with a barrier
-        # and issues one (the a / b exchange) after any earlier finish, so
-        # neither exchange needs an opening barrier.
-        comm.all_to_all_many([(ra, a), (rb, b)], fresh=True)
-        del a, b
-        njb = (shard.n + 127) // 128
-        x_loc, ptrs = owners("trimul_x", (shard.chunk, njb, 128, 128), a_dtype)
-        # the contraction stores each x row at its owner (fused return exchange)
-        phases.trimul_contract_groups(ra, rb, shard, outgoing, ld, x_owner=ptrs)
+        # Peer transport: the projection stores a / b straight into the
+        # owners' receive buffers and the contraction stores each x row at
+        # its owner, so both exchanges ride on the kernels' own stores. The
+        # receive buffers were last read by the contraction of an earlier
+        # call of this direction and the x buffers by the finish of an
+        # earlier call; every call closes its projection and its contraction
+        # with a barrier, after any earlier reader, so no opening barriers.
+        rows_p, ld = phases.trimul_group_plane(shard, outgoing)
+        dtype = phases._dtype()
+        ra, pa = owners("trimul_a", (128, rows_p, ld), dtype)
+        rb, pb = owners("trimul_b", (128, rows_p, ld), dtype)
+        phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w, a_owner=pa, b_owner=pb)
         comm.barrier()
-        del ra, rb
+        njb = (shard.n + 127) // 128
+        x_loc, px = owners("trimul_x", (shard.chunk, njb, 128, 128), dtype)
+        phases.trimul_contract_groups(ra, rb, shard, outgoing, ld, x_owner=px)
+        comm.barrier()
         phases.trimul_finish(z_loc, shard, x_loc, w, add)
         return z_loc
+    a, b, ld = phases.trimul_proj_groups(z_loc, mask, shard, outgoing, w)
+    ra = _recv_like(comm, "trimul_a", a)
+    rb = _recv_like(comm, "trimul_b", b)
     comm.all_to_all(ra, a)
     del a
     comm.all_to_all(rb, b)

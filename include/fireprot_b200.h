@@ -242,6 +242,21 @@ int fpb_trimul_group_contract(const void* a_hi, const void* a_lo, int m, int a_p
                               int b_chunks, size_t b_chunk_stride, int k, int ld, int channels,
                               void* x_blocked, int precision, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
+/* fpb_trimul_shard_proj for the channel-group exchange with a and b stored
+ * straight at their owners: channel c of a (b) goes to a_owner[c / G]
+ * (b_owner[c / G]), G = 128 / owners, plane rank * G + c % G of that
+ * rank's [owners][G][plane_rows][ld] receive buffer (a peer mapping for the
+ * other ranks), unsplit in strict mode. Columns or rows the call does not
+ * own are not written. The caller orders the stores against the owners'
+ * reads (a barrier after the call; the buffers' previous readers must have
+ * passed a barrier before it). */
+int fpb_trimul_shard_proj_scatter(const float* z_loc, const float* mask, int n, int rows, int r0,
+                                  int transposed, const float* ln_in_w, const float* ln_in_b,
+                                  const float* w_a_p, const float* w_a_g, const float* w_b_p,
+                                  const float* w_b_g, float eps, void* const* a_owner,
+                                  void* const* b_owner, int owners, int rank, int ld,
+                                  int plane_rows, int precision, void* workspace,
+                                  size_t workspace_bytes, cudaStream_t stream);
 /* fpb_trimul_group_contract with the output rows stored straight at their
  * owners: output row r goes to x_owner[r / owner_rows] (owners <= 16
  * pointers, a peer mapping for the other ranks' buffers) at row

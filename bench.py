@@ -317,7 +317,9 @@ _TO_CLOSE = []  # peer transports to unmap before the process group goes
 
 def _trimul_scheme(args):
     from fireprot_b200.sharded import trimul_scheme
-    return trimul_scheme(args.gpus) if args.trimul_scheme == "auto" else args.trimul_scheme
+    if args.trimul_scheme != "auto":
+        return args.trimul_scheme
+    return trimul_scheme(args.gpus, transport=args.comm)
 
 
 # ---------------------------------------------------------------------------
@@ -685,9 +687,11 @@ def main():
     ap.add_argument("--mode", choices=["sharded", "replicas"], default="sharded",
                     help="N>1: one block row-sharded over the GPUs, or a replica per GPU")
     ap.add_argument("--trimul-scheme", choices=["auto", "rows", "channels"], default="auto",
-                    help="N>1 sharded: TriMul exchange (auto: channels from 4 GPUs)")
-    ap.add_argument("--comm", choices=["nccl", "peer"], default="nccl",
-                    help="N>1 sharded: exchange transport (NCCL collectives or peer memory)")
+                    help="N>1 sharded: TriMul exchange (auto: channels over peer memory, "
+                         "or from 4 GPUs over NCCL)")
+    ap.add_argument("--comm", choices=["nccl", "peer"], default="peer",
+                    help="N>1 sharded: exchange transport (peer memory over NVLink, or NCCL "
+                         "collectives)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-side", action="store_true", help="skip the fast-mode side run")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3",

@@ -677,15 +677,19 @@ class CudaPhases:
 TRIMUL_SCHEMES = ("rows", "channels")
 
 
-def trimul_scheme(world: int) -> str:
+def trimul_scheme(world: int, transport: str = "nccl") -> str:
     """Exchange scheme of the TriMul contraction for ``world`` ranks. Per rank
     and operator the row scheme moves ``(W-1)/W`` of the full ``n x n x 128``
     planes (the all-gather of ``b`` or the reduce-scatter of ``x``); the
     channel scheme moves ``(W-1)/W`` of three rank shares (``a``, ``b`` and
     ``x``, each ``1/W`` of the planes), ``3/W`` of it, and splits only its own
-    group for the strict operands: channels from four ranks up, when the 128
-    channels divide evenly."""
-    return "channels" if world >= 4 and 128 % world == 0 else "rows"
+    group for the strict operands. Over NCCL: channels from four ranks up;
+    over peer memory (``transport="peer"``), where the projection and the
+    contraction store their outputs straight at the owners, channels from
+    two ranks up. Both need the 128 channels to divide evenly."""
+    if 128 % world:
+        return "rows"
+    return "channels" if world >= (2 if transport == "peer" else 4) else "rows"
 
 
 def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
@@ -730,7 +734,8 @@ def sharded_trimul(z_loc, mask, w: dict, shard: RowShard, comm, phases, *, outgo
                    add: bool = True, scheme: str | None = None):
     """Triangle multiplicative update of the rank's rows, in place on ``z_loc``.
     ``scheme``: ``"rows"`` or ``"channels"`` (default ``trimul_scheme``)."""
-    scheme = trimul_scheme(shard.world) if scheme is None else scheme
+    if scheme is None:
+        scheme = trimul_scheme(shard.world, "peer" if isinstance(comm, PeerComm) else "nccl")
     if scheme not in TRIMUL_SCHEMES:
         raise ValueError(f"unknown TriMul scheme {scheme!r}")
     if scheme == "channels":
@@ -781,7 +786,7 @@ def sharded_pair_block(z_loc, mask, weights: dict, shard: RowShard, comm, phases
     order): TriMul out, TriMul in, TriAttn start, TriAttn end, transition.
     ``weights`` maps ``tri_mul_out, tri_mul_in, tri_att_start, tri_att_end,
     pair_transition`` to the operators' weight dicts; ``scheme`` the TriMul
-    exchange scheme (default ``trimul_scheme(world)``)."""
+    exchange scheme (default ``trimul_scheme`` for the world and transport)."""
     sharded_trimul(z_loc, mask, weights["tri_mul_out"], shard, comm, phases, outgoing=True,
                    scheme=scheme)
     sharded_trimul(z_loc, mask, weights["tri_mul_in"], shard, comm, phases, outgoing=False,

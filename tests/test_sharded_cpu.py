@@ -161,6 +161,8 @@ def test_sharded_trimul_schemes_threads(n, world, scheme, outgoing):
 def test_trimul_scheme_choice():
     assert [S.trimul_scheme(w) for w in (1, 2, 3, 4, 5, 6, 8, 16)] == \
         ["rows", "rows", "rows", "channels", "rows", "rows", "channels", "channels"]
+    assert [S.trimul_scheme(w, "peer") for w in (1, 2, 3, 4, 5, 8)] == \
+        ["rows", "channels", "rows", "channels", "rows", "channels"]
     z, mask, p = _case(40, "none")
     sh = S.shard_plan(40, 3, 0)
     with pytest.raises(ValueError):

@@ -27,6 +27,7 @@ struct ContractCfg {
   static constexpr int STAGE_BYTES = NSPLIT * (A_BYTES + B_BYTES);
   static constexpr int STAGES = kStrict ? 2 : 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(STAGES * STAGE_BYTES >= BM * 132 * 4, "owner epilogue staging fits the stages");
 };
 
 // Column tile: the widest of 256/192/128/64/32 that divides the B chunk
@@ -36,6 +37,10 @@ inline int contract_bn(int chunk_rows, bool chunked) {
   for (int bn : {256, 192, 128, 64, 32})
     if (chunk_rows % bn == 0) return bn;
   return 0;
+}
+
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 template <bool kStrict, class OutT>
@@ -159,6 +164,71 @@ __global__ void __launch_bounds__(192, 1)
         // let every issued MMA retire before TMEM/smem are released
         umma_commit(drain);
         (void)mbar_wait(drain, 0, Guard{nullptr, abort_flag}, 0);
+      }
+    }
+  } else if (args.owners) {
+    // owner epilogue (rows stored at the ranks that own them, over NVLink
+    // for the other ranks): each 128-column block of the tile is staged in
+    // the now idle stage memory, then every warp stores whole rows, 32
+    // lanes x 16 bytes contiguous per instruction, so each remote write is
+    // one 512-byte burst instead of 32 separate 16-byte pieces
+    const int q = warp & 3;
+    const bool waited = mbar_wait(done, 0, g, 3);
+    if (!bar_any(!waited, 1, 128)) {
+      tc_fence_after();
+      constexpr int SP = 132;  // staged row pitch (floats): conflict-free 16-byte accesses
+      float* stg = reinterpret_cast<float*>(smem);
+      const int trow = q * 32 + lane;  // tile row drained from TMEM by this thread
+      const int wq = warp - 2;         // this warp stores tile rows wq*32 .. wq*32+31
+      const int cl = 4 * lane;         // this lane's 4 columns of a staged block
+#pragma unroll 1
+      for (int cb0 = 0; cb0 < bn; cb0 += 128) {
+        const int w = min(128, bn - cb0);
+#pragma unroll 1
+        for (int c = 0; c < w; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cb0 + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            *reinterpret_cast<float4*>(stg + trow * SP + c + 4 * v) =
+                make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                            __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        }
+        named_sync(1, 128);
+        const int col = j0 + cb0 + cl;
+#pragma unroll 1
+        for (int rr = 0; rr < 32; ++rr) {
+          const int tr = wq * 32 + rr;
+          const int row = it * C::BM + tr;
+          if (row >= args.m) break;  // uniform across the warp
+          if (cl >= w || col >= args.nn) continue;
+          const int d = min(row / args.owner_rows, args.owners - 1);
+          const size_t lr = (size_t)(row - d * args.owner_rows);
+          OutT* out = reinterpret_cast<OutT*>(args.outs[d]) +
+                      (((lr * args.njb + (col >> 7)) * 128 + ch + args.ch_off) << 7) +
+                      (col & 127);
+          const float4 v = *reinterpret_cast<const float4*>(stg + tr * SP + cl);
+          if (col + 4 <= args.nn) {
+            if constexpr (sizeof(OutT) == 4) {
+              *reinterpret_cast<float4*>(out) = v;
+            } else {
+              __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y);
+              __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z, v.w);
+              *reinterpret_cast<uint2*>(out) =
+                  make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+            }
+          } else {
+            const float e[4] = {v.x, v.y, v.z, v.w};
+            for (int u = 0; u < 4 && col + u < args.nn; ++u) {
+              if constexpr (sizeof(OutT) == 4)
+                out[u] = e[u];
+              else
+                out[u] = __float2bfloat16_rn(e[u]);
+            }
+          }
+        }
+        named_sync(1, 128);  // the staged block is read before the next overwrites it
       }
     }
   } else {

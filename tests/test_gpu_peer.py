@@ -95,3 +95,67 @@ def test_peer_scatter_rejects_bad_arguments():
     assert call(0, 0, 32, count=17) != 0
     assert call(0, 0, 32, count=-1) != 0
     torch.cuda.synchronize()
+
+
+def _split_hi_lo(x):
+    hi = (x.view(torch.int32) & -8192).view(torch.float32)  # top 11 significand bits
+    return hi, x - hi
+
+
+@pytest.mark.parametrize("precision", ["strict", "fast"])
+@pytest.mark.parametrize("m,nn,k,owners,chunk", [(200, 200, 96, 3, 96), (256, 300, 64, 2, 128),
+                                                 (90, 70, 40, 4, 32)])
+def test_group_contract_scatter_matches_local(precision, m, nn, k, owners, chunk):
+    """The contraction storing its rows at their owners (the row-sharded
+    TriMul's fused return exchange, emulated with local buffers) writes
+    exactly the rows and channels the plain call writes, and nothing else."""
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    st = ops._stream_ptr(dev)
+    p = 0 if precision == "strict" else 1
+    G, ch_off = 16, 32
+    ld = int(lib.fpb_trimul_plane_ld(k, p))
+    g = torch.Generator().manual_seed(m + nn + k)
+    a = torch.zeros(G, m, ld)
+    b = torch.zeros(G, nn, ld)
+    a[:, :, :k] = torch.randn(G, m, k, generator=g)
+    b[:, :, :k] = torch.randn(G, nn, k, generator=g)
+    a, b = a.to(dev), b.to(dev)
+    if p == 0:
+        (a_hi, a_lo), (b_hi, b_lo) = _split_hi_lo(a), _split_hi_lo(b)
+        ops_ = [a_hi, a_lo, b_hi, b_lo]
+        odt = torch.float32
+    else:
+        a_hi, b_hi = a.to(torch.bfloat16), b.to(torch.bfloat16)
+        ops_ = [a_hi, None, b_hi, None]
+        odt = torch.bfloat16
+    ptr = [ctypes.c_void_p(t.data_ptr() if t is not None else 0) for t in ops_]
+    njb = (nn + 127) // 128
+    ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+    ref = torch.zeros(m, njb, G, 128, dtype=odt, device=dev)
+    _lib.check(lib.fpb_trimul_group_contract(
+        ptr[0], ptr[1], m, m, ptr[2], ptr[3], nn, nn, 1, 0, k, ld, G,
+        ctypes.c_void_p(ref.data_ptr()), p, ctypes.c_void_p(ws.data_ptr()), 256, st),
+        "fpb_trimul_group_contract")
+    outs = [torch.full((chunk, njb, 128, 128), 7.0, dtype=odt, device=dev) for _ in range(owners)]
+    arr = (ctypes.c_void_p * owners)(*[o.data_ptr() for o in outs])
+    _lib.check(lib.fpb_trimul_group_contract_scatter(
+        ptr[0], ptr[1], m, m, ptr[2], ptr[3], nn, nn, 1, 0, k, ld, G, arr, owners, chunk,
+        ch_off, p, ctypes.c_void_p(ws.data_ptr()), 256, st),
+        "fpb_trimul_group_contract_scatter")
+    torch.cuda.synchronize()
+    ref = ref.cpu()
+    for d, o in enumerate(outs):
+        o = o.cpu()
+        rows = max(0, min(chunk, m - d * chunk))
+        got = o[:rows, :, ch_off:ch_off + G]
+        want = ref[d * chunk:d * chunk + rows]
+        # columns past nn inside the last 128-column block are not written
+        full = njb * 128
+        for jb in range(njb):
+            cols = min(128, nn - jb * 128)
+            assert torch.equal(got[:, jb, :, :cols], want[:, jb, :, :cols])
+            assert torch.all(got[:, jb, :, cols:] == 7.0)
+        assert full >= nn
+        assert torch.all(o[rows:] == 7.0)
+        assert torch.all(o[:, :, :ch_off] == 7.0) and torch.all(o[:, :, ch_off + G:] == 7.0)

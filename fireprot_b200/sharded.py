@@ -124,19 +124,26 @@ class PeerComm:
     destination is filled through a registered scratch buffer plus one local
     copy. Registered buffers live as long as the object: ``close()`` unmaps
     the peers' buffers (call it, after a device synchronise, before the
-    process group is destroyed)."""
+    process group is destroyed).
 
-    def __init__(self, group=None):
-        import torch.distributed as dist
+    ``dist``, ``lib`` and ``device`` default to ``torch.distributed``, the
+    CUDA library and the current CUDA device; another process-group API (with
+    ``get_world_size``, ``get_rank``, ``all_gather_object``, ``all_reduce``,
+    ``reduce_scatter_tensor`` and ``ReduceOp``) or an object with the
+    library's peer entry points can stand in for them."""
+
+    def __init__(self, group=None, *, dist=None, lib=None, device=None):
+        if dist is None:
+            import torch.distributed as dist
         self._dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if self.world > 16:
             raise ValueError(f"the peer transport spans at most 16 ranks (world={self.world})")
-        self.nccl = DistComm(group)
-        self.lib = _lib.load()
-        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.lib = _lib.load() if lib is None else lib
+        self.dev = (torch.device("cuda", torch.cuda.current_device()) if device is None
+                    else torch.device(device))
         self._tick = torch.zeros(1, device=self.dev)
         self._bufs: dict = {}     # (tag, shape, dtype) -> (tensor, [device pointer per rank])
         self._by_ptr: dict = {}   # data_ptr -> (tag, shape, dtype)
@@ -149,7 +156,7 @@ class PeerComm:
         handle = ctypes.create_string_buffer(self._hbytes)
         off = ctypes.c_size_t(0)
         _lib.check(self.lib.fpb_ipc_export(ctypes.c_void_p(t.data_ptr()), handle,
-                                           ctypes.byref(off)), "fpb_ipc_export")
+                                           ctypes.pointer(off)), "fpb_ipc_export")
         mine = (bytes(handle.raw), int(off.value), t.numel() * t.element_size())
         got = [None] * self.world
         self._dist.all_gather_object(got, mine, group=self.group)
@@ -165,7 +172,7 @@ class PeerComm:
             ptr = ctypes.c_void_p()
             if base is None:
                 b = ctypes.c_void_p()
-                _lib.check(self.lib.fpb_ipc_import(h, o, ctypes.byref(b), ctypes.byref(ptr)),
+                _lib.check(self.lib.fpb_ipc_import(h, o, ctypes.pointer(b), ctypes.pointer(ptr)),
                            "fpb_ipc_import")
                 self._opened[h] = base = b.value
             ptrs.append(base + o)
@@ -211,7 +218,7 @@ class PeerComm:
         current stream (``fpb_peer_scatter``) writes every peer's block side
         by side; a copy that is not 16-byte aligned goes through the copy
         engine on the same stream instead."""
-        cur = ops._stream_ptr(self.dev)
+        cur = self._stream()
         fast = [(d, s, b) for _, d, s, b in copies
                 if b and d != s and not (d | s | b) & 15]
         slow = [(d, s, b) for _, d, s, b in copies
@@ -269,21 +276,28 @@ class PeerComm:
             out.view(-1).copy_(buf)
 
     def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
-        self.nccl.reduce_scatter(out, inp)
+        """NCCL's reduce-scatter (the row scheme's incoming TriMul)."""
+        self._dist.reduce_scatter_tensor(out.view(-1), inp.reshape(-1),
+                                         op=self._dist.ReduceOp.SUM, group=self.group)
+
+    def _stream(self) -> int:
+        return ops._stream_ptr(self.dev) if self.dev.type == "cuda" else 0
 
     def transpose_rows(self, z_loc, shard: RowShard, out=None, tag="transpose", *,
                        fresh: bool = False):
         """``transpose_rows`` in one kernel over peer memory (see there)."""
         c, n, ch = shard.chunk, shard.n, z_loc.shape[-1]
-        if z_loc.dtype != torch.float32 or not z_loc.is_contiguous():
-            raise ValueError("peer transpose takes a contiguous float32 [chunk, n, c] tensor")
-        buf, ptrs = self._buffer(tag, (c, n, ch), torch.float32)
+        words = ch * z_loc.element_size() // 4  # the kernel moves 4-byte words
+        if not z_loc.is_contiguous() or (ch * z_loc.element_size()) % 16:
+            raise ValueError("peer transpose takes a contiguous [chunk, n, c] tensor whose "
+                             "rows are a multiple of 16 bytes")
+        buf, ptrs = self._buffer(tag, (c, n, ch), z_loc.dtype)
         arr = (ctypes.c_void_p * self.world)(*ptrs)
         if not fresh:
             self.barrier()
         _lib.check(self.lib.fpb_peer_transpose_rows(
-            ctypes.c_void_p(z_loc.data_ptr()), n, c, ch, self.rank, self.world, arr,
-            ops._stream_ptr(self.dev)), "fpb_peer_transpose_rows")
+            ctypes.c_void_p(z_loc.data_ptr()), n, c, words, self.rank, self.world, arr,
+            self._stream()), "fpb_peer_transpose_rows")
         self.barrier()
         if out is None:
             return buf
@@ -353,8 +367,12 @@ class CudaPhases:
     Buffers are allocated with torch on the current stream. Each phase keeps
     one workspace, reused by its later calls on the same stream (each call
     restarts its status word), so ``check()`` reports the latest call of
-    every phase.
+    every phase. ``stores_at_owners``: the TriMul projection and contraction
+    can store straight into every rank's buffers (the peer transport's
+    fused exchanges).
     """
+
+    stores_at_owners = True
 
     def __init__(self, precision="strict", eps: float = 1e-5):
         self.p = ops.precision_code(precision)
@@ -694,7 +712,7 @@ def trimul_scheme(world: int, transport: str = "nccl") -> str:
 
 def _trimul_channels(z_loc, mask, w, shard, comm, phases, outgoing, add):
     owners = getattr(comm, "owner_buffer", None)
-    if owners is not None:
+    if owners is not None and getattr(phases, "stores_at_owners", False):
         # Peer transport: the projection stores a / b straight into the
         # owners' receive buffers and the contraction stores each x row at
         # its owner, so both exchanges ride on the kernels' own stores. The

@@ -333,6 +333,8 @@ int fpb_copy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream
 /* Transposed exchange of the row-sharded pair tensor: rank `rank` of `world`
  * (world <= 16) owns rows [rank*chunk, rank*chunk + chunk) of z [n, n, ch]
  * as z_loc [chunk][n][ch] (rows at or past n are padding and are not read).
+ * ch counts 4-byte words per pair (128 for FP32 c_z = 128); the kernel only
+ * moves bytes, so any element type whose pair vector is ch words works.
  * Every owned z[i, j, :] with j < n is stored at row j - d*chunk, column i
  * of dst[d], d = j / chunk: dst[d] is rank d's [chunk][n][ch] buffer of the
  * rows of z^T it owns (a peer mapping, or the caller's own buffer for

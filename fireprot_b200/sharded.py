@@ -115,10 +115,14 @@ class PeerComm:
     transposed exchange of the ending-node operator is one kernel
     (``fpb_peer_transpose_rows``) that stores each 512-byte channel vector
     at its transposed place on its owner: no packing, staging or unpacking
-    pass. A one-element NCCL all-reduce on the current stream before the
-    copies (every peer is done with the buffer's previous contents) and
-    after them (every peer's copies into this rank have landed) orders the
-    transfers; the reduce-scatter of the row TriMul scheme stays on NCCL.
+    pass. ``owner_buffer`` hands phase kernels every rank's address of a
+    buffer, so the channel-group TriMul's projection and contraction store
+    their outputs at the owning ranks themselves. A one-element NCCL
+    all-reduce on the current stream orders the transfers: after them
+    (every peer's stores into this rank have landed), and before them
+    (every peer is done with the buffer's previous contents) unless the
+    caller passes ``fresh=True``. The reduce-scatter of the row TriMul
+    scheme stays on NCCL.
 
     A buffer obtained from ``recv_buffer`` is filled in place; any other
     destination is filled through a registered scratch buffer plus one local
